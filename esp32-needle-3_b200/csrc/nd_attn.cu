@@ -1,0 +1,918 @@
+// nd_attn.cu - host side of the C ABI declared in include/nd_attn.h.
+//
+// The handle plays the part of nd_model's session state and KV caches
+// (engine/include/nd_model.h:129-137): a host mirror of each sequence's
+// position/sink/snapshot, a device copy of the same that kernels read, the
+// per-layer caches in HBM, the RoPE cos/sin table, and split-KV scratch. State
+// changes reach the device through tiny kernels whose arguments are captured
+// by value at launch, so they stay ordered with the attention kernels on the
+// handle's stream.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/nd_attn.h"
+#include "nd_internal.h"
+
+using nda::AttnParams;
+using nda::CacheView;
+using nda::SeqState;
+using nda::TokMeta;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define ND_CUDA(call)                                                                   \
+    do {                                                                                \
+        cudaError_t e_ = (call);                                                        \
+        if (e_ != cudaSuccess)                                                          \
+            return fail(ND_ATTN_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                        __FILE__, __LINE__);                                            \
+    } while (0)
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+size_t dt_size(int dt) { return dt == ND_DT_I8 ? 1 : dt == ND_DT_F32 ? 4 : 2; }
+
+struct HostSeq {
+    uint32_t pos = 0, n_sink = 0, snap_pos = 0;
+    int has_snap = 0;
+};
+
+// ---- small state kernels (arguments by value) ----------------------------
+__global__ void set_state_kernel(SeqState *st, uint32_t seq, uint32_t pos, uint32_t n_sink) {
+    st[seq].pos = pos;
+    st[seq].n_sink = n_sink;
+}
+
+__global__ void advance_kernel(SeqState *st, uint32_t n, const uint32_t *ids, const uint32_t *len,
+                               uint32_t step) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    st[ids ? ids[i] : i].pos += len ? len[i] : step;
+}
+
+// Copies whole cache rows between a (layer-strided) cache and a dense buffer:
+// dense row (l, r) <-> cache row phys_row(seq, slot0 + r) of layer l.
+// `to_cache` selects the direction. Row sizes are multiples of 4 bytes.
+__global__ void rows_copy_kernel(char *cache, size_t layer_stride, char *dense, size_t dense_layer_stride,
+                                 uint32_t row_words, uint32_t n_rows, CacheView c, uint32_t seq,
+                                 uint32_t slot0, int to_cache) {
+    const uint32_t l = blockIdx.y;
+    for (uint32_t r = blockIdx.x; r < n_rows; r += gridDim.x) {
+        const size_t pr = nda::phys_row(c, seq, slot0 + r);
+        uint32_t *cw = reinterpret_cast<uint32_t *>(cache + l * layer_stride) + pr * row_words;
+        uint32_t *dw = reinterpret_cast<uint32_t *>(dense + l * dense_layer_stride) + (size_t)r * row_words;
+        for (uint32_t w = threadIdx.x; w < row_words; w += blockDim.x) {
+            if (to_cache) cw[w] = dw[w];
+            else dw[w] = cw[w];
+        }
+    }
+}
+
+}  // namespace
+
+struct nd_attn_prefix {
+    const nd_attn *owner;
+    uint32_t pos, sink, live;
+    size_t bytes;
+    void *dev;  // image in the reference's byte order
+};
+
+struct nd_attn {
+    nd_attn_config cfg;
+    cudaStream_t stream = nullptr;   // where work is enqueued
+    cudaStream_t own = nullptr;      // the handle's own stream
+    int sm_count = 148;
+    uint32_t rep = 1, k_dim = 0, v_dim = 0, blocks_per_seq = 1, block_shift = 0;
+    size_t rows_per_layer = 0, kes = 1;
+    void *kc = nullptr, *vc = nullptr;
+    float *ks = nullptr, *vs = nullptr;
+    float2 *rope = nullptr;
+    float *norms = nullptr;  // [layer][2][qk]
+    std::vector<uint8_t> has_norm;
+    SeqState *d_state = nullptr;
+    std::vector<HostSeq> seqs;
+    int32_t *d_btab = nullptr;
+    float *part_o = nullptr, *part_ml = nullptr;
+    int *counters = nullptr;
+    size_t part_slots = 0;     // (item, split) slots the scratch holds
+    size_t counter_cap = 0;    // items with a ticket counter
+    TokMeta *d_tok = nullptr;
+    size_t tok_cap = 0;
+    uint32_t *d_u32 = nullptr;
+    size_t u32_cap = 0;
+    int *d_err = nullptr;
+    void *pin = nullptr;
+    size_t pin_cap = 0;
+    void *dio = nullptr;
+    size_t dio_cap = 0;
+    uint64_t launches = 0;
+};
+
+namespace {
+
+int check_seq(const nd_attn *h, uint32_t seq) {
+    if (!h) return fail(ND_ATTN_ERR_ARG, "null handle");
+    if (seq >= h->cfg.max_seqs) return fail(ND_ATTN_ERR_RANGE, "sequence %u >= max_seqs %u", seq, h->cfg.max_seqs);
+    return ND_ATTN_OK;
+}
+
+int push_state(nd_attn *h, uint32_t seq) {
+    const HostSeq &s = h->seqs[seq];
+    set_state_kernel<<<1, 1, 0, h->stream>>>(h->d_state, seq, s.pos, s.n_sink);
+    h->launches++;
+    ND_CUDA(cudaGetLastError());
+    return ND_ATTN_OK;
+}
+
+CacheView layer_view(const nd_attn *h, uint32_t layer) {
+    CacheView c;
+    c.k = static_cast<char *>(h->kc) + layer * h->rows_per_layer * h->k_dim * h->kes;
+    c.v = static_cast<char *>(h->vc) + layer * h->rows_per_layer * h->v_dim * h->kes;
+    c.ks = h->ks ? h->ks + layer * h->rows_per_layer * h->cfg.n_kv_heads : nullptr;
+    c.vs = h->vs ? h->vs + layer * h->rows_per_layer * h->cfg.n_kv_heads : nullptr;
+    c.k_dim = h->k_dim;
+    c.v_dim = h->v_dim;
+    c.n_kv = h->cfg.n_kv_heads;
+    c.window = h->cfg.window;
+    c.btab = h->cfg.block_size ? h->d_btab : nullptr;
+    c.blocks_per_seq = h->blocks_per_seq;
+    c.block_shift = h->block_shift;
+    return c;
+}
+
+template <typename T>
+int grow(T **p, size_t *cap, size_t need) {
+    if (need <= *cap) return ND_ATTN_OK;
+    size_t n = std::max(need, *cap * 2);
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    if (cudaMalloc(reinterpret_cast<void **>(p), n * sizeof(T)) != cudaSuccess)
+        return fail(ND_ATTN_ERR_NOMEM, "device allocation of %zu bytes failed", n * sizeof(T));
+    *cap = n;
+    return ND_ATTN_OK;
+}
+
+// Visited positions of a token at `pos` (sink run + recent run).
+uint32_t visit_count(uint32_t pos, uint32_t n_sink, uint32_t window) {
+    const uint32_t sinks = std::min(n_sink, pos + 1);
+    uint32_t rcount = 0;
+    if (pos + 1 > n_sink) rcount = std::min(pos + 1 - n_sink, window - n_sink);
+    return sinks + rcount;
+}
+
+AttnParams base_params(nd_attn *h, uint32_t layer) {
+    AttnParams P;
+    memset(&P, 0, sizeof(P));
+    P.act_dt = h->cfg.act_dtype;
+    P.out_dt = h->cfg.out_dtype;
+    P.c = layer_view(h, layer);
+    P.rope = h->rope;
+    P.max_pos = h->cfg.max_pos;
+    if (h->has_norm[layer]) {
+        P.qnorm = h->norms + (size_t)layer * 2 * h->cfg.qk_head_dim;
+        P.knorm = P.qnorm + h->cfg.qk_head_dim;
+    }
+    P.state = h->d_state;
+    P.n_heads = h->cfg.n_heads;
+    P.rep = h->rep;
+    P.scale_log2 = 1.4426950408889634f / sqrtf((float)h->cfg.qk_head_dim);
+    P.part_o = h->part_o;
+    P.part_ml = h->part_ml;
+    P.counters = h->counters;
+    P.err = h->d_err;
+    return P;
+}
+
+cudaError_t attend_launch(const nd_attn *h, const AttnParams &P, dim3 grid) {
+    const int qk = (int)h->cfg.qk_head_dim, vd = (int)h->cfg.v_head_dim;
+    const int nq = nda::nq_for_rep(h->rep);
+    switch (h->cfg.kv_dtype) {
+    case ND_DT_I8: return nda::attend_launch_i8(qk, vd, nq, P, grid, h->stream);
+    case ND_DT_F32: return nda::attend_launch_f32(qk, vd, nq, P, grid, h->stream);
+    case ND_DT_F16: return nda::attend_launch_f16(qk, vd, nq, P, grid, h->stream);
+    default: return nda::attend_launch_bf16(qk, vd, nq, P, grid, h->stream);
+    }
+}
+
+cudaError_t append_launch(const nd_attn *h, const AttnParams &P) {
+    const int qk = (int)h->cfg.qk_head_dim, vd = (int)h->cfg.v_head_dim;
+    switch (h->cfg.kv_dtype) {
+    case ND_DT_I8: return nda::append_launch_i8(qk, vd, P, h->stream);
+    case ND_DT_F32: return nda::append_launch_f32(qk, vd, P, h->stream);
+    case ND_DT_F16: return nda::append_launch_f16(qk, vd, P, h->stream);
+    default: return nda::append_launch_bf16(qk, vd, P, h->stream);
+    }
+}
+
+// Chooses the split length for `items` (token, KV head) work items whose
+// longest visit run is jmax and whose runs total `rows`: enough CTAs to cover
+// the SMs twice over, splits that are whole loop iterations, and no more
+// splits than the scratch holds.
+void choose_split(const nd_attn *h, size_t items, uint32_t jmax, size_t rows, uint32_t *chunk,
+                  uint32_t *nsplit) {
+    const uint32_t per_iter = (uint32_t)nda::attend_rows_per_iter(h->cfg.kv_dtype, (int)h->cfg.v_head_dim);
+    const size_t target = (size_t)h->sm_count * 16;
+    size_t c = (rows + target - 1) / target;
+    c = std::max<size_t>(c, 2 * per_iter);
+    c = (c + per_iter - 1) / per_iter * per_iter;
+    uint32_t ns = (uint32_t)((jmax + c - 1) / c);
+    if (ns > 1 && (items > h->counter_cap || items * ns > h->part_slots)) {
+        const size_t cap = items > h->counter_cap ? 1 : h->part_slots / items;
+        ns = (uint32_t)std::max<size_t>(1, std::min<size_t>(cap, ns));
+        c = (jmax + ns - 1) / ns;
+        c = (c + per_iter - 1) / per_iter * per_iter;
+        ns = (uint32_t)((jmax + c - 1) / c);
+    }
+    if (ns < 1) ns = 1;
+    *chunk = (uint32_t)c;
+    *nsplit = ns;
+}
+
+// Validates the sequences of a call; fills per-call visit statistics.
+int check_call(const nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const uint32_t *len) {
+    if (!h) return fail(ND_ATTN_ERR_ARG, "null handle");
+    if (layer >= h->cfg.n_layers) return fail(ND_ATTN_ERR_RANGE, "layer %u >= n_layers %u", layer, h->cfg.n_layers);
+    if (n == 0 || n > h->cfg.max_seqs) return fail(ND_ATTN_ERR_RANGE, "%u sequences (max %u)", n, h->cfg.max_seqs);
+    std::vector<uint8_t> seen(seq_ids ? h->cfg.max_seqs : 0, 0);
+    for (uint32_t i = 0; i < n; i++) {
+        const uint32_t s = seq_ids ? seq_ids[i] : i;
+        if (s >= h->cfg.max_seqs) return fail(ND_ATTN_ERR_RANGE, "sequence id %u >= max_seqs", s);
+        if (seq_ids) {
+            if (seen[s]) return fail(ND_ATTN_ERR_ARG, "sequence id %u listed twice", s);
+            seen[s] = 1;
+        }
+        const uint32_t l = len ? len[i] : 1;
+        const uint64_t last = (uint64_t)h->seqs[s].pos + l;
+        if (last > h->cfg.max_pos)
+            return fail(ND_ATTN_ERR_RANGE, "sequence %u reaches position %llu >= max_pos %u", s,
+                        (unsigned long long)(last - 1), h->cfg.max_pos);
+    }
+    return ND_ATTN_OK;
+}
+
+int upload_tok(nd_attn *h, const std::vector<TokMeta> &tok) {
+    int rc = grow(&h->d_tok, &h->tok_cap, tok.size());
+    if (rc) return rc;
+    ND_CUDA(cudaMemcpyAsync(h->d_tok, tok.data(), tok.size() * sizeof(TokMeta), cudaMemcpyHostToDevice,
+                            h->stream));
+    return ND_ATTN_OK;
+}
+
+// One attend launch over `tok` (nullptr = identity over n sequences).
+int run_attend(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok,
+               const std::vector<uint32_t> &tok_pos, const std::vector<uint32_t> &tok_seq,
+               int fuse_append, const void *q, const void *k, const void *v, const void *gate, void *out) {
+    const uint32_t n_kv = h->cfg.n_kv_heads, W = h->cfg.window;
+    uint32_t jmax = 1;
+    size_t rows = 0;
+    for (uint32_t t = 0; t < ntok; t++) {
+        const uint32_t j = visit_count(tok_pos[t], h->seqs[tok_seq[t]].n_sink, W);
+        jmax = std::max(jmax, j);
+        rows += (size_t)j * n_kv;
+    }
+    const size_t items = (size_t)ntok * n_kv;
+    uint32_t chunk, nsplit;
+    choose_split(h, items, jmax, rows, &chunk, &nsplit);
+    if (items > 0x7fffffffu || nsplit > 65535u) return fail(ND_ATTN_ERR_RANGE, "launch too large");
+    AttnParams P = base_params(h, layer);
+    P.q = q; P.k = k; P.v = v; P.gate = gate; P.out = out;
+    P.tok = d_tok;
+    P.n_tok = ntok;
+    P.chunk = chunk;
+    P.max_splits = nsplit;
+    P.fuse_append = fuse_append;
+    ND_CUDA(attend_launch(h, P, dim3((unsigned)items, nsplit, 1)));
+    h->launches++;
+    return ND_ATTN_OK;
+}
+
+size_t act_bytes(const nd_attn *h, size_t tokens, int which) {
+    const nd_attn_config &c = h->cfg;
+    const size_t a = dt_size(c.act_dtype);
+    switch (which) {
+    case 0: return tokens * c.n_heads * c.qk_head_dim * a;          // q
+    case 1: return tokens * c.n_kv_heads * c.qk_head_dim * a;       // k
+    case 2: return tokens * c.n_kv_heads * c.v_head_dim * a;        // v
+    case 3: return tokens * c.n_heads * c.v_head_dim * a;           // gate
+    default: return tokens * c.n_heads * c.v_head_dim * dt_size(c.out_dtype);  // out
+    }
+}
+
+}  // namespace
+
+int nda::attend_rows_per_iter(int kv_dt, int vd) {
+    const int es = kv_dt == ND_DT_I8 ? 1 : kv_dt == ND_DT_F32 ? 4 : 2;
+    const int lpr = vd * es / 16;
+    return 4 * 4 * (32 / lpr);
+}
+
+// ============================================================ C ABI
+extern "C" {
+
+void nd_attn_config_init(nd_attn_config *cfg) {
+    if (!cfg) return;
+    memset(cfg, 0, sizeof(*cfg));
+    cfg->n_layers = 1;
+    cfg->n_heads = 8;
+    cfg->n_kv_heads = 8;
+    cfg->qk_head_dim = 64;
+    cfg->v_head_dim = 64;
+    cfg->window = 384;
+    cfg->max_seqs = 1;
+    cfg->rope_theta = 10000.0f;
+    cfg->kv_dtype = ND_DT_F32;
+    cfg->act_dtype = ND_DT_F32;
+    cfg->out_dtype = ND_DT_F32;
+}
+
+int nd_attn_open(const nd_attn_config *cfg_in, nd_attn **out) {
+    if (!cfg_in || !out) return fail(ND_ATTN_ERR_ARG, "null argument");
+    *out = nullptr;
+    nd_attn_config cfg = *cfg_in;
+    if (cfg.max_pos == 0) cfg.max_pos = cfg.window;
+    if (!nda::head_dims_supported(cfg.qk_head_dim, cfg.v_head_dim))
+        return fail(ND_ATTN_ERR_GEOM, "head dims (%u,%u) not compiled", cfg.qk_head_dim, cfg.v_head_dim);
+    if (cfg.n_kv_heads == 0 || cfg.n_heads % cfg.n_kv_heads || cfg.n_heads / cfg.n_kv_heads > 8)
+        return fail(ND_ATTN_ERR_GEOM, "heads %u/%u: need n_heads %% n_kv_heads == 0 and ratio <= 8",
+                    cfg.n_heads, cfg.n_kv_heads);
+    if (cfg.n_layers == 0 || cfg.window < 1 || cfg.max_seqs == 0)
+        return fail(ND_ATTN_ERR_GEOM, "n_layers, window and max_seqs must be positive");
+    if (cfg.kv_dtype < ND_DT_I8 || cfg.kv_dtype > ND_DT_BF16 || cfg.act_dtype < ND_DT_F32 ||
+        cfg.act_dtype > ND_DT_BF16 || cfg.out_dtype < ND_DT_F32 || cfg.out_dtype > ND_DT_BF16)
+        return fail(ND_ATTN_ERR_ARG, "bad dtype");
+    if (cfg.block_size) {
+        if (cfg.block_size & (cfg.block_size - 1)) return fail(ND_ATTN_ERR_GEOM, "block_size must be a power of two");
+        if (cfg.window % cfg.block_size) return fail(ND_ATTN_ERR_GEOM, "window must be a multiple of block_size");
+        if (cfg.n_blocks == 0) cfg.n_blocks = (uint32_t)((size_t)cfg.max_seqs * cfg.window / cfg.block_size);
+    }
+
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(ND_ATTN_ERR_NOGPU, "no CUDA device");
+    if (cfg.device < 0 || cfg.device >= ndev) return fail(ND_ATTN_ERR_ARG, "device %d of %d", cfg.device, ndev);
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, cfg.device) != cudaSuccess || prop.major != 10)
+        return fail(ND_ATTN_ERR_NOGPU, "device %d is not sm_100 (the library is built for sm_100a only)", cfg.device);
+    DeviceGuard dg(cfg.device);
+
+    nd_attn *h = new nd_attn();
+    h->cfg = cfg;
+    h->sm_count = prop.multiProcessorCount;
+    h->rep = cfg.n_heads / cfg.n_kv_heads;
+    h->k_dim = cfg.n_kv_heads * cfg.qk_head_dim;
+    h->v_dim = cfg.n_kv_heads * cfg.v_head_dim;
+    h->kes = dt_size(cfg.kv_dtype);
+    if (cfg.block_size) {
+        h->blocks_per_seq = cfg.window / cfg.block_size;
+        while ((1u << h->block_shift) < cfg.block_size) h->block_shift++;
+        h->rows_per_layer = (size_t)cfg.n_blocks * cfg.block_size;
+    } else {
+        h->rows_per_layer = (size_t)cfg.max_seqs * cfg.window;
+    }
+    h->seqs.assign(cfg.max_seqs, HostSeq());
+    h->has_norm.assign(cfg.n_layers, 0);
+
+    auto bail = [&](int code) {
+        nd_attn_close(h);
+        return code;
+    };
+    if (cudaStreamCreateWithFlags(&h->own, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(fail(ND_ATTN_ERR_CUDA, "stream creation failed"));
+    h->stream = h->own;
+    const size_t kbytes = cfg.n_layers * h->rows_per_layer * h->k_dim * h->kes;
+    const size_t vbytes = cfg.n_layers * h->rows_per_layer * h->v_dim * h->kes;
+    if (cudaMalloc(&h->kc, kbytes) != cudaSuccess || cudaMalloc(&h->vc, vbytes) != cudaSuccess)
+        return bail(fail(ND_ATTN_ERR_NOMEM, "KV cache allocation (%zu + %zu bytes) failed", kbytes, vbytes));
+    cudaMemsetAsync(h->kc, 0, kbytes, h->stream);
+    cudaMemsetAsync(h->vc, 0, vbytes, h->stream);
+    if (cfg.kv_dtype == ND_DT_I8) {
+        const size_t sb = cfg.n_layers * h->rows_per_layer * cfg.n_kv_heads * sizeof(float);
+        if (cudaMalloc(&h->ks, sb) != cudaSuccess || cudaMalloc(&h->vs, sb) != cudaSuccess)
+            return bail(fail(ND_ATTN_ERR_NOMEM, "scale allocation failed"));
+        cudaMemsetAsync(h->ks, 0, sb, h->stream);
+        cudaMemsetAsync(h->vs, 0, sb, h->stream);
+    }
+    // RoPE table with the reference's own expressions (nd_model.c:1233-1236,
+    // 2949-2954), so the rotated K is bit-identical to the host engine's.
+    {
+        const uint32_t half = cfg.qk_head_dim / 2;
+        std::vector<float> inv(half);
+        for (uint32_t i = 0; i < half; i++)
+            inv[i] = 1.0f / powf(cfg.rope_theta, (float)(2 * i) / (float)cfg.qk_head_dim);
+        std::vector<float2> tab((size_t)cfg.max_pos * half);
+        for (uint32_t p = 0; p < cfg.max_pos; p++)
+            for (uint32_t i = 0; i < half; i++) {
+                const float angle = (float)p * inv[i];
+                tab[(size_t)p * half + i] = make_float2(cosf(angle), sinf(angle));
+            }
+        if (cudaMalloc(&h->rope, tab.size() * sizeof(float2)) != cudaSuccess)
+            return bail(fail(ND_ATTN_ERR_NOMEM, "rope table allocation failed"));
+        if (cudaMemcpy(h->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess)
+            return bail(fail(ND_ATTN_ERR_CUDA, "rope table upload failed"));
+    }
+    if (cudaMalloc(&h->norms, (size_t)cfg.n_layers * 2 * cfg.qk_head_dim * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&h->d_state, cfg.max_seqs * sizeof(SeqState)) != cudaSuccess ||
+        cudaMalloc(&h->d_err, sizeof(int)) != cudaSuccess)
+        return bail(fail(ND_ATTN_ERR_NOMEM, "state allocation failed"));
+    cudaMemsetAsync(h->d_state, 0, cfg.max_seqs * sizeof(SeqState), h->stream);
+    cudaMemsetAsync(h->d_err, 0, sizeof(int), h->stream);
+    if (cfg.block_size) {
+        const size_t nb = (size_t)cfg.max_seqs * h->blocks_per_seq;
+        std::vector<int32_t> ident(nb);
+        for (size_t i = 0; i < nb; i++) ident[i] = (int32_t)(i % cfg.n_blocks);
+        if (cudaMalloc(&h->d_btab, nb * sizeof(int32_t)) != cudaSuccess)
+            return bail(fail(ND_ATTN_ERR_NOMEM, "block table allocation failed"));
+        if (cudaMemcpy(h->d_btab, ident.data(), nb * sizeof(int32_t), cudaMemcpyHostToDevice) != cudaSuccess)
+            return bail(fail(ND_ATTN_ERR_CUDA, "block table upload failed"));
+    }
+    // Split-KV scratch: up to 64 MB of partial outputs, tickets for every
+    // (sequence, KV head) of a full decode.
+    {
+        const size_t nq = (size_t)nda::nq_for_rep(h->rep);
+        const size_t per_slot = nq * (cfg.v_head_dim + 2) * sizeof(float);
+        h->counter_cap = (size_t)cfg.max_seqs * cfg.n_kv_heads;
+        h->part_slots = std::max<size_t>(h->counter_cap * 4, (64ull << 20) / per_slot);
+        if (cudaMalloc(&h->part_o, h->part_slots * nq * cfg.v_head_dim * sizeof(float)) != cudaSuccess ||
+            cudaMalloc(&h->part_ml, h->part_slots * nq * 2 * sizeof(float)) != cudaSuccess ||
+            cudaMalloc(&h->counters, h->counter_cap * sizeof(int)) != cudaSuccess)
+            return bail(fail(ND_ATTN_ERR_NOMEM, "split-KV scratch allocation failed"));
+        cudaMemsetAsync(h->counters, 0, h->counter_cap * sizeof(int), h->stream);
+    }
+    if (cudaStreamSynchronize(h->stream) != cudaSuccess)
+        return bail(fail(ND_ATTN_ERR_CUDA, "initialisation failed: %s", cudaGetErrorString(cudaGetLastError())));
+    *out = h;
+    return ND_ATTN_OK;
+}
+
+void nd_attn_close(nd_attn *h) {
+    if (!h) return;
+    DeviceGuard dg(h->cfg.device);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    cudaFree(h->kc); cudaFree(h->vc); cudaFree(h->ks); cudaFree(h->vs);
+    cudaFree(h->rope); cudaFree(h->norms); cudaFree(h->d_state); cudaFree(h->d_btab);
+    cudaFree(h->part_o); cudaFree(h->part_ml); cudaFree(h->counters);
+    cudaFree(h->d_tok); cudaFree(h->d_u32); cudaFree(h->d_err); cudaFree(h->dio);
+    if (h->pin) cudaFreeHost(h->pin);
+    if (h->own) cudaStreamDestroy(h->own);
+    delete h;
+}
+
+int nd_attn_set_head_norm(nd_attn *h, uint32_t layer, const float *q_scale, const float *k_scale) {
+    if (!h) return fail(ND_ATTN_ERR_ARG, "null handle");
+    if (layer >= h->cfg.n_layers) return fail(ND_ATTN_ERR_RANGE, "layer %u", layer);
+    if (!q_scale != !k_scale) return fail(ND_ATTN_ERR_ARG, "q and k norm scales go together");
+    DeviceGuard dg(h->cfg.device);
+    if (!q_scale) {
+        h->has_norm[layer] = 0;
+        return ND_ATTN_OK;
+    }
+    const size_t qk = h->cfg.qk_head_dim;
+    ND_CUDA(cudaStreamSynchronize(h->stream));
+    ND_CUDA(cudaMemcpy(h->norms + layer * 2 * qk, q_scale, qk * sizeof(float), cudaMemcpyHostToDevice));
+    ND_CUDA(cudaMemcpy(h->norms + layer * 2 * qk + qk, k_scale, qk * sizeof(float), cudaMemcpyHostToDevice));
+    h->has_norm[layer] = 1;
+    return ND_ATTN_OK;
+}
+
+int nd_attn_reset(nd_attn *h, uint32_t seq) {
+    int rc = check_seq(h, seq);
+    if (rc) return rc;
+    DeviceGuard dg(h->cfg.device);
+    h->seqs[seq] = HostSeq();
+    return push_state(h, seq);
+}
+
+int nd_attn_set_sink(nd_attn *h, uint32_t seq, uint32_t n) {
+    int rc = check_seq(h, seq);
+    if (rc) return rc;
+    DeviceGuard dg(h->cfg.device);
+    const uint32_t cap = h->cfg.window > 64u ? h->cfg.window - 64u : 0u;  // ND_MIN_RECENT
+    h->seqs[seq].n_sink = n > cap ? cap : n;
+    return push_state(h, seq);
+}
+
+int nd_attn_snapshot(nd_attn *h, uint32_t seq) {
+    int rc = check_seq(h, seq);
+    if (rc) return rc;
+    HostSeq &s = h->seqs[seq];
+    const uint32_t cap = h->cfg.window > 64u ? h->cfg.window - 64u : 0u;
+    DeviceGuard dg(h->cfg.device);
+    s.n_sink = s.pos > cap ? cap : s.pos;
+    s.snap_pos = s.pos;
+    s.has_snap = 1;
+    return push_state(h, seq);
+}
+
+int nd_attn_rewind(nd_attn *h, uint32_t seq) {
+    int rc = check_seq(h, seq);
+    if (rc) return rc;
+    HostSeq &s = h->seqs[seq];
+    if (!s.has_snap) return nd_attn_reset(h, seq);
+    DeviceGuard dg(h->cfg.device);
+    s.pos = s.snap_pos;
+    return push_state(h, seq);
+}
+
+int nd_attn_advance(nd_attn *h, uint32_t n, const uint32_t *seq_ids, const uint32_t *len) {
+    if (!h) return fail(ND_ATTN_ERR_ARG, "null handle");
+    if (n == 0) return ND_ATTN_OK;
+    if (n > h->cfg.max_seqs) return fail(ND_ATTN_ERR_RANGE, "%u sequences", n);
+    for (uint32_t i = 0; i < n; i++)
+        if ((seq_ids ? seq_ids[i] : i) >= h->cfg.max_seqs) return fail(ND_ATTN_ERR_RANGE, "sequence id");
+    DeviceGuard dg(h->cfg.device);
+    const uint32_t *d_ids = nullptr, *d_len = nullptr;
+    if (seq_ids || len) {
+        int rc = grow(&h->d_u32, &h->u32_cap, 2 * (size_t)n);
+        if (rc) return rc;
+        if (seq_ids) {
+            ND_CUDA(cudaMemcpyAsync(h->d_u32, seq_ids, n * sizeof(uint32_t), cudaMemcpyHostToDevice, h->stream));
+            d_ids = h->d_u32;
+        }
+        if (len) {
+            ND_CUDA(cudaMemcpyAsync(h->d_u32 + n, len, n * sizeof(uint32_t), cudaMemcpyHostToDevice, h->stream));
+            d_len = h->d_u32 + n;
+        }
+    }
+    for (uint32_t i = 0; i < n; i++) h->seqs[seq_ids ? seq_ids[i] : i].pos += len ? len[i] : 1;
+    advance_kernel<<<(n + 127) / 128, 128, 0, h->stream>>>(h->d_state, n, d_ids, d_len, 1);
+    h->launches++;
+    ND_CUDA(cudaGetLastError());
+    return ND_ATTN_OK;
+}
+
+int nd_attn_get_state(nd_attn *h, uint32_t seq, uint32_t *pos, uint32_t *n_sink) {
+    int rc = check_seq(h, seq);
+    if (rc) return rc;
+    if (pos) *pos = h->seqs[seq].pos;
+    if (n_sink) *n_sink = h->seqs[seq].n_sink;
+    return ND_ATTN_OK;
+}
+
+int nd_attn_set_state(nd_attn *h, uint32_t seq, uint32_t pos, uint32_t n_sink) {
+    int rc = check_seq(h, seq);
+    if (rc) return rc;
+    if (n_sink >= h->cfg.window) return fail(ND_ATTN_ERR_RANGE, "n_sink %u >= window", n_sink);
+    DeviceGuard dg(h->cfg.device);
+    h->seqs[seq].pos = pos;
+    h->seqs[seq].n_sink = n_sink;
+    return push_state(h, seq);
+}
+
+int nd_attn_decode(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const void *q,
+                   const void *k, const void *v, const void *gate, void *out) {
+    int rc = check_call(h, layer, n, seq_ids, nullptr);
+    if (rc) return rc;
+    if (!q || !k || !v || !out) return fail(ND_ATTN_ERR_ARG, "null tensor");
+    DeviceGuard dg(h->cfg.device);
+    std::vector<uint32_t> tpos(n), tseq(n);
+    std::vector<TokMeta> tok;
+    for (uint32_t i = 0; i < n; i++) {
+        tseq[i] = seq_ids ? seq_ids[i] : i;
+        tpos[i] = h->seqs[tseq[i]].pos;
+    }
+    const TokMeta *d_tok = nullptr;
+    if (seq_ids) {
+        tok.resize(n);
+        for (uint32_t i = 0; i < n; i++) tok[i] = TokMeta{tseq[i], 0u, i};
+        rc = upload_tok(h, tok);
+        if (rc) return rc;
+        d_tok = h->d_tok;
+    }
+    return run_attend(h, layer, n, d_tok, tpos, tseq, 1, q, k, v, gate, out);
+}
+
+int nd_attn_prefill(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const uint32_t *len,
+                    const void *q, const void *k, const void *v, const void *gate, void *out) {
+    if (!len) return fail(ND_ATTN_ERR_ARG, "null len");
+    int rc = check_call(h, layer, n, seq_ids, len);
+    if (rc) return rc;
+    if (!q || !k || !v || !out) return fail(ND_ATTN_ERR_ARG, "null tensor");
+    DeviceGuard dg(h->cfg.device);
+    const uint32_t W = h->cfg.window;
+    size_t total = 0;
+    uint32_t maxlen = 0;
+    bool wraps = false;
+    std::vector<uint32_t> cu(n);
+    for (uint32_t i = 0; i < n; i++) {
+        const uint32_t s = seq_ids ? seq_ids[i] : i;
+        cu[i] = (uint32_t)total;
+        total += len[i];
+        maxlen = std::max(maxlen, len[i]);
+        if ((uint64_t)h->seqs[s].pos + len[i] > W) wraps = true;
+    }
+    if (total == 0) return ND_ATTN_OK;
+    if (total > 0x7fffffffu / h->cfg.n_kv_heads) return fail(ND_ATTN_ERR_RANGE, "too many tokens");
+    if (!wraps) {
+        // Every new position gets its own slot and nothing a token reads is
+        // overwritten: append all tokens, then attend causally.
+        std::vector<TokMeta> tok(total);
+        std::vector<uint32_t> tpos(total), tseq(total);
+        for (uint32_t i = 0; i < n; i++) {
+            const uint32_t s = seq_ids ? seq_ids[i] : i;
+            for (uint32_t t = 0; t < len[i]; t++) {
+                tok[cu[i] + t] = TokMeta{s, t, cu[i] + t};
+                tpos[cu[i] + t] = h->seqs[s].pos + t;
+                tseq[cu[i] + t] = s;
+            }
+        }
+        rc = upload_tok(h, tok);
+        if (rc) return rc;
+        AttnParams P = base_params(h, layer);
+        P.k = k; P.v = v; P.tok = h->d_tok; P.n_tok = (uint32_t)total;
+        ND_CUDA(append_launch(h, P));
+        h->launches++;
+        return run_attend(h, layer, (uint32_t)total, h->d_tok, tpos, tseq, 0, q, k, v, gate, out);
+    }
+    // The ring wraps inside this call: a later token's slot can hold a position
+    // an earlier token still reads, so run the reference's token-at-a-time
+    // order (append, then attend) step by step.
+    for (uint32_t t = 0; t < maxlen; t++) {
+        std::vector<TokMeta> tok;
+        std::vector<uint32_t> tpos, tseq;
+        for (uint32_t i = 0; i < n; i++) {
+            if (t >= len[i]) continue;
+            const uint32_t s = seq_ids ? seq_ids[i] : i;
+            tok.push_back(TokMeta{s, t, cu[i] + t});
+            tpos.push_back(h->seqs[s].pos + t);
+            tseq.push_back(s);
+        }
+        rc = upload_tok(h, tok);
+        if (rc) return rc;
+        rc = run_attend(h, layer, (uint32_t)tok.size(), h->d_tok, tpos, tseq, 1, q, k, v, gate, out);
+        if (rc) return rc;
+    }
+    return ND_ATTN_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Host-buffer form: q/k/v/gate/out live in host memory.
+int run_host(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const uint32_t *len,
+             const void *q, const void *k, const void *v, const void *gate, void *out) {
+    if (!h) return fail(ND_ATTN_ERR_ARG, "null handle");
+    int rc = check_call(h, layer, n, seq_ids, len);
+    if (rc) return rc;
+    if (!q || !k || !v || !out) return fail(ND_ATTN_ERR_ARG, "null tensor");
+    DeviceGuard dg(h->cfg.device);
+    size_t tokens = 0;
+    for (uint32_t i = 0; i < n; i++) tokens += len ? len[i] : 1;
+    const size_t b[5] = {act_bytes(h, tokens, 0), act_bytes(h, tokens, 1), act_bytes(h, tokens, 2),
+                         gate ? act_bytes(h, tokens, 3) : 0, act_bytes(h, tokens, 4)};
+    size_t off[5], total = 0;
+    for (int i = 0; i < 5; i++) {
+        off[i] = total;
+        total += (b[i] + 255) / 256 * 256;
+    }
+    rc = grow(reinterpret_cast<char **>(&h->dio), &h->dio_cap, total);
+    if (rc) return rc;
+    char *d = static_cast<char *>(h->dio);
+    const void *src[4] = {q, k, v, gate};
+    for (int i = 0; i < 4; i++) {
+        if (!b[i]) continue;
+        // Pinned sources copy asynchronously; pageable ones are staged by the
+        // driver before the call returns.
+        ND_CUDA(cudaMemcpyAsync(d + off[i], src[i], b[i], cudaMemcpyHostToDevice, h->stream));
+    }
+    rc = len ? nd_attn_prefill(h, layer, n, seq_ids, len, d + off[0], d + off[1], d + off[2],
+                               gate ? d + off[3] : nullptr, d + off[4])
+             : nd_attn_decode(h, layer, n, seq_ids, d + off[0], d + off[1], d + off[2],
+                              gate ? d + off[3] : nullptr, d + off[4]);
+    if (rc) return rc;
+    ND_CUDA(cudaMemcpyAsync(out, d + off[4], b[4], cudaMemcpyDeviceToHost, h->stream));
+    return nd_attn_sync(h);
+}
+
+}  // namespace
+
+extern "C" {
+
+int nd_attn_decode_host(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const void *q,
+                        const void *k, const void *v, const void *gate, void *out) {
+    return run_host(h, layer, n, seq_ids, nullptr, q, k, v, gate, out);
+}
+
+int nd_attn_prefill_host(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const uint32_t *len,
+                         const void *q, const void *k, const void *v, const void *gate, void *out) {
+    if (!len) return fail(ND_ATTN_ERR_ARG, "null len");
+    return run_host(h, layer, n, seq_ids, len, q, k, v, gate, out);
+}
+
+// ---- prefix ------------------------------------------------------------------
+nd_attn_prefix *nd_attn_prefix_save(nd_attn *h, uint32_t seq) {
+    if (check_seq(h, seq)) return nullptr;
+    const HostSeq &s = h->seqs[seq];
+    if (!s.has_snap || s.pos != s.snap_pos) {
+        fail(ND_ATTN_ERR_ARG, "prefix_save needs a snapshot at the current position");
+        return nullptr;
+    }
+    DeviceGuard dg(h->cfg.device);
+    const nd_attn_config &c = h->cfg;
+    const uint32_t live = std::min(s.snap_pos + 1u, c.window);
+    const size_t krow = h->k_dim * h->kes, vrow = h->v_dim * h->kes, srow = c.n_kv_heads * sizeof(float);
+    const bool sc = c.kv_dtype == ND_DT_I8;
+    const size_t bytes = (size_t)c.n_layers * live * (krow + vrow + (sc ? 2 * srow : 0));
+    nd_attn_prefix *p = new nd_attn_prefix();
+    p->owner = h; p->pos = s.snap_pos; p->sink = s.n_sink; p->live = live; p->bytes = bytes;
+    if (cudaMalloc(&p->dev, std::max<size_t>(bytes, 4)) != cudaSuccess) {
+        fail(ND_ATTN_ERR_NOMEM, "prefix allocation of %zu bytes failed", bytes);
+        delete p;
+        return nullptr;
+    }
+    CacheView cv = layer_view(h, 0);
+    char *dst = static_cast<char *>(p->dev);
+    struct Part { void *base; size_t row; } parts[4] = {{h->kc, krow}, {h->vc, vrow}, {h->ks, srow}, {h->vs, srow}};
+    for (int i = 0; i < (sc ? 4 : 2); i++) {
+        rows_copy_kernel<<<dim3(std::min<uint32_t>(live, 1024u), c.n_layers), 128, 0, h->stream>>>(
+            static_cast<char *>(parts[i].base), h->rows_per_layer * parts[i].row, dst, live * parts[i].row,
+            (uint32_t)(parts[i].row / 4), live, cv, seq, 0, 0);
+        h->launches++;
+        dst += (size_t)c.n_layers * live * parts[i].row;
+    }
+    if (cudaStreamSynchronize(h->stream) != cudaSuccess) {
+        fail(ND_ATTN_ERR_CUDA, "prefix copy failed: %s", cudaGetErrorString(cudaGetLastError()));
+        cudaFree(p->dev);
+        delete p;
+        return nullptr;
+    }
+    return p;
+}
+
+int nd_attn_prefix_restore(nd_attn *h, uint32_t seq, const nd_attn_prefix *p) {
+    if (!p || !h || p->owner != h) return fail(ND_ATTN_ERR_ARG, "prefix belongs to another handle");
+    int rc = check_seq(h, seq);
+    if (rc) return rc;
+    DeviceGuard dg(h->cfg.device);
+    const nd_attn_config &c = h->cfg;
+    HostSeq &s = h->seqs[seq];
+    s.snap_pos = p->pos;
+    s.n_sink = p->sink;
+    const size_t krow = h->k_dim * h->kes, vrow = h->v_dim * h->kes, srow = c.n_kv_heads * sizeof(float);
+    const bool sc = c.kv_dtype == ND_DT_I8;
+    CacheView cv = layer_view(h, 0);
+    char *src = static_cast<char *>(p->dev);
+    struct Part { void *base; size_t row; } parts[4] = {{h->kc, krow}, {h->vc, vrow}, {h->ks, srow}, {h->vs, srow}};
+    for (int i = 0; i < (sc ? 4 : 2); i++) {
+        rows_copy_kernel<<<dim3(std::min<uint32_t>(p->live, 1024u), c.n_layers), 128, 0, h->stream>>>(
+            static_cast<char *>(parts[i].base), h->rows_per_layer * parts[i].row, src, p->live * parts[i].row,
+            (uint32_t)(parts[i].row / 4), p->live, cv, seq, 0, 1);
+        h->launches++;
+        src += (size_t)c.n_layers * p->live * parts[i].row;
+    }
+    ND_CUDA(cudaGetLastError());
+    s.has_snap = 1;
+    s.pos = s.snap_pos;  // nd_model_rewind
+    return push_state(h, seq);
+}
+
+void nd_attn_prefix_free(nd_attn_prefix *p) {
+    if (!p) return;
+    if (p->owner) {
+        DeviceGuard dg(p->owner->cfg.device);
+        cudaFree(p->dev);
+    }
+    delete p;
+}
+
+int nd_attn_prefix_read(const nd_attn_prefix *p, void *host, size_t cap, size_t *bytes, uint32_t *pos,
+                        uint32_t *n_sink) {
+    if (!p) return fail(ND_ATTN_ERR_ARG, "null prefix");
+    if (bytes) *bytes = p->bytes;
+    if (pos) *pos = p->pos;
+    if (n_sink) *n_sink = p->sink;
+    if (host && cap >= p->bytes && p->bytes) {
+        DeviceGuard dg(p->owner->cfg.device);
+        ND_CUDA(cudaStreamSynchronize(p->owner->stream));
+        ND_CUDA(cudaMemcpy(host, p->dev, p->bytes, cudaMemcpyDeviceToHost));
+    }
+    return ND_ATTN_OK;
+}
+
+// ---- cache access ----------------------------------------------------------------
+static int cache_io(nd_attn *h, uint32_t layer, uint32_t seq, uint32_t slot0, uint32_t n_slots, void *k, void *v,
+                    float *k_scale, float *v_scale, int to_cache) {
+    int rc = check_seq(h, seq);
+    if (rc) return rc;
+    if (layer >= h->cfg.n_layers) return fail(ND_ATTN_ERR_RANGE, "layer %u", layer);
+    if ((uint64_t)slot0 + n_slots > h->cfg.window) return fail(ND_ATTN_ERR_RANGE, "slots beyond the window");
+    if (n_slots == 0) return ND_ATTN_OK;
+    DeviceGuard dg(h->cfg.device);
+    const nd_attn_config &c = h->cfg;
+    const size_t krow = h->k_dim * h->kes, vrow = h->v_dim * h->kes, srow = c.n_kv_heads * sizeof(float);
+    const bool sc = c.kv_dtype == ND_DT_I8;
+    const size_t need = (size_t)n_slots * (krow + vrow + 2 * srow);
+    rc = grow(reinterpret_cast<char **>(&h->dio), &h->dio_cap, need + 1024);
+    if (rc) return rc;
+    char *d = static_cast<char *>(h->dio);
+    CacheView cv = layer_view(h, layer);
+    struct Part { void *cache; void *user; size_t row; } parts[4] = {
+        {cv.k, k, krow}, {cv.v, v, vrow}, {cv.ks, k_scale, srow}, {cv.vs, v_scale, srow}};
+    size_t off = 0;
+    for (int i = 0; i < 4; i++) {
+        if (i >= 2 && !sc) break;
+        if (!parts[i].user) continue;
+        const size_t nb = n_slots * parts[i].row;
+        char *dense = to_cache ? static_cast<char *>(parts[i].user) : d + off;
+        rows_copy_kernel<<<dim3(std::min<uint32_t>(n_slots, 4096u), 1), 128, 0, h->stream>>>(
+            static_cast<char *>(parts[i].cache), 0, dense, 0, (uint32_t)(parts[i].row / 4), n_slots, cv, seq,
+            slot0, to_cache);
+        h->launches++;
+        ND_CUDA(cudaGetLastError());
+        if (!to_cache) ND_CUDA(cudaMemcpyAsync(parts[i].user, d + off, nb, cudaMemcpyDeviceToHost, h->stream));
+        off += (nb + 255) / 256 * 256;
+    }
+    return nd_attn_sync(h);
+}
+
+int nd_attn_read_cache(nd_attn *h, uint32_t layer, uint32_t seq, uint32_t slot0, uint32_t n_slots, void *k,
+                       void *v, float *k_scale, float *v_scale) {
+    return cache_io(h, layer, seq, slot0, n_slots, k, v, k_scale, v_scale, 0);
+}
+
+int nd_attn_write_cache(nd_attn *h, uint32_t layer, uint32_t seq, uint32_t slot0, uint32_t n_slots,
+                        const void *k, const void *v, const float *k_scale, const float *v_scale) {
+    return cache_io(h, layer, seq, slot0, n_slots, const_cast<void *>(k), const_cast<void *>(v),
+                    const_cast<float *>(k_scale), const_cast<float *>(v_scale), 1);
+}
+
+int nd_attn_set_block_table(nd_attn *h, uint32_t seq, const int32_t *pages) {
+    int rc = check_seq(h, seq);
+    if (rc) return rc;
+    if (!h->cfg.block_size) return fail(ND_ATTN_ERR_ARG, "handle is not paged");
+    if (!pages) return fail(ND_ATTN_ERR_ARG, "null page list");
+    for (uint32_t i = 0; i < h->blocks_per_seq; i++)
+        if (pages[i] < 0 || (uint32_t)pages[i] >= h->cfg.n_blocks)
+            return fail(ND_ATTN_ERR_RANGE, "page %d out of range", pages[i]);
+    DeviceGuard dg(h->cfg.device);
+    ND_CUDA(cudaMemcpyAsync(h->d_btab + (size_t)seq * h->blocks_per_seq, pages, h->blocks_per_seq * sizeof(int32_t),
+                            cudaMemcpyHostToDevice, h->stream));
+    return nd_attn_sync(h);
+}
+
+int nd_attn_sync(nd_attn *h) {
+    if (!h) return fail(ND_ATTN_ERR_ARG, "null handle");
+    DeviceGuard dg(h->cfg.device);
+    ND_CUDA(cudaStreamSynchronize(h->stream));
+    int err = 0;
+    ND_CUDA(cudaMemcpy(&err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err) {
+        cudaMemset(h->d_err, 0, sizeof(int));
+        cudaMemset(h->counters, 0, h->counter_cap * sizeof(int));
+        return fail(err == 3 ? ND_ATTN_ERR_TIMEOUT : ND_ATTN_ERR_RANGE,
+                    "device reported status %d (position/state out of range or bounded wait expired)", err);
+    }
+    return ND_ATTN_OK;
+}
+
+void *nd_attn_stream(nd_attn *h) { return h ? static_cast<void *>(h->stream) : nullptr; }
+
+int nd_attn_set_stream(nd_attn *h, void *stream) {
+    if (!h) return fail(ND_ATTN_ERR_ARG, "null handle");
+    DeviceGuard dg(h->cfg.device);
+    ND_CUDA(cudaStreamSynchronize(h->stream));
+    h->stream = stream ? static_cast<cudaStream_t>(stream) : h->own;
+    return ND_ATTN_OK;
+}
+
+uint64_t nd_attn_launch_count(const nd_attn *h) { return h ? h->launches : 0; }
+
+const char *nd_attn_last_error(void) { return g_err.c_str(); }
+
+const char *nd_attn_version(void) {
+    static char buf[64];
+    if (!buf[0]) snprintf(buf, sizeof(buf), "nd_attn 0.1 sm_100a cudart %d", CUDART_VERSION);
+    return buf;
+}
+
+}  // extern "C"

@@ -1,0 +1,407 @@
+"""Parity of the CUDA path (through the C ABI) with the oracle and the
+reference's golden fixtures.
+
+Bars: KV cache bytes, scales, slot layout and saved-prefix images bit-exact;
+attention outputs within max|d| <= 1e-3 * max(1, |ref|) of the fp64 oracle or
+of the reference's fp32 output (harness.TOL)."""
+import hashlib
+import os
+import sys
+
+import numpy as np
+import pytest
+
+import ndattn
+import ndoracle as O
+from harness import TOL, cache_bits, dev, oracle_cache, random_kv_rows, rel_err
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "golden"))
+import make_golden as G  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _out(n_tok, H, VD, dt=O.F32):
+    import torch
+    from harness import torch_dtype
+    return torch.zeros((n_tok, H * VD), dtype=torch_dtype(dt), device="cuda")
+
+
+def _np(t):
+    import torch
+    return t.float().cpu().numpy() if t.dtype != torch.float32 else t.cpu().numpy()
+
+
+# ------------------------------------------------------------------ golden
+@pytest.mark.parametrize("name", sorted(G.CASES))
+def test_golden_int8_session(name):
+    """The reference's own session (prefix prefill, snapshot, suffix, decode)
+    on the GPU: int8 caches and prefix image byte-identical to the reference,
+    outputs within TOL of the reference's."""
+    c = G.CASES[name]
+    gold = np.load(os.path.join(HERE, "golden", name + ".npz"))
+    q, k, v, norms, gate = G.inputs(c)
+    L, H, HKV, QK, VD, W, P = c["L"], c["H"], c["HKV"], c["QK"], c["VD"], c["W"], c["prefix"]
+    a = ndattn.Attn(n_layers=L, n_heads=H, n_kv_heads=HKV, qk_head_dim=QK, v_head_dim=VD, window=W,
+                    rope_theta=c["theta"], kv_dtype="i8", act_dtype="f32")
+    if norms:
+        for l, (qs, ks) in enumerate(norms):
+            a.set_head_norm(l, qs, ks)
+    g = lambda t0, t1, l: None if gate is None else dev(gate[t0:t1, l], O.F32)  # noqa: E731
+    out = _out(P, H, VD)
+    for l in range(L):                                  # prefix: one prefill call per layer
+        a.prefill(l, [P], dev(q[:P, l], O.F32), dev(k[:P, l], O.F32), dev(v[:P, l], O.F32), out, gate=g(0, P, l))
+    a.advance(1, lens=[P])
+    a.snapshot(0)
+    pre = a.prefix_save(0)
+    img, ppos, psink = pre.read()
+    assert (ppos, psink) == (P, int(gold["sink"]))
+    assert hashlib.sha256(img.tobytes()).hexdigest() == str(gold["prefix_sha"])
+    got = np.zeros((c["tokens"], L, H * VD), np.float32)
+    n_suffix = c["tokens"] // 2
+    out = _out(n_suffix, H, VD)
+    for l in range(L):                                  # suffix: batched prefill
+        a.prefill(l, [n_suffix], dev(q[P:P + n_suffix, l], O.F32), dev(k[P:P + n_suffix, l], O.F32),
+                  dev(v[P:P + n_suffix, l], O.F32), out, gate=g(P, P + n_suffix, l))
+        a.sync()
+        got[:n_suffix, l] = _np(out)
+    a.advance(1, lens=[n_suffix])
+    out = _out(1, H, VD)
+    for t in range(P + n_suffix, P + c["tokens"]):     # decode
+        for l in range(L):
+            a.decode(l, 1, dev(q[t:t + 1, l], O.F32), dev(k[t:t + 1, l], O.F32), dev(v[t:t + 1, l], O.F32), out,
+                     gate=g(t, t + 1, l))
+            a.sync()
+            got[t - P, l] = _np(out)[0]
+        a.advance(1)
+    assert rel_err(got, gold["out"]) <= TOL
+    ks_all, vs_all, kk, vv = [], [], [], []
+    for l in range(L):
+        kl, vl, ksl, vsl = a.read_cache(l, 0, 0, W)
+        kk.append(kl); vv.append(vl); ks_all.append(ksl); vs_all.append(vsl)
+    assert hashlib.sha256(np.stack(kk).tobytes()).hexdigest() == str(gold["k_sha"])
+    assert hashlib.sha256(np.stack(vv).tobytes()).hexdigest() == str(gold["v_sha"])
+    assert np.array_equal(np.stack(ks_all), gold["ks"]) and np.array_equal(np.stack(vs_all), gold["vs"])
+    pre.free()
+    a.close()
+
+
+# ------------------------------------------------------------- sessions
+def run_session(kv_dt, act_dt, H, HKV, QK, VD, W, L, lens_seq, seed, n_seqs=1, norm=False, gate=False,
+                sink_after=None, decode_steps=0, block_size=0, shuffle_pages=False, max_pos=None):
+    """Same seeded tokens through the GPU (prefill calls of lens_seq[i] tokens,
+    then decode steps, n_seqs sequences in each call) and through one
+    OracleSeq per sequence. Returns (worst rel err, gpu handle, oracle seqs)."""
+    rng = np.random.default_rng(seed)
+    max_pos = max_pos or (sum(lens_seq) + decode_steps + 1)
+    a = ndattn.Attn(n_layers=L, n_heads=H, n_kv_heads=HKV, qk_head_dim=QK, v_head_dim=VD, window=W,
+                    max_seqs=n_seqs, kv_dtype=kv_dt, act_dtype=act_dt, out_dtype="f32", block_size=block_size,
+                    max_pos=max_pos)
+    seqs = [O.OracleSeq(L, H, HKV, QK, VD, W, kv_dt, max_pos=max_pos) for _ in range(n_seqs)]
+    if block_size:
+        nb = W // block_size
+        pages = np.arange(n_seqs * nb)
+        if shuffle_pages:
+            rng.shuffle(pages)
+        for s in range(n_seqs):
+            a.set_block_table(s, pages[s * nb:(s + 1) * nb])
+    if norm:
+        for l in range(L):
+            qs = (rng.standard_normal(QK) * 0.1).astype(np.float32)
+            ks = (rng.standard_normal(QK) * 0.1).astype(np.float32)
+            a.set_head_norm(l, qs, ks)
+            for s in seqs:
+                s.norms[l] = (qs, ks)
+    worst = 0.0
+    calls = [("prefill", n) for n in lens_seq] + [("decode", 1)] * decode_steps
+    for ci, (kind, n) in enumerate(calls):
+        if sink_after is not None and ci == sink_after:
+            for s in range(n_seqs):
+                a.snapshot(s)
+                seqs[s].snapshot()
+        T = n * n_seqs
+        q = (rng.standard_normal((T, H * QK)) * 0.5).astype(np.float32)
+        k = (rng.standard_normal((T, HKV * QK)) * 0.5).astype(np.float32)
+        v = (rng.standard_normal((T, HKV * VD)) * 0.5).astype(np.float32)
+        gt = rng.standard_normal((T, H * VD)).astype(np.float32) if gate else None
+        qa, ka, va = (O.round_act(x, act_dt) for x in (q, k, v))
+        ga = None if gt is None else O.round_act(gt, act_dt)
+        for l in range(L):
+            out = _out(T, H, VD)
+            if kind == "prefill":
+                a.prefill(l, [n] * n_seqs, dev(q, act_dt), dev(k, act_dt), dev(v, act_dt), out,
+                          gate=None if gt is None else dev(gt, act_dt))
+            else:
+                a.decode(l, n_seqs, dev(q, act_dt), dev(k, act_dt), dev(v, act_dt), out,
+                         gate=None if gt is None else dev(gt, act_dt))
+            a.sync()
+            got = _np(out)
+            for s in range(n_seqs):
+                for t in range(n):
+                    r = s * n + t
+                    want = seqs[s].step(l, qa[r], ka[r], va[r], None if ga is None else ga[r], off=t)
+                    worst = max(worst, rel_err(got[r].reshape(H, VD), want))
+        a.advance(n_seqs, lens=[n] * n_seqs)
+        for s in seqs:
+            s.advance(n)
+    return worst, a, seqs
+
+
+def check_caches(a, seqs, kv_dt, L, W):
+    for s, seq in enumerate(seqs):
+        for l in range(L):
+            k, v, ks, vs = a.read_cache(l, s, 0, W)
+            ok, ov = oracle_cache(seq, l, kv_dt)
+            assert np.array_equal(cache_bits(k), cache_bits(ok)), (s, l)
+            assert np.array_equal(cache_bits(v), cache_bits(ov)), (s, l)
+            if kv_dt == O.I8:
+                assert np.array_equal(ks, seq.ks[l]) and np.array_equal(vs, seq.vs[l])
+
+
+@pytest.mark.parametrize("kv_dt,act_dt", [(O.F32, O.F32), (O.I8, O.F32), (O.F16, O.F16), (O.BF16, O.BF16),
+                                          (O.F16, O.F32)])
+def test_config1_shape_all_dtypes(kv_dt, act_dt):
+    """Config 1's shape (8x64 MHA, 213 prefix pinned, 40 suffix, 32 decode)."""
+    worst, a, seqs = run_session(kv_dt, act_dt, 8, 8, 64, 64, 384, 1, [213, 40], seed=0, sink_after=1,
+                                 decode_steps=32)
+    assert worst <= TOL
+    check_caches(a, seqs, kv_dt, 1, 384)
+    a.close()
+
+
+@pytest.mark.parametrize("kv_dt", [O.I8, O.BF16])
+def test_gqa_norm_gate_real_geometry(kv_dt):
+    """The reference model's geometry: 12/2 heads, qk 48 / v 64, norms, gates."""
+    worst, a, seqs = run_session(kv_dt, O.F32, 12, 2, 48, 64, 384, 2, [40, 17], seed=5, norm=True, gate=True,
+                                 sink_after=1, decode_steps=6, n_seqs=3)
+    assert worst <= TOL
+    check_caches(a, seqs, kv_dt, 2, 384)
+    a.close()
+
+
+@pytest.mark.parametrize("kv_dt", [O.I8, O.F16])
+def test_ring_wrap_decode_and_prefill(kv_dt):
+    """window 128 with 20 sinks: positions wrap the ring in both a wrapping
+    prefill call (token-at-a-time path) and in decode."""
+    worst, a, seqs = run_session(kv_dt, O.F32, 8, 2, 64, 64, 128, 1, [20, 90, 60], seed=9, sink_after=1,
+                                 decode_steps=40, n_seqs=2)
+    assert worst <= TOL
+    check_caches(a, seqs, kv_dt, 1, 128)
+    a.close()
+
+
+def test_gqa_prefill_bf16_config3_shape():
+    """Config 3's head shape (16/4, hd64, bf16) at a reduced length."""
+    worst, a, seqs = run_session(O.BF16, O.BF16, 16, 4, 64, 64, 512, 1, [300], seed=2, n_seqs=2)
+    assert worst <= TOL
+    check_caches(a, seqs, O.BF16, 1, 512)
+    a.close()
+
+
+def test_paged_hd128_shuffled_blocks():
+    """Config 4's shape (8x128 fp16, 64-slot pages, shuffled block table)."""
+    worst, a, seqs = run_session(O.F16, O.F16, 8, 8, 128, 128, 1024, 1, [700], seed=3, n_seqs=3, block_size=64,
+                                 shuffle_pages=True, decode_steps=5)
+    assert worst <= TOL
+    check_caches(a, seqs, O.F16, 1, 1024)
+    a.close()
+
+
+def test_long_context_decode_split_kv():
+    """Synthetic cached contexts (written straight into the cache) of ragged
+    lengths up to 2048, fp16, 8x64: many splits per sequence, then decode.
+    1% of K rows scaled x8 for a peaky softmax."""
+    import torch
+    rng = np.random.default_rng(1)
+    H = HKV = 8
+    QK = VD = 64
+    W, L, B = 2304, 2, 6
+    ctx = [256, 2048, 1000, 777, 1999, 300]
+    a = ndattn.Attn(n_layers=L, n_heads=H, n_kv_heads=HKV, window=W, max_seqs=B, kv_dtype="f16", act_dtype="f16",
+                    out_dtype="f32", max_pos=W)
+    seqs = [O.OracleSeq(L, H, HKV, QK, VD, W, O.F16, max_pos=W) for _ in range(B)]
+    for s in range(B):
+        for l in range(L):
+            peaky = rng.random(ctx[s]) < 0.01
+            k, _ = random_kv_rows(rng, ctx[s], HKV * QK, O.F16, peaky_rows=peaky)
+            v, _ = random_kv_rows(rng, ctx[s], HKV * VD, O.F16)
+            a.write_cache(l, s, 0, ctx[s], torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
+            seqs[s].k[l, :ctx[s]] = k.view(np.uint16)
+            seqs[s].v[l, :ctx[s]] = v.view(np.uint16)
+        a.set_state(s, ctx[s], 0)
+        seqs[s].pos = ctx[s]
+    worst = 0.0
+    for step in range(3):
+        q = rng.standard_normal((B, H * QK)).astype(np.float32)
+        k = (rng.standard_normal((B, HKV * QK)) * 0.5).astype(np.float32)
+        v = (rng.standard_normal((B, HKV * VD)) * 0.5).astype(np.float32)
+        for l in range(L):
+            out = _out(B, H, VD)
+            a.decode(l, B, dev(q, O.F16), dev(k, O.F16), dev(v, O.F16), out)
+            a.sync()
+            got = _np(out)
+            for s in range(B):
+                want = seqs[s].step(l, O.round_act(q[s], O.F16), O.round_act(k[s], O.F16), O.round_act(v[s], O.F16))
+                worst = max(worst, rel_err(got[s].reshape(H, VD), want))
+        a.advance(B)
+        for s in seqs:
+            s.advance()
+    assert worst <= TOL
+    check_caches(a, seqs, O.F16, L, W)
+    a.close()
+
+
+# --------------------------------------------------------------- entry points
+def test_host_entry_points_match_device():
+    import torch
+    rng = np.random.default_rng(4)
+    H, HKV, QK, VD, W = 8, 8, 64, 64, 384
+    outs = []
+    for host in (False, True):
+        a = ndattn.Attn(n_heads=H, n_kv_heads=HKV, window=W, max_seqs=2, kv_dtype="f16", act_dtype="f16")
+        r = np.random.default_rng(4)
+        for kind, n in (("prefill", 50), ("decode", 1), ("decode", 1)):
+            q = r.standard_normal((2 * n, H * QK)).astype(np.float16)
+            k = r.standard_normal((2 * n, HKV * QK)).astype(np.float16)
+            v = r.standard_normal((2 * n, HKV * VD)).astype(np.float16)
+            out = np.zeros((2 * n, H * VD), np.float16)
+            if host:
+                if kind == "prefill":
+                    a.prefill_host(0, [n, n], q, k, v, out)
+                else:
+                    a.decode_host(0, 2, q, k, v, out)
+            else:
+                t = [torch.from_numpy(x).cuda() for x in (q, k, v)]
+                o = torch.zeros((2 * n, H * VD), dtype=torch.float16, device="cuda")
+                if kind == "prefill":
+                    a.prefill(0, [n, n], *t, o)
+                else:
+                    a.decode(0, 2, *t, o)
+                a.sync()
+                out = o.cpu().numpy()
+            outs.append(out)
+            a.advance(2, lens=[n, n])
+        a.close()
+    n_calls = 3
+    for i in range(n_calls):
+        assert np.array_equal(outs[i], outs[i + n_calls])
+    del rng
+
+
+def test_seq_ids_subset_and_order():
+    """A call over a permuted subset of sequences only touches those."""
+    import torch
+    H, HKV, QK, VD, W = 4, 2, 64, 64, 256
+    rng = np.random.default_rng(8)
+    a = ndattn.Attn(n_heads=H, n_kv_heads=HKV, window=W, max_seqs=5, kv_dtype="bf16", act_dtype="f32")
+    seqs = [O.OracleSeq(1, H, HKV, QK, VD, W, O.BF16) for _ in range(5)]
+    worst = 0.0
+    for step, ids in enumerate(([3, 0, 4], [1], [4, 3, 2, 1, 0], [2, 0])):
+        n = len(ids)
+        q = rng.standard_normal((n, H * QK)).astype(np.float32)
+        k = rng.standard_normal((n, HKV * QK)).astype(np.float32)
+        v = rng.standard_normal((n, HKV * VD)).astype(np.float32)
+        out = _out(n, H, VD)
+        a.decode(0, n, *(torch.from_numpy(x).cuda() for x in (q, k, v)), out, seq_ids=ids)
+        a.sync()
+        got = _np(out)
+        for i, s in enumerate(ids):
+            worst = max(worst, rel_err(got[i].reshape(H, VD), seqs[s].step(0, q[i], k[i], v[i])))
+        a.advance(n, seq_ids=ids)
+        for s in ids:
+            seqs[s].advance()
+    assert worst <= TOL
+    check_caches(a, seqs, O.BF16, 1, W)
+    assert [a.state(s)[0] for s in range(5)] == [s.pos for s in seqs]
+    a.close()
+
+
+def test_prefix_isolation_like_nd_ptest():
+    """host/nd_ptest.c: two schema prefixes saved, then alternating restores
+    must reproduce bit-identical outputs."""
+    import torch
+    H, HKV, QK, VD, W, L = 8, 2, 64, 64, 256, 2
+    rng = np.random.default_rng(12)
+    a = ndattn.Attn(n_layers=L, n_heads=H, n_kv_heads=HKV, window=W, kv_dtype="i8", act_dtype="f32")
+    t = lambda x: torch.from_numpy(x).cuda()  # noqa: E731
+    probe = [rng.standard_normal((1, n)).astype(np.float32) for n in (H * QK, HKV * QK, HKV * VD)]
+    prefixes, expected = [], []
+    for i in range(2):
+        a.reset(0)
+        for _ in range(2 + i):
+            for l in range(L):
+                x = [rng.standard_normal((1, n)).astype(np.float32) for n in (H * QK, HKV * QK, HKV * VD)]
+                a.decode(l, 1, *(t(y) for y in x), _out(1, H, VD))
+            a.advance(1)
+        a.snapshot(0)
+        prefixes.append(a.prefix_save(0))
+        assert prefixes[-1] is not None
+        outs = []
+        for l in range(L):
+            o = _out(1, H, VD)
+            a.decode(l, 1, *(t(y) for y in probe), o)
+            a.sync()
+            outs.append(o.cpu().numpy())
+        expected.append(np.stack(outs))
+    for n in range(4):
+        i = n % 2
+        a.prefix_restore(0, prefixes[i])
+        assert a.state(0) == (2 + i, 2 + i)
+        outs = []
+        for l in range(L):
+            o = _out(1, H, VD)
+            a.decode(l, 1, *(t(y) for y in probe), o)
+            a.sync()
+            outs.append(o.cpu().numpy())
+        assert np.array_equal(np.stack(outs), expected[i])
+    # a prefix of another handle is refused with -1 (nd_model.c:1545)
+    b = ndattn.Attn(n_layers=L, n_heads=H, n_kv_heads=HKV, window=W, kv_dtype="i8", act_dtype="f32")
+    with pytest.raises(ndattn.NdAttnError) as e:
+        b.prefix_restore(0, prefixes[0])
+    assert e.value.code == ndattn.ERR_ARG
+    # prefix_save without a snapshot at the current position returns NULL
+    a.advance(1)
+    assert a.prefix_save(0) is None
+    for p in prefixes:
+        p.free()
+    a.close()
+    b.close()
+
+
+def test_rewind_and_reset_semantics():
+    H, W = 8, 128
+    a = ndattn.Attn(n_heads=H, n_kv_heads=H, window=W, kv_dtype="f32", act_dtype="f32")
+    a.advance(1, lens=[10])
+    a.rewind(0)                       # no snapshot: rewind == reset
+    assert a.state(0) == (0, 0)
+    a.advance(1, lens=[100])
+    a.snapshot(0)                     # sink capped at window - 64
+    assert a.state(0) == (100, 64)
+    a.advance(1, lens=[7])
+    a.rewind(0)
+    assert a.state(0) == (100, 64)
+    a.set_sink(0, 5)
+    assert a.state(0) == (100, 5)
+    a.reset(0)
+    assert a.state(0) == (0, 0)
+    a.close()
+
+
+def test_errors_are_reported_not_hidden():
+    import torch
+    a = ndattn.Attn(n_heads=8, n_kv_heads=8, window=64, max_pos=64, max_seqs=2, kv_dtype="f32")
+    z = lambda n: torch.zeros((1, n), device="cuda")  # noqa: E731
+    a.set_state(0, 64, 0)                                    # at max_pos: no room for a token
+    with pytest.raises(ndattn.NdAttnError) as e:
+        a.decode(0, 1, z(512), z(512), z(512), z(512))
+    assert e.value.code == ndattn.ERR_RANGE
+    with pytest.raises(ndattn.NdAttnError) as e:
+        a.decode(1, 1, z(512), z(512), z(512), z(512))          # layer out of range
+    assert e.value.code == ndattn.ERR_RANGE
+    with pytest.raises(ndattn.NdAttnError) as e:
+        a.decode(0, 2, z(512), z(512), z(512), z(512), seq_ids=[1, 1])
+    assert e.value.code == ndattn.ERR_ARG
+    with pytest.raises(ndattn.NdAttnError):
+        a.reset(5)
+    a.close()
