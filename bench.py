@@ -31,7 +31,7 @@ sys.path.insert(0, os.path.join(ROOT, "esp32-needle-3_b200"))
 
 H = HKV = 8
 QK = VD = 64
-LAYERS = 8
+LAYERS = 8        # config 2; --layers shrinks it only for profiler captures
 BATCH = 64
 CTX_LO, CTX_HI = 256, 2048
 METRIC = "decode tok/s (config 2: 8-layer decode attention, B=64/GPU, ctx U[256,2048], 8x64 MHA, fp16 KV)"
@@ -53,44 +53,65 @@ def ctx_lengths(rank: int):
 
 
 class Clocks:
-    """Samples nvidia-smi during the timed region."""
+    """Samples SM clocks and throttle reasons through NVML every ~2 ms while
+    the timed region runs (nvidia-smi's 100 ms period is longer than a short
+    timed region)."""
 
-    Q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, dev: int):
-        self.dev, self.rows, self.proc = dev, [], None
+        self.dev, self.rows, self.stop, self.t = dev, [], False, None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = None
+            try:
+                import torch
+                uuid = str(torch.cuda.get_device_properties(self.dev).uuid)
+            except Exception:
+                pass
+            h = None
+            if uuid:
+                for i in range(pynvml.nvmlDeviceGetCount()):
+                    hh = pynvml.nvmlDeviceGetHandleByIndex(i)
+                    u = pynvml.nvmlDeviceGetUUID(hh)
+                    u = u.decode() if isinstance(u, bytes) else u
+                    if u.replace("GPU-", "") == uuid.replace("GPU-", ""):
+                        h = hh
+            self.h = h or pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+            self.nv = pynvml
+            self.max = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.t = threading.Thread(target=self._poll, daemon=True)
             self.t.start()
         except Exception:
-            self.proc = None
+            self.t = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+    def _poll(self):
+        nv = self.nv
+        while not self.stop:
+            try:
+                get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                self.rows.append((nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM), get_reasons(self.h)))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self.stop = True
+        if self.t:
+            self.t.join(timeout=2)
 
     def summary(self):
-        sm = [float(r[0]) for r in self.rows if r and r[0].replace(".", "").isdigit()]
-        mx = [float(r[1]) for r in self.rows if len(r) > 1 and r[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in self.rows for n, v in zip(names, r[2:]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(sm)}
+        sm = [r[0] for r in self.rows]
+        reasons = sorted({n for _, m in self.rows for n, bit in self.REASONS.items() if m & bit})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": getattr(self, "max", None), "reasons": reasons, "samples": len(sm),
+                "source": "nvml, ~2 ms period, during the timed region"}
 
 
 def cpu_reference(target_s: float, rank: int, max_steps: int = 128):
@@ -191,10 +212,12 @@ def run_ours(args):
     kev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(LAYERS)] for _ in range(K)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
+        torch.cuda.nvtx.range_push("timed")
         t0.record(stream)
         for i in range(K):
             step(Wm + i, kev[i])
         t1.record(stream)
+        torch.cuda.nvtx.range_pop()
         a.sync()
         if world > 1:
             dist.barrier()
@@ -275,9 +298,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="profiling only: fewer layers than config 2")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
+    globals()["LAYERS"] = args.layers
     if args.impl == "reference":
         run_reference(args)
     else:
