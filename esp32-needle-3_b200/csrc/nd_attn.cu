@@ -14,6 +14,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -239,16 +240,16 @@ cudaError_t append_launch(const nd_attn *h, const AttnParams &P) {
 // longest visit run is jmax and whose runs total `rows`: enough CTAs to cover
 // the SMs twice over, splits that are whole loop iterations, and no more
 // splits than the scratch holds.
-void choose_split(const nd_attn *h, size_t items, uint32_t jmax, size_t rows, uint32_t *chunk,
-                  uint32_t *nsplit) {
+void choose_split(const nd_attn *h, size_t items, uint32_t jmax, size_t rows, size_t counter_cap,
+                  size_t part_slots, uint32_t *chunk, uint32_t *nsplit) {
     const uint32_t per_iter = (uint32_t)nda::attend_rows_per_iter(h->cfg.kv_dtype, (int)h->cfg.v_head_dim);
     const size_t target = (size_t)h->sm_count * 16;
     size_t c = (rows + target - 1) / target;
     c = std::max<size_t>(c, 2 * per_iter);
     c = (c + per_iter - 1) / per_iter * per_iter;
     uint32_t ns = (uint32_t)((jmax + c - 1) / c);
-    if (ns > 1 && (items > h->counter_cap || items * ns > h->part_slots)) {
-        const size_t cap = items > h->counter_cap ? 1 : h->part_slots / items;
+    if (ns > 1 && (items > counter_cap || items * ns > part_slots)) {
+        const size_t cap = items > counter_cap ? 1 : part_slots / items;
         ns = (uint32_t)std::max<size_t>(1, std::min<size_t>(cap, ns));
         c = (jmax + ns - 1) / ns;
         c = (c + per_iter - 1) / per_iter * per_iter;
@@ -303,7 +304,7 @@ int run_attend(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok,
     }
     const size_t items = (size_t)ntok * n_kv;
     uint32_t chunk, nsplit;
-    choose_split(h, items, jmax, rows, &chunk, &nsplit);
+    choose_split(h, items, jmax, rows, h->counter_cap, h->part_slots, &chunk, &nsplit);
     if (items > 0x7fffffffu || nsplit > 65535u) return fail(ND_ATTN_ERR_RANGE, "launch too large");
     AttnParams P = base_params(h, layer);
     P.q = q; P.k = k; P.v = v; P.gate = gate; P.out = out;
@@ -727,6 +728,91 @@ int nd_attn_prefill_host(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t 
                          const void *q, const void *k, const void *v, const void *gate, void *out) {
     if (!len) return fail(ND_ATTN_ERR_ARG, "null len");
     return run_host(h, layer, n, seq_ids, len, q, k, v, gate, out);
+}
+
+}  // extern "C"
+
+// ---- allocation-free decode ------------------------------------------------------
+namespace {
+
+// Fixed split-KV scratch of nd_attn_decode_noalloc, part of the library's
+// device image: [tickets: MAX_ITEMS ints][partial (m,l)][partial o]. In host
+// code `g_noalloc_scratch` names a host-side stand-in, never a device address:
+// the address is looked up per device with cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[ND_ATTN_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_addr[kMaxDevices];
+
+// Device address of the fixed scratch on `dev` (which must be current);
+// looked up once per device.
+int noalloc_scratch(int dev, char **addr) {
+    if (dev < 0 || dev >= kMaxDevices) return fail(ND_ATTN_ERR_ARG, "device ordinal %d", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return fail(ND_ATTN_ERR_CUDA, "cudaGetSymbolAddress of the fixed scratch failed: %s",
+                        cudaGetErrorString(e));
+        g_noalloc_addr[dev] = p;
+    }
+    *addr = static_cast<char *>(g_noalloc_addr[dev]);
+    return ND_ATTN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int nd_attn_decode_noalloc(nd_attn *h, uint32_t layer, uint32_t n, const void *q, const void *k, const void *v,
+                           const void *gate, void *out) {
+    if (!h) return fail(ND_ATTN_ERR_ARG, "null handle");
+    if (!q || !k || !v || !out) return fail(ND_ATTN_ERR_ARG, "null tensor");
+    if (layer >= h->cfg.n_layers) return fail(ND_ATTN_ERR_RANGE, "layer %u >= n_layers %u", layer, h->cfg.n_layers);
+    if (n == 0 || n > h->cfg.max_seqs) return fail(ND_ATTN_ERR_RANGE, "%u sequences (max %u)", n, h->cfg.max_seqs);
+    const uint32_t n_kv = h->cfg.n_kv_heads, W = h->cfg.window;
+    const size_t items = (size_t)n * n_kv;
+    if (items > ND_ATTN_NOALLOC_MAX_ITEMS)
+        return fail(ND_ATTN_ERR_RANGE, "%u sequences x %u KV heads exceeds the %u (sequence, KV head) pairs "
+                    "the fixed scratch serves", n, n_kv, ND_ATTN_NOALLOC_MAX_ITEMS);
+    uint32_t jmax = 1;
+    size_t rows = 0;
+    for (uint32_t i = 0; i < n; i++) {
+        const HostSeq &s = h->seqs[i];
+        if ((uint64_t)s.pos + 1 > h->cfg.max_pos)
+            return fail(ND_ATTN_ERR_RANGE, "sequence %u at position %u >= max_pos %u", i, s.pos, h->cfg.max_pos);
+        const uint32_t j = visit_count(s.pos, s.n_sink, W);
+        jmax = std::max(jmax, j);
+        rows += (size_t)j * n_kv;
+    }
+    DeviceGuard dg(h->cfg.device);
+    char *base = nullptr;
+    int rc = noalloc_scratch(h->cfg.device, &base);
+    if (rc) return rc;
+    const size_t nq = (size_t)nda::nq_for_rep(h->rep);
+    const size_t vd = h->cfg.v_head_dim;
+    const size_t ticket_bytes = (size_t)ND_ATTN_NOALLOC_MAX_ITEMS * sizeof(int);
+    const size_t slot_bytes = nq * (vd + 2) * sizeof(float);
+    const size_t slots = (ND_ATTN_NOALLOC_SCRATCH_BYTES - ticket_bytes - 256) / slot_bytes;
+    uint32_t chunk, nsplit;
+    choose_split(h, items, jmax, rows, ND_ATTN_NOALLOC_MAX_ITEMS, slots, &chunk, &nsplit);
+    AttnParams P = base_params(h, layer);
+    P.q = q; P.k = k; P.v = v; P.gate = gate; P.out = out;
+    P.tok = nullptr;
+    P.n_tok = n;
+    P.chunk = chunk;
+    P.max_splits = nsplit;
+    P.fuse_append = 1;
+    P.counters = reinterpret_cast<int *>(base);
+    P.part_ml = reinterpret_cast<float *>(base + ticket_bytes);
+    const size_t ml_bytes = (slots * nq * 2 * sizeof(float) + 255) / 256 * 256;
+    P.part_o = reinterpret_cast<float *>(base + ticket_bytes + ml_bytes);
+    if (nsplit > 1) ND_CUDA(cudaMemsetAsync(P.counters, 0, items * sizeof(int), h->stream));
+    ND_CUDA(attend_launch(h, P, dim3((unsigned)items, nsplit, 1)));
+    h->launches++;
+    return ND_ATTN_OK;
 }
 
 // ---- prefix ------------------------------------------------------------------

@@ -31,6 +31,7 @@ DT_I8, DT_F32, DT_F16, DT_BF16 = 0, 1, 2, 3
 DT_NAMES = {"i8": DT_I8, "int8": DT_I8, "f32": DT_F32, "float32": DT_F32, "f16": DT_F16,
             "float16": DT_F16, "bf16": DT_BF16, "bfloat16": DT_BF16}
 ERR_ARG, ERR_GEOM, ERR_NOMEM, ERR_CUDA, ERR_RANGE, ERR_TIMEOUT, ERR_NOGPU = -1, -10, -12, -14, -15, -16, -17
+NOALLOC_MAX_ITEMS = 16384            # ND_ATTN_NOALLOC_MAX_ITEMS
 
 
 class NdAttnError(RuntimeError):
@@ -80,6 +81,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "nd_attn_decode": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp, vp]),
         "nd_attn_prefill": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp, vp, vp]),
         "nd_attn_decode_host": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp, vp]),
+        "nd_attn_decode_noalloc": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp]),
         "nd_attn_prefill_host": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp, vp, vp]),
         "nd_attn_prefix_save": (vp, [vp, u32]),
         "nd_attn_prefix_restore": (c_int, [vp, u32, vp]),
@@ -243,6 +245,11 @@ class Attn:
         ln, ids = _u32(lens), _u32(seq_ids)
         _check(load().nd_attn_prefill(self.h, layer, len(ln), _hptr(ids), _hptr(ln), _ptr(q), _ptr(k), _ptr(v),
                                       _ptr(gate), _ptr(out)))
+
+    def decode_noalloc(self, layer, n, q, k, v, out, gate=None) -> None:
+        """nd_attn_decode for sequences 0..n-1 with its scratch in the library's
+        fixed device array (no device allocation by the call)."""
+        _check(load().nd_attn_decode_noalloc(self.h, layer, n, _ptr(q), _ptr(k), _ptr(v), _ptr(gate), _ptr(out)))
 
     # ---- hot path (host arrays)
     def decode_host(self, layer, n, q, k, v, out, gate=None, seq_ids=None) -> None:

@@ -163,6 +163,33 @@ ND_ATTN_API int  nd_attn_prefill_host(nd_attn *h, uint32_t layer, uint32_t n, co
                           const uint32_t *len, const void *q, const void *k, const void *v,
                           const void *gate, void *out);
 
+/* ---- allocation-free decode ------------------------------------------------ */
+/* No counterpart in the reference engine (which allocates everything at
+ * nd_model_open and has no GPU scratch to place).
+ *
+ * Same work and arguments as nd_attn_decode for sequences 0..n-1 (no seq_ids),
+ * for callers that must not let the library allocate device memory after
+ * start-up: hosts that hand out all GPU memory from their own fixed budget,
+ * and serving loops where a cudaMalloc/cudaFree (which can synchronise the
+ * device or fail under fragmentation) is not allowed on the request path.
+ * The split-KV partial results and merge tickets live in one fixed array in
+ * the library's device image, ND_ATTN_NOALLOC_SCRATCH_BYTES per GPU, held
+ * from the first load of the library on that GPU until process exit; this call
+ * makes no cudaMalloc/cudaFree and no allocating library call.
+ * Limits: n * n_kv_heads <= ND_ATTN_NOALLOC_MAX_ITEMS, else ND_ATTN_ERR_RANGE
+ * and nothing is launched; when the partial results of the chosen split would
+ * not fit, fewer splits are used (never more memory).
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture.
+ * Every call on a device shares the one array: calls that can run at the same
+ * time on the GPU (two handles on different streams) race and must be
+ * serialised by the caller. The array keeps the previous call's contents; the
+ * tickets are cleared on the handle's stream at the start of every call. */
+#define ND_ATTN_NOALLOC_SCRATCH_BYTES (8u << 20)
+#define ND_ATTN_NOALLOC_MAX_ITEMS     16384u
+ND_ATTN_API int  nd_attn_decode_noalloc(nd_attn *h, uint32_t layer, uint32_t n, const void *q,
+                                        const void *k, const void *v, const void *gate, void *out);
+
 /* ---- schema-prefix KV ------------------------------------------------------ */
 /* nd_model_prefix_save (nd_model.c:1531-1541): requires a snapshot at the
  * current position; copies the live slots [0, min(snap_pos+1, window)) of
