@@ -7,6 +7,7 @@
 // changes reach the device through tiny kernels whose arguments are captured
 // by value at launch, so they stay ordered with the attention kernels on the
 // handle's stream.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -137,6 +138,12 @@ struct nd_attn {
     void *dio = nullptr;
     size_t dio_cap = 0;
     uint64_t launches = 0;
+    // tcgen05 prefill: work list of the last call (reused when the call's
+    // shape and positions repeat).
+    nda::PrefillWork *d_work = nullptr;
+    size_t work_cap = 0;
+    std::vector<uint32_t> work_key;
+    uint32_t n_work = 0;
 };
 
 namespace {
@@ -330,6 +337,114 @@ size_t act_bytes(const nd_attn *h, size_t tokens, int which) {
     }
 }
 
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2D map over rows of `inner` 16-bit elements (row stride `stride_bytes`), box
+// 64 elements x 128 rows, 128-byte swizzle, out-of-range rows read as zero.
+int make_map(CUtensorMap *m, bool bf16, const void *base, uint64_t inner, uint64_t rows, uint64_t stride_bytes) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return fail(ND_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {stride_bytes};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                          const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ND_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return ND_ATTN_OK;
+}
+
+// The tensor-core prefill serves 16-bit caches of head dim 64 in the
+// contiguous layout, with q in the cache's element type and 16-byte aligned.
+bool tc_prefill_ok(const nd_attn *h, const void *q) {
+    const nd_attn_config &c = h->cfg;
+    return (c.kv_dtype == ND_DT_BF16 || c.kv_dtype == ND_DT_F16) && c.act_dtype == c.kv_dtype &&
+           c.qk_head_dim == 64 && c.v_head_dim == 64 && c.block_size == 0 &&
+           (reinterpret_cast<uintptr_t>(q) & 15u) == 0;
+}
+
+int run_prefill_tc(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const uint32_t *len,
+                   const std::vector<uint32_t> &cu, size_t total, const void *q, const void *gate, void *out) {
+    const nd_attn_config &c = h->cfg;
+    // Work list: (sequence, query head, 128-token tile), longest KV run first.
+    std::vector<uint32_t> key;
+    key.reserve(3 * n + 2);
+    key.push_back(n);
+    key.push_back(c.n_heads);
+    for (uint32_t i = 0; i < n; i++) {
+        const uint32_t s = seq_ids ? seq_ids[i] : i;
+        key.push_back(s);
+        key.push_back(len[i]);
+        key.push_back(h->seqs[s].pos);
+    }
+    if (key != h->work_key) {
+        std::vector<std::vector<nda::PrefillWork>> by_tiles;
+        size_t count = 0;
+        for (uint32_t i = 0; i < n; i++) {
+            const uint32_t s = seq_ids ? seq_ids[i] : i, pos0 = h->seqs[s].pos;
+            for (uint32_t t0 = 0; t0 < len[i]; t0 += 128) {
+                const uint32_t rows = std::min(128u, len[i] - t0);
+                const uint32_t nkv = (pos0 + t0 + rows + 127) / 128;
+                if (by_tiles.size() <= nkv) by_tiles.resize(nkv + 1);
+                for (uint32_t hq = 0; hq < c.n_heads; hq++)
+                    by_tiles[nkv].push_back(nda::PrefillWork{s, cu[i], t0, rows, hq, pos0});
+                count += c.n_heads;
+            }
+        }
+        if (count > 0x7fffffffu) return fail(ND_ATTN_ERR_RANGE, "prefill too large");
+        std::vector<nda::PrefillWork> work;
+        work.reserve(count);
+        for (size_t t = by_tiles.size(); t-- > 0;) work.insert(work.end(), by_tiles[t].begin(), by_tiles[t].end());
+        int rc = grow(&h->d_work, &h->work_cap, work.size());
+        if (rc) return rc;
+        ND_CUDA(cudaMemcpyAsync(h->d_work, work.data(), work.size() * sizeof(nda::PrefillWork),
+                                cudaMemcpyHostToDevice, h->stream));
+        h->work_key = key;
+        h->n_work = (uint32_t)work.size();
+    }
+    const bool bf16 = c.kv_dtype == ND_DT_BF16;
+    CUtensorMap qm, km, vm;
+    CacheView cv = layer_view(h, layer);
+    int rc = make_map(&qm, bf16, q, (uint64_t)c.n_heads * 64, total, (uint64_t)c.n_heads * 64 * 2);
+    if (!rc) rc = make_map(&km, bf16, cv.k, h->k_dim, h->rows_per_layer, (uint64_t)h->k_dim * 2);
+    if (!rc) rc = make_map(&vm, bf16, cv.v, h->v_dim, h->rows_per_layer, (uint64_t)h->v_dim * 2);
+    if (rc) return rc;
+    nda::PrefillTcParams P;
+    P.work = h->d_work;
+    P.rope = h->rope;
+    P.qnorm = h->has_norm[layer] ? h->norms + (size_t)layer * 2 * c.qk_head_dim : nullptr;
+    P.gate = gate;
+    P.out = out;
+    P.act_dt = c.act_dtype;
+    P.out_dt = c.out_dtype;
+    P.n_heads = c.n_heads;
+    P.rep = h->rep;
+    P.window = c.window;
+    P.scale_log2 = 1.4426950408889634f / sqrtf((float)c.qk_head_dim);
+    P.err = h->d_err;
+    ND_CUDA(nda::prefill_tc_launch(bf16, &qm, &km, &vm, P, h->n_work, h->stream));
+    h->launches++;
+    return ND_ATTN_OK;
+}
+
 }  // namespace
 
 int nda::attend_rows_per_iter(int kv_dt, int vd) {
@@ -482,7 +597,7 @@ void nd_attn_close(nd_attn *h) {
     cudaFree(h->kc); cudaFree(h->vc); cudaFree(h->ks); cudaFree(h->vs);
     cudaFree(h->rope); cudaFree(h->norms); cudaFree(h->d_state); cudaFree(h->d_btab);
     cudaFree(h->part_o); cudaFree(h->part_ml); cudaFree(h->counters);
-    cudaFree(h->d_tok); cudaFree(h->d_u32); cudaFree(h->d_err); cudaFree(h->dio);
+    cudaFree(h->d_tok); cudaFree(h->d_u32); cudaFree(h->d_err); cudaFree(h->dio); cudaFree(h->d_work);
     if (h->pin) cudaFreeHost(h->pin);
     if (h->own) cudaStreamDestroy(h->own);
     delete h;
@@ -652,6 +767,7 @@ int nd_attn_prefill(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_
         P.k = k; P.v = v; P.tok = h->d_tok; P.n_tok = (uint32_t)total;
         ND_CUDA(append_launch(h, P));
         h->launches++;
+        if (tc_prefill_ok(h, q)) return run_prefill_tc(h, layer, n, seq_ids, len, cu, total, q, gate, out);
         return run_attend(h, layer, (uint32_t)total, h->d_tok, tpos, tseq, 0, q, k, v, gate, out);
     }
     // The ring wraps inside this call: a later token's slot can hold a position

@@ -27,4 +27,29 @@ ND_DECLARE_KV(f16)
 ND_DECLARE_KV(bf16)
 #undef ND_DECLARE_KV
 
+// ---- tcgen05 prefill (nd_prefill_tc.cu) ----------------------------------
+// One work item = 128 consecutive query tokens of one sequence for one query
+// head; the call's tokens are already appended (K1) and do not wrap the ring.
+struct PrefillWork {
+    uint32_t seq, tok_base, t0, rows, head, pos0;
+};
+
+struct PrefillTcParams {
+    const PrefillWork *work;
+    const float2 *rope;
+    const float *qnorm;
+    const void *gate;
+    void *out;
+    int act_dt, out_dt;
+    uint32_t n_heads, rep, window;
+    float scale_log2;
+    int *err;
+};
+
+size_t prefill_tc_smem_bytes();
+// qmap/kmap/vmap point to CUtensorMap objects (2D, 16-bit, box 64 x 128,
+// 128-byte swizzle) over q [tokens][n_heads*64], and one layer's K and V cache.
+cudaError_t prefill_tc_launch(bool bf16, const void *qmap, const void *kmap, const void *vmap,
+                              const PrefillTcParams &P, uint32_t n_work, cudaStream_t s);
+
 }  // namespace nda

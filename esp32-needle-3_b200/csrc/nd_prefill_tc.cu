@@ -1,0 +1,510 @@
+// nd_prefill_tc.cu - causal prefill attention on the 5th-generation tensor
+// cores (tcgen05 + TMEM + TMA) for 16-bit caches with head dim 64.
+//
+// Reference semantics: N successive decode steps of the host engine
+// (esp32/main/main.c:233-234; per step nd_model.c:2419-2483), i.e. query
+// token t at position p = pos0 + t attends to cache positions [0, p] of its
+// sequence once every token of the call has been appended (the caller runs K1
+// first and guarantees the call does not wrap the ring, so slot == position).
+//
+// One CTA = one work item = 128 consecutive query tokens of one sequence for
+// one query head h (KV head g = h / rep). 6 warps:
+//   warps 0-3  one thread per query row (= TMEM lane): RoPE(+norm) of the Q
+//              tile in shared memory, per-row online softmax on S read from
+//              TMEM, P written back to TMEM as bf16/f16 pairs, lazy O
+//              rescaling (only when a row max grows by more than 2^8), epilogue
+//   warp 4     TMA producer: Q tile once, then K/V tiles through a 3-stage ring
+//   warp 5     TMEM allocator + single-thread MMA issuer:
+//                S = Q K^T   (M=128, N=128, K=64: 4 x tcgen05.mma, A,B in smem)
+//                O += P V    (M=128, N=64, K=128: 8 x tcgen05.mma, A=P in TMEM,
+//                             B=V in smem, MN-major)
+// TMEM columns: S/P [0,128), O [128,192), Q_lo [192,224) -> 256 per CTA,
+// 2 CTAs per SM.
+// Precision: a 16-bit operand rounds a value by up to 2^-9 (bf16), which rows
+// attending to few keys, or normed rows with larger |q||k|, turn into output
+// errors above 1e-3. So both 16-bit operands the kernel makes itself carry
+// ~16 mantissa bits as a hi/lo pair: the rotated Q (Q_hi in shared memory,
+// Q_lo in TMEM; S = Q_hi K^T + Q_lo K^T) and P (P_hi/P_lo overwrite the S
+// columns they came from, per 32-key chunk 16 columns of P_hi then 16 of P_lo;
+// O += P_hi V + P_lo V). K and V are the cache's own values, exact already.
+// The next S waits for the previous PV to finish reading P from the S columns.
+// Every mbarrier wait is bounded (~2 s of SM clock); on expiry the CTA raises
+// the error word, drains what it issued (bounded), frees TMEM and returns.
+// No TMA multicast anywhere.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "nd_internal.h"
+
+namespace nda {
+namespace {
+
+constexpr int BM = 128;          // query rows per CTA (TMEM lanes)
+constexpr int BN = 128;          // keys per KV tile
+constexpr int HD = 64;           // head dim (one 128-byte swizzle row of 16-bit values)
+constexpr int STAGES = 3;
+constexpr uint32_t TILE_BYTES = BM * HD * 2;   // 16 KB, same for Q, K and V tiles
+constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t COL_S = 0, COL_O = 128, COL_QLO = 192;
+constexpr long long kTimeoutCycles = 4000000000LL;   // ~2 s at 1.9 GHz
+
+// Dynamic shared memory: Q tile, K and V stage rings (each tile 1024-byte
+// aligned for the 128-byte swizzle), then the barrier block. Laid out by hand
+// so two CTAs fit one SM (2 x 114 816 B + the per-CTA reserve <= 228 KB).
+constexpr uint32_t OFF_Q = 0;
+constexpr uint32_t OFF_K = OFF_Q + TILE_BYTES;
+constexpr uint32_t OFF_V = OFF_K + STAGES * TILE_BYTES;
+constexpr uint32_t OFF_BAR = OFF_V + STAGES * TILE_BYTES;
+
+struct Bars {
+    uint64_t q_full, q_ready, s_full, p_full, pv_done, drain;
+    uint64_t kv_full[STAGES], kv_empty[STAGES];
+    uint32_t tmem_base;
+    int abort_flag;
+};
+constexpr uint32_t SMEM_BYTES = OFF_BAR + sizeof(Bars);
+
+struct Smem {
+    uint8_t *q, *k[STAGES], *v[STAGES];
+};
+
+__device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the phase of parity `parity`. False when the CTA is
+// aborting (another role timed out) or this wait timed out (then it raises
+// the abort itself).
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag) {
+    if (mbar_test(b, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_test(b, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > kTimeoutCycles) {
+            *abort_flag = 1;
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            su32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(su32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, 128-byte swizzle, sm100 version bits.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;   // descriptor version 1
+    d |= (uint64_t)2 << 61;   // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor of kind::f16: fp32 accumulate, A/B format (0 f16, 1 bf16).
+__host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_fmt, uint32_t m, uint32_t n, uint32_t b_mn_major) {
+    return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (b_mn_major << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+                 : "memory");
+}
+
+#define ND_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
+#define ND_W8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), "r"(r[i + 5]), "r"(r[i + 6]), "r"(r[i + 7])
+
+// 32 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : ND_R8(0), ND_R8(8), ND_R8(16), ND_R8(24)
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        ND_W8(0), ND_W8(8), ND_W8(16), ND_W8(24)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+#undef ND_R8
+#undef ND_W8
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    uint32_t u;
+    if constexpr (BF16) {
+        __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
+        memcpy(&u, &t, 4);
+    } else {
+        __half2 t = __floats2half2_rn(lo, hi);
+        memcpy(&u, &t, 4);
+    }
+    return u;
+}
+template <bool BF16>
+__device__ __forceinline__ float2 unpack2(uint32_t u) {
+    if constexpr (BF16) {
+        return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+    } else {
+        __half2 t;
+        memcpy(&t, &u, 4);
+        return __half22float2(t);
+    }
+}
+
+// Offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled tile.
+__device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) { return r * 128u + ((c ^ (r & 7u)) << 4); }
+
+template <bool BF16>
+__global__ void __launch_bounds__(192, 2)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap, const PrefillTcParams P) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (su32(smem_raw) & 1023u) {          // the swizzled tiles need 1024-byte alignment
+        if (tid == 0) atomicExch(P.err, 4);
+        return;
+    }
+    Smem S;
+    S.q = smem_raw + OFF_Q;
+    for (int s = 0; s < STAGES; s++) {
+        S.k[s] = smem_raw + OFF_K + s * TILE_BYTES;
+        S.v[s] = smem_raw + OFF_V + s * TILE_BYTES;
+    }
+    Bars &B = *reinterpret_cast<Bars *>(smem_raw + OFF_BAR);
+    volatile int *abort_flag = &B.abort_flag;
+    const PrefillWork w = P.work[blockIdx.x];
+    const uint32_t g = w.head / P.rep;
+    const uint32_t nkv = (w.pos0 + w.t0 + w.rows + BN - 1) / BN;   // KV tiles this item reads
+    const uint32_t kv_row0 = w.seq * P.window;                      // cache row of position 0
+
+    if (tid == 0) {
+        mbar_init(&B.q_full, 1);
+        mbar_init(&B.q_ready, BM);
+        mbar_init(&B.s_full, 1);
+        mbar_init(&B.p_full, BM);
+        mbar_init(&B.pv_done, 1);
+        mbar_init(&B.drain, 1);
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&B.kv_full[s], 1);
+            mbar_init(&B.kv_empty[s], 1);
+        }
+        B.abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 5) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&B.tmem_base)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tbase = B.tmem_base;
+
+    if (warp == 4) {
+        // ---------------- TMA producer
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&kmap) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&vmap) : "memory");
+            mbar_expect_tx(&B.q_full, TILE_BYTES);
+            tma_load_2d(S.q, &qmap, (int)(w.head * HD), (int)(w.tok_base + w.t0), &B.q_full);
+            uint32_t issued = 0;
+            for (uint32_t j = 0; j < nkv; j++) {
+                const uint32_t st = j % STAGES;
+                if (j >= STAGES && !mbar_wait(&B.kv_empty[st], ((j / STAGES) - 1) & 1, abort_flag)) break;
+                mbar_expect_tx(&B.kv_full[st], 2 * TILE_BYTES);
+                tma_load_2d(S.k[st], &kmap, (int)(g * HD), (int)(kv_row0 + j * BN), &B.kv_full[st]);
+                tma_load_2d(S.v[st], &vmap, (int)(g * HD), (int)(kv_row0 + j * BN), &B.kv_full[st]);
+                issued = j + 1;
+            }
+            if (*abort_flag) {
+                // Let the copies this thread issued land before the CTA goes
+                // away (bounded: the Q tile and the newest K/V tile).
+                const long long t0 = clock64();
+                while (!mbar_test(&B.q_full, 0) && clock64() - t0 < kTimeoutCycles) {
+                }
+                if (issued) {
+                    const uint32_t j = issued - 1;
+                    const long long t1 = clock64();
+                    while (!mbar_test(&B.kv_full[j % STAGES], (j / STAGES) & 1) && clock64() - t1 < kTimeoutCycles) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 5) {
+        // ---------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t fmt = BF16 ? 1u : 0u;
+            constexpr uint32_t id_s = idesc_f16(fmt, BM, BN, 0);
+            constexpr uint32_t id_o = idesc_f16(fmt, BM, HD, 1);
+            const uint32_t q_addr = su32(S.q);
+            bool ok = mbar_wait(&B.q_ready, 0, abort_flag);
+            uint32_t issued_any = 0;
+            for (uint32_t j = 0; ok && j < nkv; j++) {
+                const uint32_t st = j % STAGES;
+                if (!mbar_wait(&B.kv_full[st], (j / STAGES) & 1, abort_flag)) break;
+                // S_j lands where PV_{j-1} reads P_hi/P_lo.
+                if (j > 0 && !mbar_wait(&B.pv_done, (j - 1) & 1, abort_flag)) break;
+                fence_after();
+                const uint32_t k_addr = su32(S.k[st]), v_addr = su32(S.v[st]);
+#pragma unroll
+                for (uint32_t kk = 0; kk < HD / 16; kk++) {
+                    const uint64_t kd = sdesc(k_addr + kk * 32, 16, 1024);
+                    umma_ss(tbase + COL_S, sdesc(q_addr + kk * 32, 16, 1024), kd, id_s, kk > 0);
+                    umma_ts(tbase + COL_S, tbase + COL_QLO + kk * 8, kd, id_s, 1u);
+                }
+                umma_commit(&B.s_full);
+                issued_any = 1;
+                if (!mbar_wait(&B.p_full, j & 1, abort_flag)) break;
+                fence_after();
+#pragma unroll
+                for (uint32_t kk = 0; kk < BN / 16; kk++) {
+                    const uint64_t vd = sdesc(v_addr + kk * 2048, TILE_BYTES, 1024);
+                    const uint32_t pc = tbase + COL_S + 32 * (kk / 2) + 8 * (kk % 2);
+                    umma_ts(tbase + COL_O, pc, vd, id_o, (j > 0 || kk > 0) ? 1u : 0u);
+                    umma_ts(tbase + COL_O, pc + 16, vd, id_o, 1u);
+                }
+                // Free the stage only where the producer will wait for it, so no
+                // arrive is still pending when the CTA exits.
+                if (j + STAGES < nkv) umma_commit(&B.kv_empty[st]);
+                umma_commit(&B.pv_done);
+            }
+            if (*abort_flag && issued_any) {
+                umma_commit(&B.drain);
+                const long long t0 = clock64();
+                while (!mbar_test(&B.drain, 0) && clock64() - t0 < kTimeoutCycles) {
+                }
+            }
+        }
+    } else {
+        // ---------------- softmax / correction / epilogue: thread = query row
+        const uint32_t r = tid;
+        const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
+        const uint32_t qpos = w.pos0 + w.t0 + r;                  // this row's position
+        const bool row_valid = r < w.rows;
+        bool ok = __all_sync(0xffffffffu, mbar_wait(&B.q_full, 0, abort_flag));
+        if (ok) {
+            // RoPE (after the optional per-head norm) of this row, in place.
+            const uint32_t pos_tab = row_valid ? qpos : w.pos0 + w.t0;
+            const float2 *cs = P.rope + (size_t)pos_tab * (HD / 2);
+            uint8_t *row = S.q;
+            float x[HD];
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const uint4 u = *reinterpret_cast<const uint4 *>(row + swz(r, c));
+                const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float2 f = unpack2<BF16>(uu[e]);
+                    x[c * 8 + 2 * e] = f.x;
+                    x[c * 8 + 2 * e + 1] = f.y;
+                }
+            }
+            float inv = 1.0f;
+            if (P.qnorm) {
+                float ss = 0.0f;
+#pragma unroll
+                for (int i = 0; i < HD; i++) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
+                inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)HD), 1e-6f)));
+            }
+#pragma unroll
+            for (int i = 0; i < HD / 2; i++) {
+                float a = x[i], b = x[i + HD / 2];
+                if (P.qnorm) {
+                    a = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, P.qnorm[i]), a), inv);
+                    b = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, P.qnorm[i + HD / 2]), b), inv);
+                }
+                const float2 t = cs[i];
+                x[i] = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(b, t.y));
+                x[i + HD / 2] = __fadd_rn(__fmul_rn(b, t.x), __fmul_rn(a, t.y));
+            }
+            uint32_t lo[32];
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                uint32_t hw[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float a = x[c * 8 + 2 * e], b = x[c * 8 + 2 * e + 1];
+                    hw[e] = pack2<BF16>(a, b);
+                    const float2 hf = unpack2<BF16>(hw[e]);
+                    lo[c * 4 + e] = pack2<BF16>(a - hf.x, b - hf.y);
+                }
+                *reinterpret_cast<uint4 *>(row + swz(r, c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            }
+            tmem_st32(lane_addr + COL_QLO, lo);
+            tmem_wait_st();
+            fence_before();
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(&B.q_ready);
+        }
+        const float c = P.scale_log2;
+        float m = -INFINITY, l = 0.0f;
+        for (uint32_t j = 0; ok && j < nkv; j++) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&B.s_full, j & 1, abort_flag))) {
+                ok = false;
+                break;
+            }
+            fence_after();
+            const int lim = (int)qpos - (int)(j * BN);   // keys [0, lim] of this tile are visible
+            float tmax = -INFINITY;
+#pragma unroll
+            for (int c4 = 0; c4 < BN / 32; c4++) {
+                uint32_t sv[32];
+                tmem_ld32(lane_addr + COL_S + c4 * 32, sv);
+#pragma unroll
+                for (int e = 0; e < 32; e++) {
+                    const float s = (c4 * 32 + e <= lim) ? __uint_as_float(sv[e]) : -INFINITY;
+                    tmax = fmaxf(tmax, s);
+                }
+            }
+            tmax *= c;
+            const bool grow = (j == 0) || (tmax > m + 8.0f);
+            if (j > 0) {
+                // PV of the previous tile must be done before O or P is touched.
+                if (!__all_sync(0xffffffffu, mbar_wait(&B.pv_done, (j - 1) & 1, abort_flag))) {
+                    ok = false;
+                    break;
+                }
+                fence_after();
+                // TMEM loads/stores are warp-wide: rescale when any row of the
+                // warp needs it, with a factor of 1 for the others.
+                if (__any_sync(0xffffffffu, grow)) {
+                    const float alpha = grow ? ex2(m - tmax) : 1.0f;
+                    l *= alpha;
+#pragma unroll
+                    for (int h2 = 0; h2 < HD / 32; h2++) {
+                        uint32_t ov[32];
+                        tmem_ld32(lane_addr + COL_O + h2 * 32, ov);
+#pragma unroll
+                        for (int e = 0; e < 32; e++) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+                        tmem_st32(lane_addr + COL_O + h2 * 32, ov);
+                    }
+                }
+            }
+            if (grow) m = tmax;
+#pragma unroll
+            for (int c4 = 0; c4 < BN / 32; c4++) {
+                uint32_t sv[32];
+                tmem_ld32(lane_addr + COL_S + c4 * 32, sv);
+                {
+                    uint32_t pk[32];
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2) {
+                        const float s0 = (c4 * 32 + e <= lim) ? __uint_as_float(sv[e]) : -INFINITY;
+                        const float s1 = (c4 * 32 + e + 1 <= lim) ? __uint_as_float(sv[e + 1]) : -INFINITY;
+                        const float p0 = ex2(fmaf(s0, c, -m)), p1 = ex2(fmaf(s1, c, -m));
+                        l += p0 + p1;
+                        const uint32_t hi = pack2<BF16>(p0, p1);
+                        const float2 hf = unpack2<BF16>(hi);
+                        pk[e / 2] = hi;
+                        pk[16 + e / 2] = pack2<BF16>(p0 - hf.x, p1 - hf.y);
+                    }
+                    tmem_st32(lane_addr + COL_S + c4 * 32, pk);
+                }
+            }
+            tmem_wait_st();
+            fence_before();
+            mbar_arrive(&B.p_full);
+        }
+        if (ok && __all_sync(0xffffffffu, mbar_wait(&B.pv_done, (nkv - 1) & 1, abort_flag))) {
+            fence_after();
+            const float inv_l = 1.0f / l;
+            const size_t obase = ((size_t)(w.tok_base + w.t0 + r) * P.n_heads + w.head) * HD;
+#pragma unroll
+            for (int h2 = 0; h2 < HD / 32; h2++) {
+                uint32_t ov[32];
+                tmem_ld32(lane_addr + COL_O + h2 * 32, ov);
+                if (row_valid) {
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        float val = __uint_as_float(ov[e]) * inv_l;
+                        if (P.gate)
+                            val *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, obase + h2 * 32 + e) *
+                                                         1.4426950408889634f));
+                        act_store(P.out, P.out_dt, obase + h2 * 32 + e, val);
+                    }
+                }
+            }
+        }
+    }
+
+    fence_before();
+    __syncthreads();
+    if (tid == 0 && B.abort_flag) atomicExch(P.err, 3);
+    if (warp == 5) {
+        fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TMEM_COLS));
+    }
+}
+
+}  // namespace
+
+size_t prefill_tc_smem_bytes() { return SMEM_BYTES; }
+
+cudaError_t prefill_tc_launch(bool bf16, const void *qmap, const void *kmap, const void *vmap,
+                              const PrefillTcParams &P, uint32_t n_work, cudaStream_t s) {
+    const CUtensorMap &q = *static_cast<const CUtensorMap *>(qmap);
+    const CUtensorMap &k = *static_cast<const CUtensorMap *>(kmap);
+    const CUtensorMap &v = *static_cast<const CUtensorMap *>(vmap);
+    const size_t smem = prefill_tc_smem_bytes();
+    if (bf16) {
+        cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+        prefill_tc_kernel<true><<<n_work, 192, smem, s>>>(q, k, v, P);
+    } else {
+        cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+        prefill_tc_kernel<false><<<n_work, 192, smem, s>>>(q, k, v, P);
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace nda

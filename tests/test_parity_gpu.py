@@ -405,3 +405,21 @@ def test_errors_are_reported_not_hidden():
     with pytest.raises(ndattn.NdAttnError):
         a.reset(5)
     a.close()
+
+
+@pytest.mark.parametrize("dt", [O.BF16, O.F16])
+@pytest.mark.parametrize("norm,gate", [(False, False), (True, True)])
+def test_tensor_core_prefill_ragged(dt, norm, gate):
+    """The tcgen05 prefill (16-bit caches, head dim 64): ragged lengths around
+    the 128-token tile (1, 127, 128, 129, 300), a second call starting after a
+    cached prefix (pos0 > 0, diagonal tiles not aligned), GQA 4:1."""
+    worst, a, seqs = run_session(dt, dt, 8, 2, 64, 64, 640, 1, [1, 127, 128, 129, 230][:5], seed=21, n_seqs=1,
+                                 norm=norm, gate=gate)
+    assert worst <= TOL
+    check_caches(a, seqs, dt, 1, 640)
+    a.close()
+    worst, a, seqs = run_session(dt, dt, 8, 2, 64, 64, 1024, 2, [300, 200], seed=22, n_seqs=3, norm=norm,
+                                 gate=gate, sink_after=1)
+    assert worst <= TOL
+    check_caches(a, seqs, dt, 2, 1024)
+    a.close()
