@@ -1,19 +1,27 @@
 """Benchmark of the Needle attention hot path on B200.
 
-Default workload (the one the metric is quoted on): 8-layer
-decode attention, 64 independent sequences per GPU, cached contexts
-U[256, 2048] (seed 1), 8 q / 8 kv heads x 64, fp16 KV N(0,1)*0.5, q N(0,1),
-RoPE at each step's absolute position. A step = one new token for every
-sequence through all 8 layers (RoPE + KV append + split-KV attention) plus the
-position advance. Multi-GPU: sequences are batch-sharded (each rank owns its
-own 64 sequences and caches, no collective on the data path; weak scaling),
-timed on the device, max over ranks.
+Headline workload (the config the metric is quoted on):
+8-layer decode attention, 64 independent sequences per GPU, cached contexts
+U[256, 2048] (seed 1 + rank), 8 q / 8 kv heads x 64, fp16 KV N(0,1)*0.5,
+q N(0,1), RoPE at each step's absolute position. A step = one new token for
+every sequence through all 8 layers (RoPE + KV append + split-KV attention)
+plus the position advance.
+
+Second workload in the same line (`prefill`): causal
+prefill of 512 sequences x 1024 tokens through 8 layers, 16 q / 4 kv heads x
+64, bf16 in / fp32 accumulate, q/k/v N(0,1)*0.5 (seed 2 + rank), K/V written
+to a contiguous per-layer cache. A step = the whole batch through 8 layers
+(K1 append + tcgen05 prefill per layer).
+
+Multi-GPU: sequences are batch-sharded (each rank owns its own sequences and
+caches, no collective on the data path; weak scaling), timed on the device
+with CUDA events, max over ranks.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 Prints one JSON line. `--impl reference` times the reference engine's own C
 attention (int8 KV, its only format) on the host cores on a bounded sample of
-the same workload.
+the same workloads.
 """
 from __future__ import annotations
 
@@ -21,7 +29,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -29,21 +36,25 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "esp32-needle-3_b200"))
 
+# config 2 (decode)
 H = HKV = 8
 QK = VD = 64
-LAYERS = 8        # config 2; --layers shrinks it only for profiler captures
+LAYERS = 8
 BATCH = 64
 CTX_LO, CTX_HI = 256, 2048
 METRIC = "decode tok/s (config 2: 8-layer decode attention, B=64/GPU, ctx U[256,2048], 8x64 MHA, fp16 KV)"
+# config 3 (prefill)
+P_SEQS, P_TOK, P_H, P_HKV, P_HD = 512, 1024, 16, 4, 64
+P_METRIC = "prefill tok/s (config 3: 512 seq x 1024 tok x 8 layers, GQA 16/4, hd 64, bf16)"
 
 
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
+        return p, "measured"
     except Exception:
-        return 6650.0, "fallback"
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
 def ctx_lengths(rank: int):
@@ -92,10 +103,10 @@ class Clocks:
 
     def _poll(self):
         nv = self.nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
         while not self.stop:
             try:
-                get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-                    nv.nvmlDeviceGetCurrentClocksThrottleReasons
                 self.rows.append((nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM), get_reasons(self.h)))
             except Exception:
                 pass
@@ -114,13 +125,19 @@ class Clocks:
                 "source": "nvml, ~2 ms period, during the timed region"}
 
 
-def cpu_reference(target_s: float, rank: int, max_steps: int = 128):
-    """The reference engine's own attention (oracle/_ref, int8 KV) on the host
-    cores: each thread runs whole sequences (contexts cached, then decode steps
-    through 8 layers). One calibration step sizes the sample to ~target_s of
-    wall time. Returns (tok/s, cores, sample text)."""
+# ------------------------------------------------------------ CPU reference
+def _oracle():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import ndoracle as O
+    return O
+
+
+def cpu_decode(target_s: float, rank: int, max_steps: int = 128):
+    """The reference engine's own attention (oracle/_ref, int8 KV) on all host
+    cores for config 2: each thread runs whole sequences (contexts cached, then
+    decode steps through 8 layers); one calibration step sizes the sample to
+    ~target_s. Returns (tok/s, threads, sample text)."""
+    O = _oracle()
     ctx = ctx_lengths(rank)
     threads = os.cpu_count() or 1
     window = CTX_HI + max_steps + 4
@@ -129,44 +146,50 @@ def cpu_reference(target_s: float, rank: int, max_steps: int = 128):
         raise RuntimeError(f"reference decode bench failed ({t1})")
     steps = int(max(1, min(max_steps, target_s / max(t1, 1e-6))))
     secs = O.ref_decode_bench(H, HKV, QK, VD, window, ctx, steps, LAYERS, 10000.0, threads)
-    toks = len(ctx) * steps
     sample = (f"{len(ctx)} sequences x {steps} decode steps x {LAYERS} layers of config 2, reference C "
               f"attention (engine/src/nd_model.c attn_heads + int8 KV store), {threads} threads")
-    return toks / secs, threads, sample
+    return len(ctx) * steps / secs, threads, sample
+
+
+def cpu_prefill(target_s: float):
+    """Config 3 on the host cores the reference's way (N successive single-token
+    steps, int8 KV): a whole-sequence sample of `threads` sequences x 1 layer,
+    grown until ~target_s, scaled to 8 layers (extrapolated)."""
+    O = _oracle()
+    threads = os.cpu_count() or 1
+    n = threads
+    secs = O.ref_prefill_bench(P_H, P_HKV, P_HD, P_HD, P_TOK, n, P_TOK, 1, 10000.0, threads)
+    while secs < target_s / 2 and n < P_SEQS:
+        n = min(P_SEQS, n * 2)
+        secs = O.ref_prefill_bench(P_H, P_HKV, P_HD, P_HD, P_TOK, n, P_TOK, 1, 10000.0, threads)
+    tok_s = n * P_TOK / (secs * LAYERS)
+    sample = (f"{n} sequences x {P_TOK} tokens x 1 layer of config 3, reference C attention one token at a "
+              f"time (int8 KV), {threads} threads; 8 layers extrapolated linearly")
+    return tok_s, threads, sample
 
 
 def run_reference(args):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    if int(os.environ.get("RANK", "0")) != 0:
         return
-    v, cores, sample = cpu_reference(10.0, 0)
+    v, cores, sample = cpu_decode(10.0, 0)
     steps = int(sample.split(" x ")[1].split()[0])
+    pv, pcores, psample = cpu_prefill(10.0)
     line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": steps,
             "warmup": 1, "ms_per_step": 1e3 * BATCH / v, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32 math over int8 KV", "data": "synthetic",
-            "impl": "reference",
+            "vs_baseline": None, "dtype": "f32 math over int8 KV", "data": "synthetic", "impl": "reference",
             "config": {"workload": "config2-decode", "layers": LAYERS, "batch": BATCH,
                        "ctx": f"U[{CTX_LO},{CTX_HI}] seed 1", "heads": "8x64 MHA", "kv_dtype": "int8 (reference)"},
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference", "sample": sample},
-            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "prefill": {"metric": P_METRIC, "value": pv, "unit": "tok/s", "cores": pcores, "sample": psample}}
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args):
-    import numpy as np
+# ------------------------------------------------------------ GPU: decode
+def run_decode(args, world, rank, local, dist):
     import torch
-    import torch.distributed as dist
 
     import ndattn
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
 
     K, Wm = args.steps, args.warmup
     ctx = ctx_lengths(rank)
@@ -176,8 +199,7 @@ def run_ours(args):
     stream = torch.cuda.ExternalStream(a.stream)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(1000 + rank)
-    # Cached contexts: K/V ~ N(0,1)*0.5 written straight into the cache.
-    for l in range(LAYERS):
+    for l in range(LAYERS):                       # cached contexts, straight into the cache
         for s in range(BATCH):
             n = int(ctx[s])
             kk = (torch.randn((n, HKV * QK), generator=gen, device="cuda") * 0.5).half()
@@ -226,13 +248,12 @@ def run_ours(args):
     ms = t0.elapsed_time(t1)
     kern_ms = [kev[i][l][0].elapsed_time(kev[i][l][1]) for i in range(K) for l in range(LAYERS)]
     # Algorithmic bytes of one attend launch: every visited K and V row once
-    # (positions 0..pos inclusive of the new token) plus q/k/v in and out.
+    # (positions 0..pos, the new token included) plus q/k/v in and out.
     pos0 = ctx + Wm
     kv_bytes = sum(float((pos0 + i + 1).sum()) * HKV * (QK + VD) * 2 for i in range(K)) / K
-    io_bytes = BATCH * (H * QK + HKV * QK + HKV * VD + H * VD) * 2
-    bytes_per_launch = kv_bytes + io_bytes
+    bytes_per_launch = kv_bytes + BATCH * (H * QK + HKV * QK + HKV * VD + H * VD) * 2
     avg_kern_s = statistics.mean(kern_ms) / 1e3
-    hbm_peak, peak_kind = peaks()
+    pk, peak_kind = peaks()
     achieved = bytes_per_launch / avg_kern_s / 1e9
 
     # End to end through the C ABI with host buffers (pinned), copies inside.
@@ -255,38 +276,144 @@ def run_ours(args):
     e1.record(stream)
     a.sync()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    a.close()
 
     times = torch.tensor([ms, e2e_ms], device="cuda", dtype=torch.float64)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     ms, e2e_ms = float(times[0]), float(times[1])
-    value = BATCH * world * K / (ms / 1e3)
-    e2e = BATCH * world / (e2e_ms / 1e3)
+    return {
+        "value": BATCH * world * K / (ms / 1e3), "ms_per_step": ms / K, "steps": K, "warmup": Wm,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_kind": f"{peak_kind} copy bandwidth",
+                     "kernel": "attend_kernel<64,64,half,1> (RoPE + KV append + split-KV + combine)",
+                     "avg_launch_us": avg_kern_s * 1e6, "bytes_per_launch": bytes_per_launch},
+        "e2e": {"value": BATCH * world / (e2e_ms / 1e3), "unit": "tok/s",
+                "h2d_bytes_per_step": int(LAYERS * BATCH * (H * QK + HKV * QK + HKV * VD) * 2),
+                "d2h_bytes_per_step": int(LAYERS * BATCH * H * VD * 2)},
+        "gpu_launches": int(launches), "clocks": clk.summary(),
+    }
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        v_cpu, cores, sample = cpu_reference(10.0, 0)
-        cpu = {"value": v_cpu, "unit": "tok/s", "cores": cores, "kind": "reference", "sample": sample}
-    if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": Wm,
-                "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "f16", "data": "synthetic",
-                "config": {"workload": "config2-decode", "layers": LAYERS, "batch_per_gpu": BATCH,
-                           "ctx": f"U[{CTX_LO},{CTX_HI}] seed 1+rank", "heads": "8x64 MHA", "kv_dtype": "fp16",
-                           "l2": "inputs larger than L2 (~1.3 GB of KV read per step)",
-                           "parallelism": f"batch-sharded x{world} (no collective)"},
-                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                             "frac": achieved / hbm_peak, "traffic": None, "peak_kind": peak_kind,
-                             "kernel": "attend_kernel<64,64,half,1> (RoPE+append+split-KV+combine)",
-                             "avg_launch_us": avg_kern_s * 1e6, "bytes_per_launch": bytes_per_launch},
-                "cpu_baseline": cpu,
-                "e2e": {"value": e2e, "unit": "tok/s",
-                        "h2d_bytes_per_step": int(LAYERS * BATCH * (H * QK + HKV * QK + HKV * VD) * 2),
-                        "d2h_bytes_per_step": int(LAYERS * BATCH * H * VD * 2)},
-                "gpu_launches": int(launches),
-                "clocks": clk.summary()}
-        print(json.dumps(line), flush=True)
+
+# ------------------------------------------------------------ GPU: prefill
+def run_prefill(args, world, rank, local, dist, seqs=P_SEQS):
+    import torch
+
+    import ndattn
+
+    K, Wm = args.prefill_steps, args.warmup
+    T = seqs * P_TOK
+    a = ndattn.Attn(n_layers=LAYERS, n_heads=P_H, n_kv_heads=P_HKV, qk_head_dim=P_HD, v_head_dim=P_HD,
+                    window=P_TOK, max_seqs=seqs, kv_dtype="bf16", act_dtype="bf16", out_dtype="bf16",
+                    device=local)
+    stream = torch.cuda.ExternalStream(a.stream)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(2 + rank)
+    q = (torch.randn((LAYERS, T, P_H * P_HD), generator=gen, device="cuda") * 0.5).bfloat16()
+    k = (torch.randn((LAYERS, T, P_HKV * P_HD), generator=gen, device="cuda") * 0.5).bfloat16()
+    v = (torch.randn((LAYERS, T, P_HKV * P_HD), generator=gen, device="cuda") * 0.5).bfloat16()
+    out = torch.empty((T, P_H * P_HD), dtype=torch.bfloat16, device="cuda")
+    lens = [P_TOK] * seqs
+    torch.cuda.synchronize()
+
+    def step(ev=None):
+        # Every sequence starts at position 0: the prefill call does not move
+        # positions, so each step re-prefills the same tokens.
+        for l in range(LAYERS):
+            if ev is not None:
+                ev[l][0].record(stream)
+            a.prefill(l, lens, q[l], k[l], v[l], out)
+            if ev is not None:
+                ev[l][1].record(stream)
+
+    for _ in range(Wm):
+        step()
+    a.sync()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = a.launches
+    kev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(LAYERS)] for _ in range(K)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        torch.cuda.nvtx.range_push("timed_prefill")
+        t0.record(stream)
+        for i in range(K):
+            step(kev[i])
+        t1.record(stream)
+        torch.cuda.nvtx.range_pop()
+        a.sync()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+    launches = a.launches - launches0
+    ms = t0.elapsed_time(t1)
+    layer_ms = statistics.mean(kev[i][l][0].elapsed_time(kev[i][l][1]) for i in range(K) for l in range(LAYERS))
     a.close()
+    times = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms = float(times[0])
+    # Causal FLOPs of one layer call: QK^T and PV over keys 0..t for every token
+    # (4 * hd * Hq * N(N+1)/2 per sequence).
+    flops_layer = 4.0 * P_HD * P_H * P_TOK * (P_TOK + 1) / 2 * seqs
+    pk, peak_kind = peaks()
+    achieved = flops_layer / (layer_ms / 1e3) / 1e12
+    peak = pk["bf16_tflops_sustained"]
+    return {
+        "metric": P_METRIC, "value": T * world * K / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms / K,
+        "steps": K, "warmup": Wm, "dtype": "bf16",
+        "config": {"workload": "config3-prefill", "seqs_per_gpu": seqs, "tokens": P_TOK, "layers": LAYERS,
+                   "heads": "16 q / 4 kv x 64", "l2": "inputs larger than L2 (1.6 GB of q/k/v per layer)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "peak_kind": f"{peak_kind} cuBLAS bf16, sustained (kernel runs inside a long step)",
+                     "unit_of_work": "one layer call = K1 append + tcgen05 prefill, causal FLOPs",
+                     "avg_layer_ms": layer_ms, "flops_per_layer": flops_layer},
+        "gpu_launches": int(launches), "clocks": clk.summary(),
+    }
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    if args.workload == "prefill":
+        pre = run_prefill(args, world, rank, local, dist, seqs=args.seqs or P_SEQS)
+        if rank == 0:
+            print(json.dumps(dict(pre, n_gpus=world, higher_is_better=True, scaling="weak", vs_baseline=None,
+                                  data="synthetic")), flush=True)
+    else:
+        dec = run_decode(args, world, rank, local, dist)
+        pre = run_prefill(args, world, rank, local, dist) if args.prefill_steps > 0 else None
+        cpu = None
+        if rank == 0 and world == 1 and not args.no_cpu:
+            v_cpu, cores, sample = cpu_decode(10.0, 0)
+            cpu = {"value": v_cpu, "unit": "tok/s", "cores": cores, "kind": "reference", "sample": sample}
+            if pre is not None:
+                pv, pcores, psample = cpu_prefill(10.0)
+                pre["cpu_baseline"] = {"value": pv, "unit": "tok/s", "cores": pcores, "kind": "reference",
+                                       "sample": psample}
+        if rank == 0:
+            line = {"metric": METRIC, "value": dec["value"], "unit": "tok/s", "n_gpus": world, "steps": dec["steps"],
+                    "warmup": dec["warmup"], "ms_per_step": dec["ms_per_step"], "higher_is_better": True,
+                    "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                    "config": {"workload": "config2-decode", "layers": LAYERS, "batch_per_gpu": BATCH,
+                               "ctx": f"U[{CTX_LO},{CTX_HI}] seed 1+rank", "heads": "8x64 MHA", "kv_dtype": "fp16",
+                               "l2": "inputs larger than L2 (~1.3 GB of KV read per step)",
+                               "parallelism": f"batch-sharded x{world} (no collective)"},
+                    "roofline": dec["roofline"], "cpu_baseline": cpu, "e2e": dec["e2e"],
+                    "gpu_launches": dec["gpu_launches"] + (pre["gpu_launches"] if pre else 0),
+                    "clocks": dec["clocks"], "prefill": pre}
+            print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
@@ -298,10 +425,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--layers", type=int, default=LAYERS, help="profiling only: fewer layers than config 2")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                    help="decode: config 2 line with the config 3 prefill inside; prefill: config 3 alone")
+    ap.add_argument("--prefill-steps", type=int, default=5, help="timed config-3 steps (0 skips the prefill leg)")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="profiling only: fewer layers than the config")
+    ap.add_argument("--seqs", type=int, default=0, help="profiling only: fewer config-3 sequences")
     args = ap.parse_args()
-    if args.warmup < 3 and args.impl == "ours":
-        args.warmup = 3
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     globals()["LAYERS"] = args.layers
     if args.impl == "reference":
         run_reference(args)

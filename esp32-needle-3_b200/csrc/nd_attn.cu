@@ -130,6 +130,8 @@ struct nd_attn {
     size_t counter_cap = 0;    // items with a ticket counter
     TokMeta *d_tok = nullptr;
     size_t tok_cap = 0;
+    nda::SeqSpan *d_spans = nullptr;
+    size_t spans_cap = 0;
     uint32_t *d_u32 = nullptr;
     size_t u32_cap = 0;
     int *d_err = nullptr;
@@ -297,25 +299,21 @@ int upload_tok(nd_attn *h, const std::vector<TokMeta> &tok) {
     return ND_ATTN_OK;
 }
 
-// One attend launch over `tok` (nullptr = identity over n sequences).
-int run_attend(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok,
-               const std::vector<uint32_t> &tok_pos, const std::vector<uint32_t> &tok_seq,
-               int fuse_append, const void *q, const void *k, const void *v, const void *gate, void *out) {
-    const uint32_t n_kv = h->cfg.n_kv_heads, W = h->cfg.window;
-    uint32_t jmax = 1;
-    size_t rows = 0;
-    for (uint32_t t = 0; t < ntok; t++) {
-        const uint32_t j = visit_count(tok_pos[t], h->seqs[tok_seq[t]].n_sink, W);
-        jmax = std::max(jmax, j);
-        rows += (size_t)j * n_kv;
-    }
+// One attend launch over `ntok` query tokens mapped by d_tok, or d_spans, or
+// identity; jmax / rows: longest visit run and total visited rows (x KV heads).
+int run_attend(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, const nda::SeqSpan *d_spans,
+               uint32_t n_spans, uint32_t jmax, size_t rows, int fuse_append, const void *q, const void *k,
+               const void *v, const void *gate, void *out) {
+    const uint32_t n_kv = h->cfg.n_kv_heads;
     const size_t items = (size_t)ntok * n_kv;
     uint32_t chunk, nsplit;
-    choose_split(h, items, jmax, rows, h->counter_cap, h->part_slots, &chunk, &nsplit);
+    choose_split(h, items, std::max(jmax, 1u), rows, h->counter_cap, h->part_slots, &chunk, &nsplit);
     if (items > 0x7fffffffu || nsplit > 65535u) return fail(ND_ATTN_ERR_RANGE, "launch too large");
     AttnParams P = base_params(h, layer);
     P.q = q; P.k = k; P.v = v; P.gate = gate; P.out = out;
     P.tok = d_tok;
+    P.spans = d_spans;
+    P.n_spans = n_spans;
     P.n_tok = ntok;
     P.chunk = chunk;
     P.max_splits = nsplit;
@@ -356,13 +354,14 @@ EncodeTiledFn encode_tiled() {
 }
 
 // 2D map over rows of `inner` 16-bit elements (row stride `stride_bytes`), box
-// 64 elements x 128 rows, 128-byte swizzle, out-of-range rows read as zero.
-int make_map(CUtensorMap *m, bool bf16, const void *base, uint64_t inner, uint64_t rows, uint64_t stride_bytes) {
+// 64 elements x box_rows rows, 128-byte swizzle, out-of-range rows read as zero.
+int make_map(CUtensorMap *m, bool bf16, const void *base, uint64_t inner, uint64_t rows, uint64_t stride_bytes,
+             uint32_t box_rows) {
     EncodeTiledFn fn = encode_tiled();
     if (!fn) return fail(ND_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     const cuuint64_t dims[2] = {inner, rows};
     const cuuint64_t strides[1] = {stride_bytes};
-    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t box[2] = {64, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                           const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -402,7 +401,7 @@ int run_prefill_tc(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
             const uint32_t s = seq_ids ? seq_ids[i] : i, pos0 = h->seqs[s].pos;
             for (uint32_t t0 = 0; t0 < len[i]; t0 += 128) {
                 const uint32_t rows = std::min(128u, len[i] - t0);
-                const uint32_t nkv = (pos0 + t0 + rows + 127) / 128;
+                const uint32_t nkv = (pos0 + t0 + rows + 63) / 64;   // 64-key tiles the item reads
                 if (by_tiles.size() <= nkv) by_tiles.resize(nkv + 1);
                 for (uint32_t hq = 0; hq < c.n_heads; hq++)
                     by_tiles[nkv].push_back(nda::PrefillWork{s, cu[i], t0, rows, hq, pos0});
@@ -423,9 +422,9 @@ int run_prefill_tc(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
     const bool bf16 = c.kv_dtype == ND_DT_BF16;
     CUtensorMap qm, km, vm;
     CacheView cv = layer_view(h, layer);
-    int rc = make_map(&qm, bf16, q, (uint64_t)c.n_heads * 64, total, (uint64_t)c.n_heads * 64 * 2);
-    if (!rc) rc = make_map(&km, bf16, cv.k, h->k_dim, h->rows_per_layer, (uint64_t)h->k_dim * 2);
-    if (!rc) rc = make_map(&vm, bf16, cv.v, h->v_dim, h->rows_per_layer, (uint64_t)h->v_dim * 2);
+    int rc = make_map(&qm, bf16, q, (uint64_t)c.n_heads * 64, total, (uint64_t)c.n_heads * 64 * 2, 128);
+    if (!rc) rc = make_map(&km, bf16, cv.k, h->k_dim, h->rows_per_layer, (uint64_t)h->k_dim * 2, 64);
+    if (!rc) rc = make_map(&vm, bf16, cv.v, h->v_dim, h->rows_per_layer, (uint64_t)h->v_dim * 2, 64);
     if (rc) return rc;
     nda::PrefillTcParams P;
     P.work = h->d_work;
@@ -597,7 +596,7 @@ void nd_attn_close(nd_attn *h) {
     cudaFree(h->kc); cudaFree(h->vc); cudaFree(h->ks); cudaFree(h->vs);
     cudaFree(h->rope); cudaFree(h->norms); cudaFree(h->d_state); cudaFree(h->d_btab);
     cudaFree(h->part_o); cudaFree(h->part_ml); cudaFree(h->counters);
-    cudaFree(h->d_tok); cudaFree(h->d_u32); cudaFree(h->d_err); cudaFree(h->dio); cudaFree(h->d_work);
+    cudaFree(h->d_tok); cudaFree(h->d_u32); cudaFree(h->d_err); cudaFree(h->dio); cudaFree(h->d_work); cudaFree(h->d_spans);
     if (h->pin) cudaFreeHost(h->pin);
     if (h->own) cudaStreamDestroy(h->own);
     delete h;
@@ -710,21 +709,23 @@ int nd_attn_decode(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
     if (rc) return rc;
     if (!q || !k || !v || !out) return fail(ND_ATTN_ERR_ARG, "null tensor");
     DeviceGuard dg(h->cfg.device);
-    std::vector<uint32_t> tpos(n), tseq(n);
-    std::vector<TokMeta> tok;
+    uint32_t jmax = 1;
+    size_t rows = 0;
     for (uint32_t i = 0; i < n; i++) {
-        tseq[i] = seq_ids ? seq_ids[i] : i;
-        tpos[i] = h->seqs[tseq[i]].pos;
+        const HostSeq &s = h->seqs[seq_ids ? seq_ids[i] : i];
+        const uint32_t j = visit_count(s.pos, s.n_sink, h->cfg.window);
+        jmax = std::max(jmax, j);
+        rows += (size_t)j * h->cfg.n_kv_heads;
     }
     const TokMeta *d_tok = nullptr;
     if (seq_ids) {
-        tok.resize(n);
-        for (uint32_t i = 0; i < n; i++) tok[i] = TokMeta{tseq[i], 0u, i};
+        std::vector<TokMeta> tok(n);
+        for (uint32_t i = 0; i < n; i++) tok[i] = TokMeta{seq_ids[i], 0u, i};
         rc = upload_tok(h, tok);
         if (rc) return rc;
         d_tok = h->d_tok;
     }
-    return run_attend(h, layer, n, d_tok, tpos, tseq, 1, q, k, v, gate, out);
+    return run_attend(h, layer, n, d_tok, nullptr, 0, jmax, rows, 1, q, k, v, gate, out);
 }
 
 int nd_attn_prefill(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const uint32_t *len,
@@ -751,41 +752,48 @@ int nd_attn_prefill(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_
     if (!wraps) {
         // Every new position gets its own slot and nothing a token reads is
         // overwritten: append all tokens, then attend causally.
-        std::vector<TokMeta> tok(total);
-        std::vector<uint32_t> tpos(total), tseq(total);
+        std::vector<nda::SeqSpan> spans;
+        spans.reserve(n);
+        uint32_t jmax = 1;
+        size_t rows = 0;
         for (uint32_t i = 0; i < n; i++) {
             const uint32_t s = seq_ids ? seq_ids[i] : i;
-            for (uint32_t t = 0; t < len[i]; t++) {
-                tok[cu[i] + t] = TokMeta{s, t, cu[i] + t};
-                tpos[cu[i] + t] = h->seqs[s].pos + t;
-                tseq[cu[i] + t] = s;
-            }
+            if (!len[i]) continue;
+            spans.push_back(nda::SeqSpan{s, cu[i], len[i]});
+            const uint64_t p0 = h->seqs[s].pos, L = len[i];
+            jmax = std::max<uint32_t>(jmax, (uint32_t)(p0 + L));
+            rows += (size_t)((L * p0 + L * (L + 1) / 2) * h->cfg.n_kv_heads);   // positions 0..p0+t per token
         }
-        rc = upload_tok(h, tok);
+        rc = grow(&h->d_spans, &h->spans_cap, spans.size());
         if (rc) return rc;
+        ND_CUDA(cudaMemcpyAsync(h->d_spans, spans.data(), spans.size() * sizeof(nda::SeqSpan),
+                                cudaMemcpyHostToDevice, h->stream));
         AttnParams P = base_params(h, layer);
-        P.k = k; P.v = v; P.tok = h->d_tok; P.n_tok = (uint32_t)total;
+        P.k = k; P.v = v; P.spans = h->d_spans; P.n_spans = (uint32_t)spans.size(); P.n_tok = (uint32_t)total;
         ND_CUDA(append_launch(h, P));
         h->launches++;
         if (tc_prefill_ok(h, q)) return run_prefill_tc(h, layer, n, seq_ids, len, cu, total, q, gate, out);
-        return run_attend(h, layer, (uint32_t)total, h->d_tok, tpos, tseq, 0, q, k, v, gate, out);
+        return run_attend(h, layer, (uint32_t)total, nullptr, h->d_spans, (uint32_t)spans.size(), jmax, rows, 0, q,
+                          k, v, gate, out);
     }
     // The ring wraps inside this call: a later token's slot can hold a position
     // an earlier token still reads, so run the reference's token-at-a-time
     // order (append, then attend) step by step.
     for (uint32_t t = 0; t < maxlen; t++) {
         std::vector<TokMeta> tok;
-        std::vector<uint32_t> tpos, tseq;
+        uint32_t jmax = 1;
+        size_t rows = 0;
         for (uint32_t i = 0; i < n; i++) {
             if (t >= len[i]) continue;
             const uint32_t s = seq_ids ? seq_ids[i] : i;
             tok.push_back(TokMeta{s, t, cu[i] + t});
-            tpos.push_back(h->seqs[s].pos + t);
-            tseq.push_back(s);
+            const uint32_t j = visit_count(h->seqs[s].pos + t, h->seqs[s].n_sink, W);
+            jmax = std::max(jmax, j);
+            rows += (size_t)j * h->cfg.n_kv_heads;
         }
         rc = upload_tok(h, tok);
         if (rc) return rc;
-        rc = run_attend(h, layer, (uint32_t)tok.size(), h->d_tok, tpos, tseq, 1, q, k, v, gate, out);
+        rc = run_attend(h, layer, (uint32_t)tok.size(), h->d_tok, nullptr, 0, jmax, rows, 1, q, k, v, gate, out);
         if (rc) return rc;
     }
     return ND_ATTN_OK;

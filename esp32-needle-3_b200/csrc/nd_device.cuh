@@ -43,6 +43,12 @@ struct TokMeta {
     uint32_t seq, off, row;
 };
 
+// One sequence of a batched prefill call: its tokens are rows
+// [tok_base, tok_base + len) of the packed tensors, in position order.
+struct SeqSpan {
+    uint32_t seq, tok_base, len;
+};
+
 // One layer of the cache. Rows are [n_kv][head_dim] elements; a sequence's
 // logical slot s lives in row seq*window + s (contiguous) or in page
 // btab[seq][s >> block_shift] at offset s & mask (paged).
@@ -63,7 +69,9 @@ struct AttnParams {
     uint32_t max_pos;
     const float *qnorm, *knorm;  // [qk_hd] or nullptr
     const SeqState *state;
-    const TokMeta *tok;          // nullptr: token i = sequence i, offset 0, row i
+    const TokMeta *tok;          // per-token map, or
+    const SeqSpan *spans;        // per-sequence spans (binary search), or neither:
+    uint32_t n_spans;            //   token i = sequence i, offset 0, row i
     uint32_t n_tok, n_heads, rep;
     float scale_log2;            // log2(e) / sqrtf(qk_hd)
     uint32_t chunk;              // visit rows per split
@@ -91,6 +99,20 @@ __device__ __forceinline__ void act_store(void *p, int dt, size_t i, float x) {
     if (dt == DT_F32) static_cast<float *>(p)[i] = x;
     else if (dt == DT_F16) static_cast<__half *>(p)[i] = __float2half_rn(x);
     else static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(x);
+}
+
+__device__ __forceinline__ TokMeta token_meta(const AttnParams &P, uint32_t tok) {
+    if (P.tok) return P.tok[tok];
+    if (P.spans) {
+        uint32_t lo = 0, hi = P.n_spans;   // last span with tok_base <= tok
+        while (hi - lo > 1) {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (P.spans[mid].tok_base <= tok) lo = mid;
+            else hi = mid;
+        }
+        return TokMeta{P.spans[lo].seq, tok - P.spans[lo].tok_base, tok};
+    }
+    return TokMeta{tok, 0u, tok};
 }
 
 __device__ __forceinline__ uint32_t kv_slot(uint32_t window, uint32_t n_sink, uint32_t p) {
@@ -310,7 +332,7 @@ __global__ void __launch_bounds__(128) append_kernel(const AttnParams P) {
     const size_t item = (size_t)blockIdx.x * 4u + (threadIdx.x >> 5);
     if (item >= (size_t)P.n_tok * P.c.n_kv) return;
     const uint32_t tok = (uint32_t)(item / P.c.n_kv), g = (uint32_t)(item % P.c.n_kv);
-    const TokMeta tm = P.tok ? P.tok[tok] : TokMeta{tok, 0u, tok};
+    const TokMeta tm = token_meta(P, tok);
     const SeqState st = P.state[tm.seq];
     const uint32_t pos = st.pos + tm.off;
     if (pos >= P.max_pos || st.n_sink >= P.c.window) {
@@ -483,7 +505,7 @@ __global__ void __launch_bounds__(128) attend_kernel(const AttnParams P) {
     const uint32_t item = blockIdx.x, split = blockIdx.y;
     const uint32_t n_kv = P.c.n_kv, W = P.c.window;
     const uint32_t tok = item / n_kv, g = item % n_kv;
-    const TokMeta tm = P.tok ? P.tok[tok] : TokMeta{tok, 0u, tok};
+    const TokMeta tm = token_meta(P, tok);
     const SeqState st = P.state[tm.seq];
     const uint32_t pos = st.pos + tm.off, n_sink = st.n_sink;
     if (pos >= P.max_pos || n_sink >= W) {

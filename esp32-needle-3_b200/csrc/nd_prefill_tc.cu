@@ -8,26 +8,28 @@
 // first and guarantees the call does not wrap the ring, so slot == position).
 //
 // One CTA = one work item = 128 consecutive query tokens of one sequence for
-// one query head h (KV head g = h / rep). 6 warps:
+// one query head h (KV head g = h / rep), walking 64-key tiles. 6 warps:
 //   warps 0-3  one thread per query row (= TMEM lane): RoPE(+norm) of the Q
-//              tile in shared memory, per-row online softmax on S read from
-//              TMEM, P written back to TMEM as bf16/f16 pairs, lazy O
-//              rescaling (only when a row max grows by more than 2^8), epilogue
-//   warp 4     TMA producer: Q tile once, then K/V tiles through a 3-stage ring
-//   warp 5     TMEM allocator + single-thread MMA issuer:
-//                S = Q K^T   (M=128, N=128, K=64: 4 x tcgen05.mma, A,B in smem)
-//                O += P V    (M=128, N=64, K=128: 8 x tcgen05.mma, A=P in TMEM,
-//                             B=V in smem, MN-major)
-// TMEM columns: S/P [0,128), O [128,192), Q_lo [192,224) -> 256 per CTA,
-// 2 CTAs per SM.
+//              row, per-row online softmax on S read from TMEM, P written back
+//              over S, lazy O rescaling (only when a row max grows by more than
+//              2^8), epilogue
+//   warp 4     TMA producer: Q tile once, then K/V tiles through a 4-stage ring
+//   warp 5     TMEM allocator + single-thread MMA issuer, S one tile ahead:
+//                S_j = Q K_j^T  (M=128, N=64, K=64; A = Q from TMEM, B = K smem)
+//                O  += P_j V_j  (M=128, N=64, K=64; A = P from TMEM, B = V smem,
+//                                MN-major)
+// TMEM columns (256 per CTA, 2 CTAs per SM): S/P double buffer [0,64) and
+// [64,128), O [128,192), Q_hi [192,224), Q_lo [224,256).
+//
 // Precision: a 16-bit operand rounds a value by up to 2^-9 (bf16), which rows
 // attending to few keys, or normed rows with larger |q||k|, turn into output
 // errors above 1e-3. So both 16-bit operands the kernel makes itself carry
-// ~16 mantissa bits as a hi/lo pair: the rotated Q (Q_hi in shared memory,
-// Q_lo in TMEM; S = Q_hi K^T + Q_lo K^T) and P (P_hi/P_lo overwrite the S
-// columns they came from, per 32-key chunk 16 columns of P_hi then 16 of P_lo;
-// O += P_hi V + P_lo V). K and V are the cache's own values, exact already.
-// The next S waits for the previous PV to finish reading P from the S columns.
+// ~16 mantissa bits as a hi/lo pair: the rotated Q (S = Q_hi K^T + Q_lo K^T)
+// and P (P_hi/P_lo overwrite the S columns they came from, per 32-key chunk 16
+// columns of P_hi then 16 of P_lo; O += P_hi V + P_lo V). K and V are the
+// cache's own values, exact already. S_{j+2} reuses S_j's columns, so it waits
+// for PV_j to finish reading P_j.
+//
 // Every mbarrier wait is bounded (~2 s of SM clock); on expiry the CTA raises
 // the error word, drains what it issued (bounded), frees TMEM and returns.
 // No TMA multicast anywhere.
@@ -42,33 +44,34 @@ namespace nda {
 namespace {
 
 constexpr int BM = 128;          // query rows per CTA (TMEM lanes)
-constexpr int BN = 128;          // keys per KV tile
+constexpr int BN = 64;           // keys per KV tile
 constexpr int HD = 64;           // head dim (one 128-byte swizzle row of 16-bit values)
-constexpr int STAGES = 3;
-constexpr uint32_t TILE_BYTES = BM * HD * 2;   // 16 KB, same for Q, K and V tiles
+constexpr int STAGES = 4;
+constexpr uint32_t Q_BYTES = BM * HD * 2;    // 16 KB
+constexpr uint32_t KV_BYTES = BN * HD * 2;   // 8 KB per K or V tile
 constexpr uint32_t TMEM_COLS = 256;
-constexpr uint32_t COL_S = 0, COL_O = 128, COL_QLO = 192;
+constexpr uint32_t COL_S = 0, COL_O = 128, COL_QHI = 192, COL_QLO = 224;
 constexpr long long kTimeoutCycles = 4000000000LL;   // ~2 s at 1.9 GHz
 
-// Dynamic shared memory: Q tile, K and V stage rings (each tile 1024-byte
-// aligned for the 128-byte swizzle), then the barrier block. Laid out by hand
-// so two CTAs fit one SM (2 x 114 816 B + the per-CTA reserve <= 228 KB).
+// Dynamic shared memory: Q landing tile, K and V stage rings (1024-byte
+// aligned tiles for the 128-byte swizzle), then the barrier block.
 constexpr uint32_t OFF_Q = 0;
-constexpr uint32_t OFF_K = OFF_Q + TILE_BYTES;
-constexpr uint32_t OFF_V = OFF_K + STAGES * TILE_BYTES;
-constexpr uint32_t OFF_BAR = OFF_V + STAGES * TILE_BYTES;
+constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
+constexpr uint32_t OFF_V = OFF_K + STAGES * KV_BYTES;
+constexpr uint32_t OFF_BAR = OFF_V + STAGES * KV_BYTES;
 
+// Per S/P buffer b (tiles j with j&1 == b, phase j>>1): s_full (S landed),
+// p_full (P written), pv_done (PV read P and wrote O). Every wait below is for
+// the next phase to complete or the one just completed, never further away,
+// which is what makes the parity test exact.
 struct Bars {
-    uint64_t q_full, q_ready, s_full, p_full, pv_done, drain;
+    uint64_t q_full, q_ready, drain;
+    uint64_t s_full[2], p_full[2], pv_done[2];
     uint64_t kv_full[STAGES], kv_empty[STAGES];
     uint32_t tmem_base;
     int abort_flag;
 };
 constexpr uint32_t SMEM_BYTES = OFF_BAR + sizeof(Bars);
-
-struct Smem {
-    uint8_t *q, *k[STAGES], *v[STAGES];
-};
 
 __device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -106,6 +109,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile
     }
     return true;
 }
+__device__ __forceinline__ void mbar_drain(uint64_t *b, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_test(b, parity) && clock64() - t0 < kTimeoutCycles) {
+    }
+}
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
@@ -134,12 +142,7 @@ __host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_fmt, uint32_t m, ui
     return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (b_mn_major << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
+// D (+)= A * B with A from TMEM and B from shared memory.
 __device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -196,6 +199,13 @@ __device__ __forceinline__ float2 unpack2(uint32_t u) {
         return __half22float2(t);
     }
 }
+// hi/lo split of a pair: hi = RN16(a,b), lo = RN16(a - hi, b - hi).
+template <bool BF16>
+__device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t &lo) {
+    hi = pack2<BF16>(a, b);
+    const float2 h = unpack2<BF16>(hi);
+    lo = pack2<BF16>(a - h.x, b - h.y);
+}
 
 // Offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled tile.
 __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) { return r * 128u + ((c ^ (r & 7u)) << 4); }
@@ -210,12 +220,7 @@ __global__ void __launch_bounds__(192, 2)
         if (tid == 0) atomicExch(P.err, 4);
         return;
     }
-    Smem S;
-    S.q = smem_raw + OFF_Q;
-    for (int s = 0; s < STAGES; s++) {
-        S.k[s] = smem_raw + OFF_K + s * TILE_BYTES;
-        S.v[s] = smem_raw + OFF_V + s * TILE_BYTES;
-    }
+    uint8_t *sq = smem_raw + OFF_Q;
     Bars &B = *reinterpret_cast<Bars *>(smem_raw + OFF_BAR);
     volatile int *abort_flag = &B.abort_flag;
     const PrefillWork w = P.work[blockIdx.x];
@@ -226,10 +231,12 @@ __global__ void __launch_bounds__(192, 2)
     if (tid == 0) {
         mbar_init(&B.q_full, 1);
         mbar_init(&B.q_ready, BM);
-        mbar_init(&B.s_full, 1);
-        mbar_init(&B.p_full, BM);
-        mbar_init(&B.pv_done, 1);
         mbar_init(&B.drain, 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&B.s_full[b], 1);
+            mbar_init(&B.p_full[b], BM);
+            mbar_init(&B.pv_done[b], 1);
+        }
         for (int s = 0; s < STAGES; s++) {
             mbar_init(&B.kv_full[s], 1);
             mbar_init(&B.kv_empty[s], 1);
@@ -250,76 +257,71 @@ __global__ void __launch_bounds__(192, 2)
     if (warp == 4) {
         // ---------------- TMA producer
         if (lane == 0) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(&kmap) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"(&vmap) : "memory");
-            mbar_expect_tx(&B.q_full, TILE_BYTES);
-            tma_load_2d(S.q, &qmap, (int)(w.head * HD), (int)(w.tok_base + w.t0), &B.q_full);
+            mbar_expect_tx(&B.q_full, Q_BYTES);
+            tma_load_2d(sq, &qmap, (int)(w.head * HD), (int)(w.tok_base + w.t0), &B.q_full);
             uint32_t issued = 0;
             for (uint32_t j = 0; j < nkv; j++) {
                 const uint32_t st = j % STAGES;
                 if (j >= STAGES && !mbar_wait(&B.kv_empty[st], ((j / STAGES) - 1) & 1, abort_flag)) break;
-                mbar_expect_tx(&B.kv_full[st], 2 * TILE_BYTES);
-                tma_load_2d(S.k[st], &kmap, (int)(g * HD), (int)(kv_row0 + j * BN), &B.kv_full[st]);
-                tma_load_2d(S.v[st], &vmap, (int)(g * HD), (int)(kv_row0 + j * BN), &B.kv_full[st]);
+                mbar_expect_tx(&B.kv_full[st], 2 * KV_BYTES);
+                tma_load_2d(smem_raw + OFF_K + st * KV_BYTES, &kmap, (int)(g * HD), (int)(kv_row0 + j * BN),
+                            &B.kv_full[st]);
+                tma_load_2d(smem_raw + OFF_V + st * KV_BYTES, &vmap, (int)(g * HD), (int)(kv_row0 + j * BN),
+                            &B.kv_full[st]);
                 issued = j + 1;
             }
             if (*abort_flag) {
-                // Let the copies this thread issued land before the CTA goes
-                // away (bounded: the Q tile and the newest K/V tile).
-                const long long t0 = clock64();
-                while (!mbar_test(&B.q_full, 0) && clock64() - t0 < kTimeoutCycles) {
-                }
-                if (issued) {
-                    const uint32_t j = issued - 1;
-                    const long long t1 = clock64();
-                    while (!mbar_test(&B.kv_full[j % STAGES], (j / STAGES) & 1) && clock64() - t1 < kTimeoutCycles) {
-                    }
-                }
+                // Let the copies this thread issued land before the CTA goes away.
+                mbar_drain(&B.q_full, 0);
+                if (issued) mbar_drain(&B.kv_full[(issued - 1) % STAGES], ((issued - 1) / STAGES) & 1);
             }
         }
     } else if (warp == 5) {
-        // ---------------- MMA issuer
+        // ---------------- MMA issuer: S one tile ahead of PV
         if (lane == 0) {
             constexpr uint32_t fmt = BF16 ? 1u : 0u;
             constexpr uint32_t id_s = idesc_f16(fmt, BM, BN, 0);
             constexpr uint32_t id_o = idesc_f16(fmt, BM, HD, 1);
-            const uint32_t q_addr = su32(S.q);
             bool ok = mbar_wait(&B.q_ready, 0, abort_flag);
-            uint32_t issued_any = 0;
-            for (uint32_t j = 0; ok && j < nkv; j++) {
-                const uint32_t st = j % STAGES;
-                if (!mbar_wait(&B.kv_full[st], (j / STAGES) & 1, abort_flag)) break;
-                // S_j lands where PV_{j-1} reads P_hi/P_lo.
-                if (j > 0 && !mbar_wait(&B.pv_done, (j - 1) & 1, abort_flag)) break;
+            uint32_t issued = 0;
+            // O += P_i V_i for tile i (P in S buffer i&1, V in stage i%STAGES).
+            auto issue_pv = [&](uint32_t i) -> bool {
+                const uint32_t b = i & 1, st = i % STAGES;
+                if (!mbar_wait(&B.p_full[b], (i >> 1) & 1, abort_flag)) return false;
                 fence_after();
-                const uint32_t k_addr = su32(S.k[st]), v_addr = su32(S.v[st]);
+                const uint32_t v_addr = su32(smem_raw + OFF_V + st * KV_BYTES);
+#pragma unroll
+                for (uint32_t kk = 0; kk < BN / 16; kk++) {
+                    const uint64_t vd = sdesc(v_addr + kk * 2048, KV_BYTES, 1024);
+                    const uint32_t pc = tbase + COL_S + b * BN + 32 * (kk / 2) + 8 * (kk % 2);
+                    umma_ts(tbase + COL_O, pc, vd, id_o, (i > 0 || kk > 0) ? 1u : 0u);
+                    umma_ts(tbase + COL_O, pc + 16, vd, id_o, 1u);
+                }
+                if (i + STAGES < nkv) umma_commit(&B.kv_empty[st]);
+                umma_commit(&B.pv_done[b]);
+                return true;
+            };
+            for (uint32_t j = 0; ok && j < nkv; j++) {
+                const uint32_t st = j % STAGES, b = j & 1;
+                if (!mbar_wait(&B.kv_full[st], (j / STAGES) & 1, abort_flag)) break;
+                // S_j overwrites the columns where PV_{j-2} read P_{j-2}.
+                if (j >= 2 && !mbar_wait(&B.pv_done[b], ((j - 2) >> 1) & 1, abort_flag)) break;
+                fence_after();
+                const uint32_t k_addr = su32(smem_raw + OFF_K + st * KV_BYTES);
 #pragma unroll
                 for (uint32_t kk = 0; kk < HD / 16; kk++) {
                     const uint64_t kd = sdesc(k_addr + kk * 32, 16, 1024);
-                    umma_ss(tbase + COL_S, sdesc(q_addr + kk * 32, 16, 1024), kd, id_s, kk > 0);
-                    umma_ts(tbase + COL_S, tbase + COL_QLO + kk * 8, kd, id_s, 1u);
+                    umma_ts(tbase + COL_S + b * BN, tbase + COL_QHI + kk * 8, kd, id_s, kk > 0);
+                    umma_ts(tbase + COL_S + b * BN, tbase + COL_QLO + kk * 8, kd, id_s, 1u);
                 }
-                umma_commit(&B.s_full);
-                issued_any = 1;
-                if (!mbar_wait(&B.p_full, j & 1, abort_flag)) break;
-                fence_after();
-#pragma unroll
-                for (uint32_t kk = 0; kk < BN / 16; kk++) {
-                    const uint64_t vd = sdesc(v_addr + kk * 2048, TILE_BYTES, 1024);
-                    const uint32_t pc = tbase + COL_S + 32 * (kk / 2) + 8 * (kk % 2);
-                    umma_ts(tbase + COL_O, pc, vd, id_o, (j > 0 || kk > 0) ? 1u : 0u);
-                    umma_ts(tbase + COL_O, pc + 16, vd, id_o, 1u);
-                }
-                // Free the stage only where the producer will wait for it, so no
-                // arrive is still pending when the CTA exits.
-                if (j + STAGES < nkv) umma_commit(&B.kv_empty[st]);
-                umma_commit(&B.pv_done);
+                umma_commit(&B.s_full[b]);
+                issued = 1;
+                if (j >= 1 && !issue_pv(j - 1)) break;
             }
-            if (*abort_flag && issued_any) {
+            if (ok && !*abort_flag) issue_pv(nkv - 1);
+            if (*abort_flag && issued) {
                 umma_commit(&B.drain);
-                const long long t0 = clock64();
-                while (!mbar_test(&B.drain, 0) && clock64() - t0 < kTimeoutCycles) {
-                }
+                mbar_drain(&B.drain, 0);
             }
         }
     } else {
@@ -330,14 +332,14 @@ __global__ void __launch_bounds__(192, 2)
         const bool row_valid = r < w.rows;
         bool ok = __all_sync(0xffffffffu, mbar_wait(&B.q_full, 0, abort_flag));
         if (ok) {
-            // RoPE (after the optional per-head norm) of this row, in place.
+            // RoPE (after the optional per-head norm) of this row, split hi/lo
+            // into TMEM as the A operand of S = Q K^T.
             const uint32_t pos_tab = row_valid ? qpos : w.pos0 + w.t0;
             const float2 *cs = P.rope + (size_t)pos_tab * (HD / 2);
-            uint8_t *row = S.q;
             float x[HD];
 #pragma unroll
             for (int c = 0; c < 8; c++) {
-                const uint4 u = *reinterpret_cast<const uint4 *>(row + swz(r, c));
+                const uint4 u = *reinterpret_cast<const uint4 *>(sq + swz(r, c));
                 const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
@@ -364,95 +366,79 @@ __global__ void __launch_bounds__(192, 2)
                 x[i] = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(b, t.y));
                 x[i + HD / 2] = __fadd_rn(__fmul_rn(b, t.x), __fmul_rn(a, t.y));
             }
-            uint32_t lo[32];
+            uint32_t hi[32], lo[32];
 #pragma unroll
-            for (int c = 0; c < 8; c++) {
-                uint32_t hw[4];
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const float a = x[c * 8 + 2 * e], b = x[c * 8 + 2 * e + 1];
-                    hw[e] = pack2<BF16>(a, b);
-                    const float2 hf = unpack2<BF16>(hw[e]);
-                    lo[c * 4 + e] = pack2<BF16>(a - hf.x, b - hf.y);
-                }
-                *reinterpret_cast<uint4 *>(row + swz(r, c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            }
+            for (int e = 0; e < 32; e++) split2<BF16>(x[2 * e], x[2 * e + 1], hi[e], lo[e]);
+            tmem_st32(lane_addr + COL_QHI, hi);
             tmem_st32(lane_addr + COL_QLO, lo);
             tmem_wait_st();
             fence_before();
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(&B.q_ready);
         }
         const float c = P.scale_log2;
         float m = -INFINITY, l = 0.0f;
         for (uint32_t j = 0; ok && j < nkv; j++) {
-            if (!__all_sync(0xffffffffu, mbar_wait(&B.s_full, j & 1, abort_flag))) {
+            const uint32_t b = j & 1, sbuf = lane_addr + COL_S + b * BN;
+            if (!__all_sync(0xffffffffu, mbar_wait(&B.s_full[b], (j >> 1) & 1, abort_flag))) {
                 ok = false;
                 break;
             }
             fence_after();
             const int lim = (int)qpos - (int)(j * BN);   // keys [0, lim] of this tile are visible
+            uint32_t sv[2][32];
+            tmem_ld32(sbuf, sv[0]);
+            tmem_ld32(sbuf + 32, sv[1]);
             float tmax = -INFINITY;
 #pragma unroll
-            for (int c4 = 0; c4 < BN / 32; c4++) {
-                uint32_t sv[32];
-                tmem_ld32(lane_addr + COL_S + c4 * 32, sv);
+            for (int c2 = 0; c2 < 2; c2++)
 #pragma unroll
-                for (int e = 0; e < 32; e++) {
-                    const float s = (c4 * 32 + e <= lim) ? __uint_as_float(sv[e]) : -INFINITY;
-                    tmax = fmaxf(tmax, s);
-                }
-            }
+                for (int e = 0; e < 32; e++)
+                    if (c2 * 32 + e <= lim) tmax = fmaxf(tmax, __uint_as_float(sv[c2][e]));
             tmax *= c;
             const bool grow = (j == 0) || (tmax > m + 8.0f);
-            if (j > 0) {
-                // PV of the previous tile must be done before O or P is touched.
-                if (!__all_sync(0xffffffffu, mbar_wait(&B.pv_done, (j - 1) & 1, abort_flag))) {
+            // O rescale when a row max grew: TMEM loads/stores are warp-wide, so
+            // the warp rescales when any of its rows needs it (factor 1 for the
+            // others), after PV_{j-1} has finished writing O.
+            if (j > 0 && __any_sync(0xffffffffu, grow)) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&B.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag))) {
                     ok = false;
                     break;
                 }
                 fence_after();
-                // TMEM loads/stores are warp-wide: rescale when any row of the
-                // warp needs it, with a factor of 1 for the others.
-                if (__any_sync(0xffffffffu, grow)) {
-                    const float alpha = grow ? ex2(m - tmax) : 1.0f;
-                    l *= alpha;
+                const float alpha = grow ? ex2(m - tmax) : 1.0f;
+                l *= alpha;
+                uint32_t ov[32];
 #pragma unroll
-                    for (int h2 = 0; h2 < HD / 32; h2++) {
-                        uint32_t ov[32];
-                        tmem_ld32(lane_addr + COL_O + h2 * 32, ov);
+                for (int h2 = 0; h2 < HD / 32; h2++) {
+                    tmem_ld32(lane_addr + COL_O + h2 * 32, ov);
 #pragma unroll
-                        for (int e = 0; e < 32; e++) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-                        tmem_st32(lane_addr + COL_O + h2 * 32, ov);
-                    }
+                    for (int e = 0; e < 32; e++) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+                    tmem_st32(lane_addr + COL_O + h2 * 32, ov);
                 }
             }
             if (grow) m = tmax;
 #pragma unroll
-            for (int c4 = 0; c4 < BN / 32; c4++) {
-                uint32_t sv[32];
-                tmem_ld32(lane_addr + COL_S + c4 * 32, sv);
-                {
-                    uint32_t pk[32];
+            for (int c2 = 0; c2 < 2; c2++) {
+                uint32_t pk[32];
 #pragma unroll
-                    for (int e = 0; e < 32; e += 2) {
-                        const float s0 = (c4 * 32 + e <= lim) ? __uint_as_float(sv[e]) : -INFINITY;
-                        const float s1 = (c4 * 32 + e + 1 <= lim) ? __uint_as_float(sv[e + 1]) : -INFINITY;
-                        const float p0 = ex2(fmaf(s0, c, -m)), p1 = ex2(fmaf(s1, c, -m));
-                        l += p0 + p1;
-                        const uint32_t hi = pack2<BF16>(p0, p1);
-                        const float2 hf = unpack2<BF16>(hi);
-                        pk[e / 2] = hi;
-                        pk[16 + e / 2] = pack2<BF16>(p0 - hf.x, p1 - hf.y);
-                    }
-                    tmem_st32(lane_addr + COL_S + c4 * 32, pk);
+                for (int e = 0; e < 32; e += 2) {
+                    const float s0 = (c2 * 32 + e <= lim) ? __uint_as_float(sv[c2][e]) : -INFINITY;
+                    const float s1 = (c2 * 32 + e + 1 <= lim) ? __uint_as_float(sv[c2][e + 1]) : -INFINITY;
+                    const float p0 = ex2(fmaf(s0, c, -m)), p1 = ex2(fmaf(s1, c, -m));
+                    l += p0 + p1;
+                    split2<BF16>(p0, p1, pk[e / 2], pk[16 + e / 2]);
                 }
+                tmem_st32(sbuf + c2 * 32, pk);
             }
             tmem_wait_st();
             fence_before();
-            mbar_arrive(&B.p_full);
+            mbar_arrive(&B.p_full[b]);
         }
-        if (ok && __all_sync(0xffffffffu, mbar_wait(&B.pv_done, (nkv - 1) & 1, abort_flag))) {
+        // O is final once the last two PVs (one per buffer) are done.
+        if (ok && nkv >= 2 &&
+            !__all_sync(0xffffffffu, mbar_wait(&B.pv_done[(nkv - 2) & 1], ((nkv - 2) >> 1) & 1, abort_flag)))
+            ok = false;
+        if (ok && __all_sync(0xffffffffu, mbar_wait(&B.pv_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, abort_flag))) {
             fence_after();
             const float inv_l = 1.0f / l;
             const size_t obase = ((size_t)(w.tok_base + w.t0 + r) * P.n_heads + w.head) * HD;
@@ -460,14 +446,32 @@ __global__ void __launch_bounds__(192, 2)
             for (int h2 = 0; h2 < HD / 32; h2++) {
                 uint32_t ov[32];
                 tmem_ld32(lane_addr + COL_O + h2 * 32, ov);
-                if (row_valid) {
+                if (!row_valid) continue;
+                float val[32];
 #pragma unroll
-                    for (int e = 0; e < 32; e++) {
-                        float val = __uint_as_float(ov[e]) * inv_l;
-                        if (P.gate)
-                            val *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, obase + h2 * 32 + e) *
-                                                         1.4426950408889634f));
-                        act_store(P.out, P.out_dt, obase + h2 * 32 + e, val);
+                for (int e = 0; e < 32; e++) {
+                    val[e] = __uint_as_float(ov[e]) * inv_l;
+                    if (P.gate)
+                        val[e] *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, obase + h2 * 32 + e) *
+                                                    1.4426950408889634f));
+                }
+                if (P.out_dt == DT_F32) {
+                    float4 *o4 = reinterpret_cast<float4 *>(static_cast<float *>(P.out) + obase + h2 * 32);
+#pragma unroll
+                    for (int e = 0; e < 8; e++)
+                        o4[e] = make_float4(val[4 * e], val[4 * e + 1], val[4 * e + 2], val[4 * e + 3]);
+                } else {
+                    uint4 *o4 = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(P.out) + obase + h2 * 32);
+                    const bool obf = P.out_dt == DT_BF16;
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        uint32_t wd[4];
+#pragma unroll
+                        for (int f = 0; f < 4; f++) {
+                            const float a = val[8 * e + 2 * f], bb = val[8 * e + 2 * f + 1];
+                            wd[f] = obf ? pack2<true>(a, bb) : pack2<false>(a, bb);
+                        }
+                        o4[e] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
                     }
                 }
             }

@@ -100,6 +100,8 @@ def ref() -> ctypes.CDLL:
         lib.ndref_prefix_image.restype = c_long
         lib.ndref_prefix_image.argtypes = [POINTER(RefGeom), c_void_p, c_void_p, c_void_p, c_void_p, c_uint32,
                                            c_void_p, c_size_t, POINTER(c_uint32)]
+        lib.ndref_prefill_bench.restype = c_double
+        lib.ndref_prefill_bench.argtypes = [POINTER(RefGeom), c_uint32, c_uint32, c_uint32, c_float, c_uint32]
         lib.ndref_decode_bench.restype = c_double
         lib.ndref_decode_bench.argtypes = [POINTER(RefGeom), c_uint32, c_void_p, c_uint32, c_uint32, c_float,
                                            c_uint32]
@@ -294,3 +296,8 @@ def ref_decode_bench(n_heads, n_kv, qk, vd, window, ctx, steps, layers, theta, t
     c = np.ascontiguousarray(ctx, dtype=np.uint32)
     return float(ref().ndref_decode_bench(ctypes.byref(g), len(c), c.ctypes.data, steps, layers, c_float(theta),
                                           threads))
+
+
+def ref_prefill_bench(n_heads, n_kv, qk, vd, window, n_seqs, tokens, layers, theta, threads) -> float:
+    g = RefGeom(layers, n_heads, n_kv, qk, vd, window)
+    return float(ref().ndref_prefill_bench(ctypes.byref(g), n_seqs, tokens, layers, c_float(theta), threads))

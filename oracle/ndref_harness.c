@@ -295,3 +295,83 @@ double ndref_decode_bench(const ndref_geom *g, uint32_t n_seqs, const uint32_t *
     }
     return worst;
 }
+
+/* ---- CPU baseline: prefill, the reference's way (one token at a time) ----- */
+typedef struct {
+    const ndref_geom *g;
+    uint32_t          first, count, tokens, layers;
+    float             theta;
+    double            secs;
+    int               rc;
+} ndref_pjob;
+
+static void *ndref_prefill_worker(void *arg)
+{
+    ndref_pjob       *j = (ndref_pjob *)arg;
+    const ndref_geom *g = j->g;
+    uint32_t          nh = g->n_heads, nkv = g->n_kv_heads;
+    uint32_t          qk = g->qk_head_dim, vh = g->v_head_dim, W = g->window;
+    size_t            kn = (size_t)j->layers * W * nkv * qk;
+    size_t            vn = (size_t)j->layers * W * nkv * vh;
+    size_t            sn = (size_t)j->layers * W * nkv;
+    int8_t           *kc = (int8_t *)calloc(kn, 1), *vc = (int8_t *)calloc(vn, 1);
+    float            *ks = (float *)calloc(sn, 4), *vs = (float *)calloc(sn, 4);
+    float            *q = (float *)malloc(4 * nh * qk), *k = (float *)malloc(4 * nkv * qk);
+    float            *v = (float *)malloc(4 * nkv * vh), *o = (float *)malloc(4 * nh * vh);
+    float             inv[ND_KV_HD_CAP], cs[ND_KV_HD_CAP], sn_[ND_KV_HD_CAP];
+    uint32_t          s, t, l, i, seed = 777u + j->first;
+    struct timespec   a, b;
+
+    j->rc = -12;
+    if (!kc || !vc || !ks || !vs || !q || !k || !v || !o) goto out;
+    ndref_rope_inv(j->theta, qk, inv);
+    clock_gettime(CLOCK_MONOTONIC, &a);
+    for (s = j->first; s < j->first + j->count; s++) {
+        for (t = 0; t < j->tokens && t < W; t++) {
+            ndref_rope_at(inv, qk, t, cs, sn_);
+            for (l = 0; l < j->layers; l++) {
+                for (i = 0; i < nh * qk; i++) { seed = seed * 1664525u + 1013904223u; q[i] = (float)(seed >> 8) * 5.96e-8f - 0.5f; }
+                for (i = 0; i < nkv * qk; i++) { seed = seed * 1664525u + 1013904223u; k[i] = (float)(seed >> 8) * 5.96e-8f - 0.5f; }
+                for (i = 0; i < nkv * vh; i++) { seed = seed * 1664525u + 1013904223u; v[i] = (float)(seed >> 8) * 5.96e-8f - 0.5f; }
+                if (ndref_attn_token(g, kc, vc, ks, vs, l, t, 0, cs, sn_, NULL, NULL, q, k, v, NULL, o))
+                    goto out;
+            }
+        }
+    }
+    clock_gettime(CLOCK_MONOTONIC, &b);
+    j->secs = (double)(b.tv_sec - a.tv_sec) + 1e-9 * (double)(b.tv_nsec - a.tv_nsec);
+    j->rc = 0;
+out:
+    free(kc); free(vc); free(ks); free(vs); free(q); free(k); free(v); free(o);
+    return NULL;
+}
+
+/* Prefills `n_seqs` sequences of `tokens` tokens through `layers` layers on
+ * `threads` threads (whole sequences per thread). Returns the slowest
+ * thread's wall seconds, or a negative code. */
+double ndref_prefill_bench(const ndref_geom *g, uint32_t n_seqs, uint32_t tokens, uint32_t layers, float theta,
+                           uint32_t threads)
+{
+    pthread_t   tid[256];
+    ndref_pjob  job[256];
+    uint32_t    t, per, first = 0;
+    double      worst = 0.0;
+
+    if (threads == 0) threads = 1;
+    if (threads > 256) threads = 256;
+    if (threads > n_seqs) threads = n_seqs;
+    per = (n_seqs + threads - 1) / threads;
+    for (t = 0; t < threads; t++) {
+        uint32_t cnt = (first + per <= n_seqs) ? per : n_seqs - first;
+        job[t].g = g; job[t].first = first; job[t].count = cnt; job[t].tokens = tokens;
+        job[t].layers = layers; job[t].theta = theta; job[t].secs = 0.0; job[t].rc = 0;
+        first += cnt;
+        pthread_create(&tid[t], NULL, ndref_prefill_worker, &job[t]);
+    }
+    for (t = 0; t < threads; t++) {
+        pthread_join(tid[t], NULL);
+        if (job[t].rc) return (double)job[t].rc;
+        if (job[t].secs > worst) worst = job[t].secs;
+    }
+    return worst;
+}
