@@ -347,6 +347,55 @@ __global__ void __launch_bounds__(128) append_kernel(const AttnParams P) {
                              P.rope + (size_t)pos * (QK / 2), P.knorm, (int)lane);
 }
 
+// K1 fast path: no head norm, activations already in the cache's 16-bit type,
+// QK == VD. TPR = QK/8 threads per (token, KV head) row; thread t rotates the
+// pairs (4t..4t+3, HALF+4t..HALF+4t+3) with 8-byte loads/stores and copies 8
+// values of v with one 16-byte load/store. Same rounded statements as
+// warp_norm_rope, so the rotated K is the same bits.
+template <int HDIM, typename KVT>
+__global__ void __launch_bounds__(256) append_vec_kernel(const AttnParams P) {
+    constexpr int TPR = HDIM / 8, HALF = HDIM / 2, ROWS = 256 / TPR;
+    static_assert(KvT<KVT>::dt == DT_F16 || KvT<KVT>::dt == DT_BF16, "16-bit caches");
+    const int t = threadIdx.x % TPR;
+    const size_t item = (size_t)blockIdx.x * ROWS + threadIdx.x / TPR;
+    if (item >= (size_t)P.n_tok * P.c.n_kv) return;
+    const uint32_t tok = (uint32_t)(item / P.c.n_kv), g = (uint32_t)(item % P.c.n_kv);
+    const TokMeta tm = token_meta(P, tok);
+    const SeqState st = P.state[tm.seq];
+    const uint32_t pos = st.pos + tm.off;
+    if (pos >= P.max_pos || st.n_sink >= P.c.window) {
+        if (t == 0) atomicExch(P.err, 2);
+        return;
+    }
+    const size_t row = phys_row(P.c, tm.seq, kv_slot(P.c.window, st.n_sink, pos));
+    const size_t src = ((size_t)tm.row * P.c.n_kv + g) * HDIM;
+    const KVT *k = static_cast<const KVT *>(P.k) + src;
+    const KVT *v = static_cast<const KVT *>(P.v) + src;
+    const uint2 ka = *reinterpret_cast<const uint2 *>(k + 4 * t);
+    const uint2 kb = *reinterpret_cast<const uint2 *>(k + HALF + 4 * t);
+    const uint4 vv = *reinterpret_cast<const uint4 *>(v + 8 * t);
+    const float4 *cs4 = reinterpret_cast<const float4 *>(P.rope + (size_t)pos * HALF + 4 * t);
+    const float4 c01 = cs4[0], c23 = cs4[1];
+    const float cc[4] = {c01.x, c01.z, c23.x, c23.z}, sn[4] = {c01.y, c01.w, c23.y, c23.w};
+    KVT a[4], b[4];
+    memcpy(a, &ka, 8);
+    memcpy(b, &kb, 8);
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const float x1 = (float)a[e], x2 = (float)b[e];
+        a[e] = kv_from_float<KVT>(__fsub_rn(__fmul_rn(x1, cc[e]), __fmul_rn(x2, sn[e])));
+        b[e] = kv_from_float<KVT>(__fadd_rn(__fmul_rn(x2, cc[e]), __fmul_rn(x1, sn[e])));
+    }
+    KVT *kd = static_cast<KVT *>(P.c.k) + row * P.c.k_dim + (size_t)g * HDIM;
+    KVT *vd = static_cast<KVT *>(P.c.v) + row * P.c.v_dim + (size_t)g * HDIM;
+    uint2 oa, ob;
+    memcpy(&oa, a, 8);
+    memcpy(&ob, b, 8);
+    *reinterpret_cast<uint2 *>(kd + 4 * t) = oa;
+    *reinterpret_cast<uint2 *>(kd + HALF + 4 * t) = ob;
+    *reinterpret_cast<uint4 *>(vd + 8 * t) = vv;
+}
+
 // ------------------------------------------------------ split-KV attention
 template <int W, bool NC>
 __device__ __forceinline__ void load_words(const void *p, uint32_t (&w)[W]) {

@@ -26,6 +26,19 @@ template <typename KVT>
 cudaError_t append_launch_t(int qk, int vd, const AttnParams &P, cudaStream_t s) {
     const size_t items = (size_t)P.n_tok * P.c.n_kv;
     if (items == 0) return cudaSuccess;
+    if constexpr (KvT<KVT>::dt == DT_F16 || KvT<KVT>::dt == DT_BF16) {
+        // Vectorised path: no head norm, activations in the cache's type,
+        // 16-byte aligned k/v rows.
+        const bool vec = !P.knorm && P.act_dt == KvT<KVT>::dt && qk == vd && (qk == 64 || qk == 128) &&
+                         ((reinterpret_cast<uintptr_t>(P.k) | reinterpret_cast<uintptr_t>(P.v)) & 15u) == 0;
+        if (vec) {
+            const size_t rows_per_block = 256 / (qk / 8);
+            const unsigned blocks = (unsigned)((items + rows_per_block - 1) / rows_per_block);
+            if (qk == 64) append_vec_kernel<64, KVT><<<blocks, 256, 0, s>>>(P);
+            else append_vec_kernel<128, KVT><<<blocks, 256, 0, s>>>(P);
+            return cudaGetLastError();
+        }
+    }
     const unsigned blocks = (unsigned)((items + 3) / 4);
 #define ND_CASE(Q, V)                                                      \
     if (qk == Q && vd == V) {                                              \

@@ -8,27 +8,34 @@
 // first and guarantees the call does not wrap the ring, so slot == position).
 //
 // One CTA = one work item = 128 consecutive query tokens of one sequence for
-// one query head h (KV head g = h / rep), walking 64-key tiles. 6 warps:
+// one query head h (KV head g = h / rep), walking 128-key tiles. 6 warps:
 //   warps 0-3  one thread per query row (= TMEM lane): RoPE(+norm) of the Q
 //              row, per-row online softmax on S read from TMEM, P written back
 //              over S, lazy O rescaling (only when a row max grows by more than
 //              2^8), epilogue
-//   warp 4     TMA producer: Q tile once, then K/V tiles through a 4-stage ring
-//   warp 5     TMEM allocator + single-thread MMA issuer, S one tile ahead:
-//                S_j = Q K_j^T  (M=128, N=64, K=64; A = Q from TMEM, B = K smem)
-//                O  += P_j V_j  (M=128, N=64, K=64; A = P from TMEM, B = V smem,
+//   warp 4     TMA producer: Q tile once, then K/V tiles through a 2-stage ring
+//   warp 5     TMEM allocator + single-thread MMA issuer, an event loop that
+//              issues each PV as soon as its P is written and each S as soon
+//              as its K tile has landed and its buffer is free:
+//                S_j = Q K_j^T  (M=128, N=128, K=64; A = Q from TMEM, B = K smem)
+//                O  += P_j V_j  (M=128, N=64, K=128; A = P from TMEM, B = V smem,
 //                                MN-major)
-// TMEM columns (256 per CTA, 2 CTAs per SM): S/P double buffer [0,64) and
-// [64,128), O [128,192), Q_hi [192,224), Q_lo [224,256).
+// TMEM columns (256 per CTA, 2 CTAs per SM): the S/P buffer [0,128), O
+// [128,192), Q_hi [192,224), Q_lo [224,256). A tcgen05.mma costs at least ~46
+// cycles whatever its N, and reaches the tensor core's peak only from N=128 on,
+// so S uses 128-key tiles; the two CTAs of an SM overlap one CTA's softmax
+// with the other's MMAs.
 //
-// Precision: a 16-bit operand rounds a value by up to 2^-9 (bf16), which rows
-// attending to few keys, or normed rows with larger |q||k|, turn into output
-// errors above 1e-3. So both 16-bit operands the kernel makes itself carry
-// ~16 mantissa bits as a hi/lo pair: the rotated Q (S = Q_hi K^T + Q_lo K^T)
+// Precision: bf16 rounds a value by up to 2^-9, which rows attending to few
+// keys (P) or normed rows with larger |q||k| (Q) turn into output errors above
+// 1e-3 (measured ~1.5e-3 and ~2e-3). So with bf16 both operands the kernel
+// makes itself carry ~16 mantissa bits as a hi/lo pair: the rotated Q
+// (S = Q_hi K^T + Q_lo K^T)
 // and P (P_hi/P_lo overwrite the S columns they came from, per 32-key chunk 16
 // columns of P_hi then 16 of P_lo; O += P_hi V + P_lo V). K and V are the
-// cache's own values, exact already. S_{j+2} reuses S_j's columns, so it waits
-// for PV_j to finish reading P_j.
+// cache's own values, exact already. f16 (11-bit mantissa, errors ~2e-4 and
+// ~5e-4) needs no split: one MMA per k-step, P as single f16 pairs. S_{j+NB}
+// reuses S_j's columns, so it waits for PV_j.
 //
 // Every mbarrier wait is bounded (~2 s of SM clock); on expiry the CTA raises
 // the error word, drains what it issued (bounded), frees TMEM and returns.
@@ -46,7 +53,8 @@ namespace {
 constexpr int BM = 128;          // query rows per CTA (TMEM lanes)
 constexpr int BN = 64;           // keys per KV tile
 constexpr int HD = 64;           // head dim (one 128-byte swizzle row of 16-bit values)
-constexpr int STAGES = 4;
+constexpr int NB = 2;            // S/P buffers in TMEM
+constexpr int STAGES = 4;        // K/V ring
 constexpr uint32_t Q_BYTES = BM * HD * 2;    // 16 KB
 constexpr uint32_t KV_BYTES = BN * HD * 2;   // 8 KB per K or V tile
 constexpr uint32_t TMEM_COLS = 256;
@@ -60,13 +68,13 @@ constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
 constexpr uint32_t OFF_V = OFF_K + STAGES * KV_BYTES;
 constexpr uint32_t OFF_BAR = OFF_V + STAGES * KV_BYTES;
 
-// Per S/P buffer b (tiles j with j&1 == b, phase j>>1): s_full (S landed),
-// p_full (P written), pv_done (PV read P and wrote O). Every wait below is for
-// the next phase to complete or the one just completed, never further away,
-// which is what makes the parity test exact.
+// Per S/P buffer b (tiles j with j % NB == b, phase j / NB): s_full (S
+// landed), p_full (P written), pv_done (PV read P and wrote O). Every wait
+// below is for the next phase to complete or the one just completed, never
+// further away, which is what makes the parity test exact.
 struct Bars {
     uint64_t q_full, q_ready, drain;
-    uint64_t s_full[2], p_full[2], pv_done[2];
+    uint64_t s_full[NB], p_full[NB], pv_done[NB];
     uint64_t kv_full[STAGES], kv_empty[STAGES];
     uint32_t tmem_base;
     int abort_flag;
@@ -157,20 +165,33 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
 #define ND_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
 #define ND_W8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), "r"(r[i + 5]), "r"(r[i + 6]), "r"(r[i + 7])
 
-// 32 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// 32 consecutive 32-bit TMEM columns of this thread's lane; tmem_ld32 waits,
+// tmem_ld32_async leaves the wait to tmem_wait_ld() so loads can overlap.
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t *r) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
         "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
         : ND_R8(0), ND_R8(8), ND_R8(16), ND_R8(24)
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    tmem_ld32_async(taddr, r);
+    tmem_wait_ld();
 }
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
         "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
         ND_W8(0), ND_W8(8), ND_W8(16), ND_W8(24)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -207,6 +228,36 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t 
     lo = pack2<BF16>(a - h.x, b - h.y);
 }
 
+// P = 2^(S*c - m) for 32 keys of a row, written over their S columns as
+// hi/lo 16-bit pairs (16 columns of hi, then 16 of lo); the row sum goes into l2.
+template <bool BF16>
+__device__ __forceinline__ void write_p_chunk(const uint32_t (&sv)[32], uint32_t taddr, float c, float m, float2 &l2) {
+    const float2 c2v = make_float2(c, c), nm2 = make_float2(-m, -m), neg1 = make_float2(-1.0f, -1.0f);
+    float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+    uint32_t pk[32];
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+        const float2 sp = make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
+        const float2 t = __ffma2_rn(sp, c2v, nm2);
+        const float2 pp = make_float2(ex2(t.x), ex2(t.y));
+        acc[(e >> 1) & 1] = __fadd2_rn(acc[(e >> 1) & 1], pp);
+        if constexpr (BF16) {
+            // hi = the upper halves (truncated bf16), lo = RN(p - hi): p - hi is
+            // exact in fp32, so hi + lo keeps ~16 bits of p.
+            const uint32_t u0 = __float_as_uint(pp.x), u1 = __float_as_uint(pp.y);
+            pk[e / 2] = __byte_perm(u0, u1, 0x7632);
+            const float2 hf = make_float2(__uint_as_float(u0 & 0xffff0000u), __uint_as_float(u1 & 0xffff0000u));
+            const float2 lf = __ffma2_rn(hf, neg1, pp);
+            pk[16 + e / 2] = pack2<true>(lf.x, lf.y);
+        } else {
+            pk[e / 2] = pack2<false>(pp.x, pp.y);
+        }
+    }
+    if constexpr (BF16) tmem_st32(taddr, pk);
+    else tmem_st16(taddr, pk);
+    l2 = __fadd2_rn(l2, __fadd2_rn(acc[0], acc[1]));
+}
+
 // Offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled tile.
 __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) { return r * 128u + ((c ^ (r & 7u)) << 4); }
 
@@ -230,11 +281,11 @@ __global__ void __launch_bounds__(192, 2)
 
     if (tid == 0) {
         mbar_init(&B.q_full, 1);
-        mbar_init(&B.q_ready, BM);
+        mbar_init(&B.q_ready, BM / 32);       // one arrive per softmax warp
         mbar_init(&B.drain, 1);
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < NB; b++) {
             mbar_init(&B.s_full[b], 1);
-            mbar_init(&B.p_full[b], BM);
+            mbar_init(&B.p_full[b], BM / 32);
             mbar_init(&B.pv_done[b], 1);
         }
         for (int s = 0; s < STAGES; s++) {
@@ -284,41 +335,57 @@ __global__ void __launch_bounds__(192, 2)
             constexpr uint32_t id_o = idesc_f16(fmt, BM, HD, 1);
             bool ok = mbar_wait(&B.q_ready, 0, abort_flag);
             uint32_t issued = 0;
-            // O += P_i V_i for tile i (P in S buffer i&1, V in stage i%STAGES).
-            auto issue_pv = [&](uint32_t i) -> bool {
-                const uint32_t b = i & 1, st = i % STAGES;
-                if (!mbar_wait(&B.p_full[b], (i >> 1) & 1, abort_flag)) return false;
-                fence_after();
-                const uint32_t v_addr = su32(smem_raw + OFF_V + st * KV_BYTES);
+            // Event loop: issue whatever is ready, PV first (it frees an S
+            // buffer), then the next S. A barrier is only tested once the
+            // operation it tracks has been issued, so each test is for the
+            // next phase or the one just completed (the parity test is exact).
+            uint32_t sj = 0, pi = 0;                 // next S to issue, next PV to issue
+            long long idle_since = clock64();
+            while (ok && pi < nkv) {
+                bool progressed = false;
+                if (pi < sj && mbar_test(&B.p_full[pi % NB], (pi / NB) & 1)) {
+                    // O += P_pi V_pi (P in S buffer pi % NB, V in stage pi % STAGES).
+                    const uint32_t b = pi % NB, st = pi % STAGES;
+                    fence_after();
+                    const uint32_t v_addr = su32(smem_raw + OFF_V + st * KV_BYTES);
 #pragma unroll
-                for (uint32_t kk = 0; kk < BN / 16; kk++) {
-                    const uint64_t vd = sdesc(v_addr + kk * 2048, KV_BYTES, 1024);
-                    const uint32_t pc = tbase + COL_S + b * BN + 32 * (kk / 2) + 8 * (kk % 2);
-                    umma_ts(tbase + COL_O, pc, vd, id_o, (i > 0 || kk > 0) ? 1u : 0u);
-                    umma_ts(tbase + COL_O, pc + 16, vd, id_o, 1u);
+                    for (uint32_t kk = 0; kk < BN / 16; kk++) {
+                        const uint64_t vd = sdesc(v_addr + kk * 2048, KV_BYTES, 1024);
+                        const uint32_t pc = tbase + COL_S + b * BN + 32 * (kk / 2) + 8 * (kk % 2);
+                        umma_ts(tbase + COL_O, pc, vd, id_o, (pi > 0 || kk > 0) ? 1u : 0u);
+                        if constexpr (BF16) umma_ts(tbase + COL_O, pc + 16, vd, id_o, 1u);
+                    }
+                    if (pi + STAGES < nkv) umma_commit(&B.kv_empty[st]);
+                    umma_commit(&B.pv_done[b]);
+                    pi++;
+                    progressed = true;
                 }
-                if (i + STAGES < nkv) umma_commit(&B.kv_empty[st]);
-                umma_commit(&B.pv_done[b]);
-                return true;
-            };
-            for (uint32_t j = 0; ok && j < nkv; j++) {
-                const uint32_t st = j % STAGES, b = j & 1;
-                if (!mbar_wait(&B.kv_full[st], (j / STAGES) & 1, abort_flag)) break;
-                // S_j overwrites the columns where PV_{j-2} read P_{j-2}.
-                if (j >= 2 && !mbar_wait(&B.pv_done[b], ((j - 2) >> 1) & 1, abort_flag)) break;
-                fence_after();
-                const uint32_t k_addr = su32(smem_raw + OFF_K + st * KV_BYTES);
+                if (sj < nkv && (sj < NB || (pi > sj - NB && mbar_test(&B.pv_done[sj % NB], (sj / NB - 1) & 1))) &&
+                    mbar_test(&B.kv_full[sj % STAGES], (sj / STAGES) & 1)) {
+                    // S_sj = Q K_sj^T into buffer sj % NB (its previous P was read).
+                    const uint32_t b = sj % NB, st = sj % STAGES;
+                    fence_after();
+                    const uint32_t k_addr = su32(smem_raw + OFF_K + st * KV_BYTES);
 #pragma unroll
-                for (uint32_t kk = 0; kk < HD / 16; kk++) {
-                    const uint64_t kd = sdesc(k_addr + kk * 32, 16, 1024);
-                    umma_ts(tbase + COL_S + b * BN, tbase + COL_QHI + kk * 8, kd, id_s, kk > 0);
-                    umma_ts(tbase + COL_S + b * BN, tbase + COL_QLO + kk * 8, kd, id_s, 1u);
+                    for (uint32_t kk = 0; kk < HD / 16; kk++) {
+                        const uint64_t kd = sdesc(k_addr + kk * 32, 16, 1024);
+                        umma_ts(tbase + COL_S + b * BN, tbase + COL_QHI + kk * 8, kd, id_s, kk > 0);
+                        if constexpr (BF16) umma_ts(tbase + COL_S + b * BN, tbase + COL_QLO + kk * 8, kd, id_s, 1u);
+                    }
+                    umma_commit(&B.s_full[b]);
+                    sj++;
+                    issued = 1;
+                    progressed = true;
                 }
-                umma_commit(&B.s_full[b]);
-                issued = 1;
-                if (j >= 1 && !issue_pv(j - 1)) break;
+                if (progressed) {
+                    idle_since = clock64();
+                } else if (*abort_flag) {
+                    ok = false;
+                } else if (clock64() - idle_since > kTimeoutCycles) {
+                    *abort_flag = 1;
+                    ok = false;
+                }
             }
-            if (ok && !*abort_flag) issue_pv(nkv - 1);
             if (*abort_flag && issued) {
                 umma_commit(&B.drain);
                 mbar_drain(&B.drain, 0);
@@ -370,43 +437,57 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
             for (int e = 0; e < 32; e++) split2<BF16>(x[2 * e], x[2 * e + 1], hi[e], lo[e]);
             tmem_st32(lane_addr + COL_QHI, hi);
-            tmem_st32(lane_addr + COL_QLO, lo);
+            if constexpr (BF16) tmem_st32(lane_addr + COL_QLO, lo);
             tmem_wait_st();
             fence_before();
-            mbar_arrive(&B.q_ready);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&B.q_ready);
         }
         const float c = P.scale_log2;
-        float m = -INFINITY, l = 0.0f;
+        float m = -INFINITY;
+        float2 l2 = make_float2(0.0f, 0.0f);   // row sum of P, two partial sums
         for (uint32_t j = 0; ok && j < nkv; j++) {
-            const uint32_t b = j & 1, sbuf = lane_addr + COL_S + b * BN;
-            if (!__all_sync(0xffffffffu, mbar_wait(&B.s_full[b], (j >> 1) & 1, abort_flag))) {
+            const uint32_t b = j % NB, sbuf = lane_addr + COL_S + b * BN;
+            if (!__all_sync(0xffffffffu, mbar_wait(&B.s_full[b], (j / NB) & 1, abort_flag))) {
                 ok = false;
                 break;
             }
             fence_after();
             const int lim = (int)qpos - (int)(j * BN);   // keys [0, lim] of this tile are visible
-            uint32_t sv[2][32];
-            tmem_ld32(sbuf, sv[0]);
-            tmem_ld32(sbuf + 32, sv[1]);
-            float tmax = -INFINITY;
+            const bool masked = !__all_sync(0xffffffffu, lim >= BN - 1);   // tile crosses the warp's diagonal
+            // Pass 1: the tile's row max (8 independent chains per 32 columns).
+            float mx[8];
 #pragma unroll
-            for (int c2 = 0; c2 < 2; c2++)
+            for (int k = 0; k < 8; k++) mx[k] = -INFINITY;
 #pragma unroll
-                for (int e = 0; e < 32; e++)
-                    if (c2 * 32 + e <= lim) tmax = fmaxf(tmax, __uint_as_float(sv[c2][e]));
-            tmax *= c;
-            const bool grow = (j == 0) || (tmax > m + 8.0f);
-            // O rescale when a row max grew: TMEM loads/stores are warp-wide, so
-            // the warp rescales when any of its rows needs it (factor 1 for the
-            // others), after PV_{j-1} has finished writing O.
+            for (int c2 = 0; c2 < BN / 32; c2++) {
+                uint32_t sv[32];
+                tmem_ld32(sbuf + 32 * c2, sv);
+                if (masked) {
+#pragma unroll
+                    for (int e = 0; e < 32; e++)
+                        if (c2 * 32 + e > lim) sv[e] = 0xff800000u;
+                }
+#pragma unroll
+                for (int e = 0; e < 32; e++) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(sv[e]));
+            }
+#pragma unroll
+            for (int w2 = 4; w2 > 0; w2 >>= 1)
+#pragma unroll
+                for (int k = 0; k < w2; k++) mx[k] = fmaxf(mx[k], mx[k + w2]);
+            const float tmax = mx[0] * c;
+            // Lazy rescale: keep the running max unless a row's max grew by more
+            // than 2^8; then O and l move to the new max (PV_{j-1} is done: S_j
+            // was issued after it).
+            const bool grow = j == 0 || tmax > m + 8.0f;
             if (j > 0 && __any_sync(0xffffffffu, grow)) {
-                if (!__all_sync(0xffffffffu, mbar_wait(&B.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag))) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&B.pv_done[(j - 1) % NB], ((j - 1) / NB) & 1, abort_flag))) {
                     ok = false;
                     break;
                 }
                 fence_after();
                 const float alpha = grow ? ex2(m - tmax) : 1.0f;
-                l *= alpha;
+                l2 = __fmul2_rn(l2, make_float2(alpha, alpha));
                 uint32_t ov[32];
 #pragma unroll
                 for (int h2 = 0; h2 < HD / 32; h2++) {
@@ -417,30 +498,29 @@ __global__ void __launch_bounds__(192, 2)
                 }
             }
             if (grow) m = tmax;
+            // Pass 2: P = 2^(S*c - m) in hi/lo pairs over the S columns.
 #pragma unroll
-            for (int c2 = 0; c2 < 2; c2++) {
-                uint32_t pk[32];
+            for (int c2 = 0; c2 < BN / 32; c2++) {
+                uint32_t sv[32];
+                tmem_ld32(sbuf + 32 * c2, sv);
+                if (masked) {
 #pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    const float s0 = (c2 * 32 + e <= lim) ? __uint_as_float(sv[c2][e]) : -INFINITY;
-                    const float s1 = (c2 * 32 + e + 1 <= lim) ? __uint_as_float(sv[c2][e + 1]) : -INFINITY;
-                    const float p0 = ex2(fmaf(s0, c, -m)), p1 = ex2(fmaf(s1, c, -m));
-                    l += p0 + p1;
-                    split2<BF16>(p0, p1, pk[e / 2], pk[16 + e / 2]);
+                    for (int e = 0; e < 32; e++)
+                        if (c2 * 32 + e > lim) sv[e] = 0xff800000u;
                 }
-                tmem_st32(sbuf + c2 * 32, pk);
+                write_p_chunk<BF16>(sv, sbuf + 32 * c2, c, m, l2);
             }
             tmem_wait_st();
             fence_before();
-            mbar_arrive(&B.p_full[b]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&B.p_full[b]);
         }
-        // O is final once the last two PVs (one per buffer) are done.
-        if (ok && nkv >= 2 &&
-            !__all_sync(0xffffffffu, mbar_wait(&B.pv_done[(nkv - 2) & 1], ((nkv - 2) >> 1) & 1, abort_flag)))
-            ok = false;
-        if (ok && __all_sync(0xffffffffu, mbar_wait(&B.pv_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, abort_flag))) {
+        // O is final once the last PV of every buffer is done.
+        for (uint32_t t = nkv > NB ? nkv - NB : 0; ok && t < nkv; t++)
+            if (!__all_sync(0xffffffffu, mbar_wait(&B.pv_done[t % NB], (t / NB) & 1, abort_flag))) ok = false;
+        if (ok) {
             fence_after();
-            const float inv_l = 1.0f / l;
+            const float inv_l = 1.0f / (l2.x + l2.y);
             const size_t obase = ((size_t)(w.tok_base + w.t0 + r) * P.n_heads + w.head) * HD;
 #pragma unroll
             for (int h2 = 0; h2 < HD / 32; h2++) {
