@@ -134,6 +134,18 @@ struct nd_attn {
     size_t spans_cap = 0;
     uint32_t *d_u32 = nullptr;
     size_t u32_cap = 0;
+    uint32_t *d_lean = nullptr;        // balanced grid: [tile prefix per token | first token per CTA]
+    size_t lean_cap = 0;
+    std::vector<uint32_t> lean_last;   // what d_lean holds (uploads skipped when unchanged)
+    int lean_occ[8] = {0};             // CTAs per SM of each (dtype, hd, nq) instantiation, 0 = not asked yet
+    std::vector<uint32_t> lean_up;     // host staging of the next d_lean image
+    std::vector<CUtensorMap> lean_kmap, lean_vmap;   // per layer, built on first use
+    std::vector<uint8_t> lean_map_ok;
+    uint32_t lean_parity = 0;          // half of counters / partials the next balanced launch uses
+    // Cache rows our most recently launched kernel may write: kNoLayer (none),
+    // a layer, or kAllLayers. A balanced launch may stream K/V before that
+    // kernel ends only when it cannot be writing the launch's layer.
+    int last_writer = -1;
     int *d_err = nullptr;
     void *pin = nullptr;
     size_t pin_cap = 0;
@@ -150,6 +162,11 @@ struct nd_attn {
 
 namespace {
 
+constexpr int kNoLayer = -1, kAllLayers = -2;
+
+// Records which cache rows the kernel about to be launched may write.
+inline void note_writer(nd_attn *h, int layer_or_none) { h->last_writer = layer_or_none; }
+
 int check_seq(const nd_attn *h, uint32_t seq) {
     if (!h) return fail(ND_ATTN_ERR_ARG, "null handle");
     if (seq >= h->cfg.max_seqs) return fail(ND_ATTN_ERR_RANGE, "sequence %u >= max_seqs %u", seq, h->cfg.max_seqs);
@@ -158,6 +175,7 @@ int check_seq(const nd_attn *h, uint32_t seq) {
 
 int push_state(nd_attn *h, uint32_t seq) {
     const HostSeq &s = h->seqs[seq];
+    note_writer(h, kNoLayer);
     set_state_kernel<<<1, 1, 0, h->stream>>>(h->d_state, seq, s.pos, s.n_sink);
     h->launches++;
     ND_CUDA(cudaGetLastError());
@@ -251,7 +269,8 @@ cudaError_t append_launch(const nd_attn *h, const AttnParams &P) {
 // splits than the scratch holds.
 void choose_split(const nd_attn *h, size_t items, uint32_t jmax, size_t rows, size_t counter_cap,
                   size_t part_slots, uint32_t *chunk, uint32_t *nsplit) {
-    const uint32_t per_iter = (uint32_t)nda::attend_rows_per_iter(h->cfg.kv_dtype, (int)h->cfg.v_head_dim);
+    const uint32_t per_iter = (uint32_t)nda::attend_rows_per_iter(h->cfg.kv_dtype, (int)h->cfg.v_head_dim,
+                                                                  nda::nq_for_rep(h->rep));
     const size_t target = (size_t)h->sm_count * 16;
     size_t c = (rows + target - 1) / target;
     c = std::max<size_t>(c, 2 * per_iter);
@@ -299,27 +318,195 @@ int upload_tok(nd_attn *h, const std::vector<TokMeta> &tok) {
     return ND_ATTN_OK;
 }
 
+int make_map(CUtensorMap *m, bool bf16, const void *base, uint64_t inner, uint64_t rows, uint64_t stride_bytes,
+             uint32_t box_rows, uint32_t box_inner, bool swizzle);
+
+// The balanced TMA-staged attend covers 16-bit caches with equal head dims of
+// 64 or 128 (GQA width <= 4 at 128), calls in which no position wraps the
+// ring, and pages (if any) holding whole 64-row boxes.
+bool lean_ok(const nd_attn *h, bool no_wrap) {
+    const nd_attn_config &cf = h->cfg;
+    const int nq = nda::nq_for_rep(h->rep);
+    return no_wrap && (cf.kv_dtype == ND_DT_F16 || cf.kv_dtype == ND_DT_BF16) && cf.qk_head_dim == cf.v_head_dim &&
+           (cf.qk_head_dim == 64 || (cf.qk_head_dim == 128 && nq <= 4)) &&
+           (cf.block_size == 0 || cf.block_size % (uint32_t)nda::kTmaRows == 0) && h->rows_per_layer < 0x7fffffffu;
+}
+
+// Balanced-launch tuning: share of the tiles in static units (percent), least
+// tiles per dynamic unit, dynamic units a producer holds ahead.
+constexpr uint64_t kLeanStaticPct = 75, kLeanUnitMin = 2;
+constexpr uint32_t kLeanAhead = 2;
+
+// Balanced launch: item (t, g) holds T_t = max(1, ceil((vis[t] - fuse_append)
+// / 64)) tiles (the newest row of a fused append is not in the TMA stream).
+// G = the CTAs the GPU holds at once; the NT tiles of the call become G
+// static units of S ~ 3/4 NT / G tiles, then dynamic units of CH tiles (at
+// most ~4 per CTA) that CTAs take as they run dry. Each unit needs two
+// partial slots and one ticket; two more counters drive the unit queue.
+int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, const nda::SeqSpan *d_spans,
+             uint32_t n_spans, const std::vector<uint32_t> &vis, const std::vector<uint32_t> &tok_seq,
+             const std::vector<uint32_t> &tok_pos, int fuse_append, const void *q, const void *k, const void *v,
+             const void *gate, void *out) {
+    const nd_attn_config &cf = h->cfg;
+    const uint32_t n_kv = cf.n_kv_heads, hd = cf.qk_head_dim;
+    const int nq = nda::nq_for_rep(h->rep);
+    const bool bf16 = cf.kv_dtype == ND_DT_BF16;
+    auto launch = [&](const void *km, const void *vm, const nda::AttnParams &P, int *occ) {
+        return bf16 ? nda::attend_lean_launch_bf16((int)hd, nq, km, vm, P, occ, h->stream)
+                    : nda::attend_lean_launch_f16((int)hd, nq, km, vm, P, occ, h->stream);
+    };
+    int &occ = h->lean_occ[(bf16 ? 4 : 0) + (nq == 1 ? 0 : nq == 2 ? 1 : nq == 4 ? 2 : 3)];
+    AttnParams P = base_params(h, layer);
+    if (occ <= 0) {
+        int b = 0;
+        ND_CUDA(launch(nullptr, nullptr, P, &b));
+        if (b <= 0) return fail(ND_ATTN_ERR_CUDA, "balanced attend kernel does not fit on an SM");
+        occ = b;
+    }
+    // Plan: per token {first tile, tiles per item, sequence, position} (and a
+    // sentinel), then per unit the walk state at its first tile.
+    std::vector<uint32_t> &up = h->lean_up;
+    up.assign((size_t)(ntok + 1) * 4, 0u);
+    uint64_t nt = 0;
+    for (uint32_t t = 0; t < ntok; t++) {
+        const uint32_t rows = vis[t] - (fuse_append ? 1u : 0u);
+        const uint32_t T = std::max<uint32_t>(1u, (rows + nda::kTmaRows - 1) / nda::kTmaRows);
+        up[4 * t + 0] = (uint32_t)nt;
+        up[4 * t + 1] = T;
+        up[4 * t + 2] = tok_seq[t];
+        up[4 * t + 3] = tok_pos[t];
+        nt += (uint64_t)n_kv * T;
+        if (nt > 0x7fffffffu) return fail(ND_ATTN_ERR_RANGE, "launch too large");
+    }
+    up[4 * ntok] = (uint32_t)nt;
+    // Launches alternate between two halves of the tickets and of the partial
+    // scratch (two consecutive launches may overlap). Unit budget per half:
+    // tickets [0, NU) plus the two queue counters, 2 NU partial slots.
+    const size_t cnt_half = h->counter_cap / 2, slot_half = h->part_slots / 2;
+    const uint64_t budget = std::min<uint64_t>(cnt_half - 2, slot_half / 2);
+    const uint64_t G = std::min<uint64_t>({nt, (uint64_t)h->sm_count * (uint64_t)occ, budget});
+    const uint64_t S = std::max<uint64_t>(1, nt * kLeanStaticPct / (100 * G));
+    const uint64_t dyn = nt - G * S;
+    uint64_t CH = std::max<uint64_t>(kLeanUnitMin, (dyn + 4 * G - 1) / (4 * G));
+    while (G + (dyn + CH - 1) / CH > budget) CH *= 2;
+    const uint64_t NU = G + (dyn + CH - 1) / CH;
+    const size_t ub = up.size();
+    up.resize(ub + NU * 8, 0u);
+    for (uint64_t u = 0, t = 0; u < NU; u++) {
+        const uint64_t x0 = u < G ? u * S : G * S + (u - G) * CH;
+        while (up[4 * (t + 1)] <= x0) t++;
+        const uint32_t T = up[4 * t + 1], r = (uint32_t)(x0 - up[4 * t]);
+        uint32_t *e = &up[ub + 8 * u];
+        e[0] = (uint32_t)t, e[1] = r / T, e[2] = r % T, e[3] = T;
+        e[4] = up[4 * t], e[5] = up[4 * t + 2], e[6] = up[4 * t + 3];
+    }
+    if (up != h->lean_last) {
+        int rc = grow(&h->d_lean, &h->lean_cap, up.size());
+        if (rc) return rc;
+        ND_CUDA(cudaMemcpyAsync(h->d_lean, up.data(), up.size() * sizeof(uint32_t), cudaMemcpyHostToDevice,
+                                h->stream));
+        h->lean_last = up;
+    }
+    P.lean_ahead = kLeanAhead;
+    P.lean_s = (uint32_t)S;
+    P.lean_ch = (uint32_t)CH;
+    P.n_units = (uint32_t)NU;
+    P.work_slot = (uint32_t)(cnt_half - 2);
+    const uint32_t par = h->lean_parity;
+    h->lean_parity ^= 1u;
+    P.counters = h->counters + par * cnt_half;
+    P.part_o = h->part_o + par * slot_half * nq * hd;
+    P.part_ml = h->part_ml + par * slot_half * nq * 2;
+    P.early_kv = h->last_writer == kNoLayer || (h->last_writer >= 0 && h->last_writer != (int)layer);
+    P.q = q; P.k = k; P.v = v; P.gate = gate; P.out = out;
+    P.tok = d_tok;
+    P.spans = d_spans;
+    P.n_spans = n_spans;
+    P.n_tok = ntok;
+    P.split_cu = h->d_lean;
+    P.cta_tok = h->d_lean + (size_t)(ntok + 1) * 4;
+    P.n_cta = (uint32_t)G;
+    P.n_tiles = (uint32_t)nt;
+    P.fuse_append = fuse_append;
+    if (h->lean_map_ok.size() != cf.n_layers) {
+        h->lean_kmap.resize(cf.n_layers);
+        h->lean_vmap.resize(cf.n_layers);
+        h->lean_map_ok.assign(cf.n_layers, 0);
+    }
+    if (!h->lean_map_ok[layer]) {   // the layer's cache never moves: encode its maps once
+        int rc = make_map(&h->lean_kmap[layer], bf16, P.c.k, h->k_dim, h->rows_per_layer, (uint64_t)h->k_dim * 2,
+                          nda::kTmaRows, hd, false);
+        if (!rc) rc = make_map(&h->lean_vmap[layer], bf16, P.c.v, h->v_dim, h->rows_per_layer,
+                               (uint64_t)h->v_dim * 2, nda::kTmaRows, hd, false);
+        if (rc) return rc;
+        h->lean_map_ok[layer] = 1;
+    }
+    note_writer(h, fuse_append ? (int)layer : kNoLayer);
+    ND_CUDA(launch(&h->lean_kmap[layer], &h->lean_vmap[layer], P, nullptr));
+    h->launches++;
+    return ND_ATTN_OK;
+}
+
 // One attend launch over `ntok` query tokens mapped by d_tok, or d_spans, or
-// identity; jmax / rows: longest visit run and total visited rows (x KV heads).
+// identity. vis[t] = visited positions of token t. The grid is exact: token t
+// gets nsplit_t = ceil(vis[t] / C) splits (C sized so the call fills the GPU
+// about twice over), uploaded as a prefix sum; no CTA starts without work.
+// tok_seq / tok_pos (host copies of each token's sequence and position) are
+// given where no position of the call wraps the ring, else null.
 int run_attend(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, const nda::SeqSpan *d_spans,
-               uint32_t n_spans, uint32_t jmax, size_t rows, int fuse_append, const void *q, const void *k,
-               const void *v, const void *gate, void *out) {
+               uint32_t n_spans, const std::vector<uint32_t> &vis, int fuse_append, const void *q, const void *k,
+               const void *v, const void *gate, void *out, const std::vector<uint32_t> *tok_seq,
+               const std::vector<uint32_t> *tok_pos) {
     const uint32_t n_kv = h->cfg.n_kv_heads;
+    if (tok_seq && tok_pos && lean_ok(h, true))
+        return run_lean(h, layer, ntok, d_tok, d_spans, n_spans, vis, *tok_seq, *tok_pos, fuse_append, q, k, v,
+                        gate, out);
     const size_t items = (size_t)ntok * n_kv;
-    uint32_t chunk, nsplit;
-    choose_split(h, items, std::max(jmax, 1u), rows, h->counter_cap, h->part_slots, &chunk, &nsplit);
-    if (items > 0x7fffffffu || nsplit > 65535u) return fail(ND_ATTN_ERR_RANGE, "launch too large");
+    if (items > 0x7fffffffu) return fail(ND_ATTN_ERR_RANGE, "launch too large");
+    size_t rows = 0;
+    uint32_t jmax = 1;
+    for (uint32_t t = 0; t < ntok; t++) {
+        rows += vis[t];
+        jmax = std::max(jmax, vis[t]);
+    }
+    const uint32_t rpi = (uint32_t)nda::attend_rows_per_iter(h->cfg.kv_dtype, (int)h->cfg.v_head_dim,
+                                                             nda::nq_for_rep(h->rep));
+    size_t C = std::max<size_t>((rows * n_kv + (size_t)h->sm_count * 12 - 1) / ((size_t)h->sm_count * 12),
+                                (size_t)2 * rpi);
+    // The scratch holds max_split partials per (token, KV head); grow C until it fits.
+    uint32_t max_split = 1;
+    std::vector<uint32_t> cu(ntok + 1, 0);
+    for (int attempt = 0; attempt < 64; attempt++) {
+        max_split = 1;
+        for (uint32_t t = 0; t < ntok; t++) {
+            const uint32_t ns = (uint32_t)std::max<size_t>(1, (vis[t] + C - 1) / C);
+            cu[t + 1] = cu[t] + ns;
+            max_split = std::max(max_split, ns);
+        }
+        if (max_split == 1 || (items <= h->counter_cap && items * max_split <= h->part_slots)) break;
+        C *= 2;
+    }
+    if (max_split > 1 && (items > h->counter_cap || items * max_split > h->part_slots)) {
+        max_split = 1;   // no split at all: one CTA per (token, KV head)
+        for (uint32_t t = 0; t < ntok; t++) cu[t + 1] = cu[t] + 1;
+    }
+    if (cu[ntok] > 0x7fffffffu) return fail(ND_ATTN_ERR_RANGE, "launch too large");
+    int rc = grow(&h->d_u32, &h->u32_cap, (size_t)ntok + 1);
+    if (rc) return rc;
+    ND_CUDA(cudaMemcpyAsync(h->d_u32, cu.data(), (ntok + 1) * sizeof(uint32_t), cudaMemcpyHostToDevice, h->stream));
     AttnParams P = base_params(h, layer);
     P.q = q; P.k = k; P.v = v; P.gate = gate; P.out = out;
     P.tok = d_tok;
     P.spans = d_spans;
     P.n_spans = n_spans;
     P.n_tok = ntok;
-    P.chunk = chunk;
-    P.max_splits = nsplit;
+    P.max_splits = max_split;
+    P.split_cu = h->d_u32;
     P.fuse_append = fuse_append;
-    ND_CUDA(attend_launch(h, P, dim3((unsigned)items, nsplit, 1)));
+    note_writer(h, fuse_append ? (int)layer : kNoLayer);
+    ND_CUDA(attend_launch(h, P, dim3(cu[ntok], n_kv, 1)));
     h->launches++;
+    (void)jmax;
     return ND_ATTN_OK;
 }
 
@@ -356,16 +543,17 @@ EncodeTiledFn encode_tiled() {
 // 2D map over rows of `inner` 16-bit elements (row stride `stride_bytes`), box
 // 64 elements x box_rows rows, 128-byte swizzle, out-of-range rows read as zero.
 int make_map(CUtensorMap *m, bool bf16, const void *base, uint64_t inner, uint64_t rows, uint64_t stride_bytes,
-             uint32_t box_rows) {
+             uint32_t box_rows, uint32_t box_inner, bool swizzle) {
     EncodeTiledFn fn = encode_tiled();
     if (!fn) return fail(ND_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     const cuuint64_t dims[2] = {inner, rows};
     const cuuint64_t strides[1] = {stride_bytes};
-    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint32_t box[2] = {box_inner, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                           const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(ND_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return ND_ATTN_OK;
@@ -422,9 +610,9 @@ int run_prefill_tc(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
     const bool bf16 = c.kv_dtype == ND_DT_BF16;
     CUtensorMap qm, km, vm;
     CacheView cv = layer_view(h, layer);
-    int rc = make_map(&qm, bf16, q, (uint64_t)c.n_heads * 64, total, (uint64_t)c.n_heads * 64 * 2, 128);
-    if (!rc) rc = make_map(&km, bf16, cv.k, h->k_dim, h->rows_per_layer, (uint64_t)h->k_dim * 2, 64);
-    if (!rc) rc = make_map(&vm, bf16, cv.v, h->v_dim, h->rows_per_layer, (uint64_t)h->v_dim * 2, 64);
+    int rc = make_map(&qm, bf16, q, (uint64_t)c.n_heads * 64, total, (uint64_t)c.n_heads * 64 * 2, 128, 64, true);
+    if (!rc) rc = make_map(&km, bf16, cv.k, h->k_dim, h->rows_per_layer, (uint64_t)h->k_dim * 2, 64, 64, true);
+    if (!rc) rc = make_map(&vm, bf16, cv.v, h->v_dim, h->rows_per_layer, (uint64_t)h->v_dim * 2, 64, 64, true);
     if (rc) return rc;
     nda::PrefillTcParams P;
     P.work = h->d_work;
@@ -439,6 +627,7 @@ int run_prefill_tc(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
     P.window = c.window;
     P.scale_log2 = 1.4426950408889634f / sqrtf((float)c.qk_head_dim);
     P.err = h->d_err;
+    note_writer(h, kNoLayer);
     ND_CUDA(nda::prefill_tc_launch(bf16, &qm, &km, &vm, P, h->n_work, h->stream));
     h->launches++;
     return ND_ATTN_OK;
@@ -446,10 +635,10 @@ int run_prefill_tc(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
 
 }  // namespace
 
-int nda::attend_rows_per_iter(int kv_dt, int vd) {
+int nda::attend_rows_per_iter(int kv_dt, int vd, int nq) {
     const int es = kv_dt == ND_DT_I8 ? 1 : kv_dt == ND_DT_F32 ? 4 : 2;
     const int lpr = vd * es / 16;
-    return 4 * 4 * (32 / lpr);
+    return 4 * 4 * (32 / lpr) + 0 * nq;   // warps x row groups x rows per warp load
 }
 
 // ============================================================ C ABI
@@ -575,7 +764,10 @@ int nd_attn_open(const nd_attn_config *cfg_in, nd_attn **out) {
     {
         const size_t nq = (size_t)nda::nq_for_rep(h->rep);
         const size_t per_slot = nq * (cfg.v_head_dim + 2) * sizeof(float);
-        h->counter_cap = (size_t)cfg.max_seqs * cfg.n_kv_heads;
+        // Tickets for every (sequence, KV head) of a full decode, and, in each
+        // of two halves, for every unit of a balanced launch (at most 5 per
+        // CTA, 16 CTAs per SM).
+        h->counter_cap = std::max<size_t>((size_t)cfg.max_seqs * cfg.n_kv_heads, (size_t)h->sm_count * 160);
         h->part_slots = std::max<size_t>(h->counter_cap * 4, (64ull << 20) / per_slot);
         if (cudaMalloc(&h->part_o, h->part_slots * nq * cfg.v_head_dim * sizeof(float)) != cudaSuccess ||
             cudaMalloc(&h->part_ml, h->part_slots * nq * 2 * sizeof(float)) != cudaSuccess ||
@@ -596,7 +788,7 @@ void nd_attn_close(nd_attn *h) {
     cudaFree(h->kc); cudaFree(h->vc); cudaFree(h->ks); cudaFree(h->vs);
     cudaFree(h->rope); cudaFree(h->norms); cudaFree(h->d_state); cudaFree(h->d_btab);
     cudaFree(h->part_o); cudaFree(h->part_ml); cudaFree(h->counters);
-    cudaFree(h->d_tok); cudaFree(h->d_u32); cudaFree(h->d_err); cudaFree(h->dio); cudaFree(h->d_work); cudaFree(h->d_spans);
+    cudaFree(h->d_tok); cudaFree(h->d_u32); cudaFree(h->d_lean); cudaFree(h->d_err); cudaFree(h->dio); cudaFree(h->d_work); cudaFree(h->d_spans);
     if (h->pin) cudaFreeHost(h->pin);
     if (h->own) cudaStreamDestroy(h->own);
     delete h;
@@ -679,6 +871,7 @@ int nd_attn_advance(nd_attn *h, uint32_t n, const uint32_t *seq_ids, const uint3
         }
     }
     for (uint32_t i = 0; i < n; i++) h->seqs[seq_ids ? seq_ids[i] : i].pos += len ? len[i] : 1;
+    note_writer(h, kNoLayer);
     advance_kernel<<<(n + 127) / 128, 128, 0, h->stream>>>(h->d_state, n, d_ids, d_len, 1);
     h->launches++;
     ND_CUDA(cudaGetLastError());
@@ -709,13 +902,14 @@ int nd_attn_decode(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
     if (rc) return rc;
     if (!q || !k || !v || !out) return fail(ND_ATTN_ERR_ARG, "null tensor");
     DeviceGuard dg(h->cfg.device);
-    uint32_t jmax = 1;
-    size_t rows = 0;
+    std::vector<uint32_t> vis(n), tseq(n), tpos(n);
+    bool no_wrap = true;
     for (uint32_t i = 0; i < n; i++) {
-        const HostSeq &s = h->seqs[seq_ids ? seq_ids[i] : i];
-        const uint32_t j = visit_count(s.pos, s.n_sink, h->cfg.window);
-        jmax = std::max(jmax, j);
-        rows += (size_t)j * h->cfg.n_kv_heads;
+        tseq[i] = seq_ids ? seq_ids[i] : i;
+        const HostSeq &s = h->seqs[tseq[i]];
+        vis[i] = visit_count(s.pos, s.n_sink, h->cfg.window);
+        tpos[i] = s.pos;
+        no_wrap = no_wrap && s.pos < h->cfg.window;
     }
     const TokMeta *d_tok = nullptr;
     if (seq_ids) {
@@ -725,7 +919,8 @@ int nd_attn_decode(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
         if (rc) return rc;
         d_tok = h->d_tok;
     }
-    return run_attend(h, layer, n, d_tok, nullptr, 0, jmax, rows, 1, q, k, v, gate, out);
+    return run_attend(h, layer, n, d_tok, nullptr, 0, vis, 1, q, k, v, gate, out, no_wrap ? &tseq : nullptr,
+                      no_wrap ? &tpos : nullptr);
 }
 
 int nd_attn_prefill(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const uint32_t *len,
@@ -754,15 +949,10 @@ int nd_attn_prefill(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_
         // overwritten: append all tokens, then attend causally.
         std::vector<nda::SeqSpan> spans;
         spans.reserve(n);
-        uint32_t jmax = 1;
-        size_t rows = 0;
         for (uint32_t i = 0; i < n; i++) {
             const uint32_t s = seq_ids ? seq_ids[i] : i;
             if (!len[i]) continue;
             spans.push_back(nda::SeqSpan{s, cu[i], len[i]});
-            const uint64_t p0 = h->seqs[s].pos, L = len[i];
-            jmax = std::max<uint32_t>(jmax, (uint32_t)(p0 + L));
-            rows += (size_t)((L * p0 + L * (L + 1) / 2) * h->cfg.n_kv_heads);   // positions 0..p0+t per token
         }
         rc = grow(&h->d_spans, &h->spans_cap, spans.size());
         if (rc) return rc;
@@ -770,30 +960,38 @@ int nd_attn_prefill(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_
                                 cudaMemcpyHostToDevice, h->stream));
         AttnParams P = base_params(h, layer);
         P.k = k; P.v = v; P.spans = h->d_spans; P.n_spans = (uint32_t)spans.size(); P.n_tok = (uint32_t)total;
+        note_writer(h, (int)layer);
         ND_CUDA(append_launch(h, P));
         h->launches++;
         if (tc_prefill_ok(h, q)) return run_prefill_tc(h, layer, n, seq_ids, len, cu, total, q, gate, out);
-        return run_attend(h, layer, (uint32_t)total, nullptr, h->d_spans, (uint32_t)spans.size(), jmax, rows, 0, q,
-                          k, v, gate, out);
+        std::vector<uint32_t> vis(total), tseq(total), tpos(total);
+        for (uint32_t i = 0; i < n; i++) {
+            const uint32_t s = seq_ids ? seq_ids[i] : i;
+            for (uint32_t t = 0; t < len[i]; t++) {
+                vis[cu[i] + t] = h->seqs[s].pos + t + 1;   // no wrap: [0, pos]
+                tseq[cu[i] + t] = s;
+                tpos[cu[i] + t] = h->seqs[s].pos + t;
+            }
+        }
+        return run_attend(h, layer, (uint32_t)total, nullptr, h->d_spans, (uint32_t)spans.size(), vis, 0, q, k, v,
+                          gate, out, &tseq, &tpos);
     }
     // The ring wraps inside this call: a later token's slot can hold a position
     // an earlier token still reads, so run the reference's token-at-a-time
     // order (append, then attend) step by step.
     for (uint32_t t = 0; t < maxlen; t++) {
         std::vector<TokMeta> tok;
-        uint32_t jmax = 1;
-        size_t rows = 0;
+        std::vector<uint32_t> vis;
         for (uint32_t i = 0; i < n; i++) {
             if (t >= len[i]) continue;
             const uint32_t s = seq_ids ? seq_ids[i] : i;
             tok.push_back(TokMeta{s, t, cu[i] + t});
-            const uint32_t j = visit_count(h->seqs[s].pos + t, h->seqs[s].n_sink, W);
-            jmax = std::max(jmax, j);
-            rows += (size_t)j * h->cfg.n_kv_heads;
+            vis.push_back(visit_count(h->seqs[s].pos + t, h->seqs[s].n_sink, W));
         }
         rc = upload_tok(h, tok);
         if (rc) return rc;
-        rc = run_attend(h, layer, (uint32_t)tok.size(), h->d_tok, nullptr, 0, jmax, rows, 1, q, k, v, gate, out);
+        rc = run_attend(h, layer, (uint32_t)tok.size(), h->d_tok, nullptr, 0, vis, 1, q, k, v, gate, out, nullptr,
+                        nullptr);
         if (rc) return rc;
     }
     return ND_ATTN_OK;
@@ -934,6 +1132,7 @@ int nd_attn_decode_noalloc(nd_attn *h, uint32_t layer, uint32_t n, const void *q
     const size_t ml_bytes = (slots * nq * 2 * sizeof(float) + 255) / 256 * 256;
     P.part_o = reinterpret_cast<float *>(base + ticket_bytes + ml_bytes);
     if (nsplit > 1) ND_CUDA(cudaMemsetAsync(P.counters, 0, items * sizeof(int), h->stream));
+    note_writer(h, (int)layer);
     ND_CUDA(attend_launch(h, P, dim3((unsigned)items, nsplit, 1)));
     h->launches++;
     return ND_ATTN_OK;
@@ -964,6 +1163,7 @@ nd_attn_prefix *nd_attn_prefix_save(nd_attn *h, uint32_t seq) {
     char *dst = static_cast<char *>(p->dev);
     struct Part { void *base; size_t row; } parts[4] = {{h->kc, krow}, {h->vc, vrow}, {h->ks, srow}, {h->vs, srow}};
     for (int i = 0; i < (sc ? 4 : 2); i++) {
+        note_writer(h, kAllLayers);
         rows_copy_kernel<<<dim3(std::min<uint32_t>(live, 1024u), c.n_layers), 128, 0, h->stream>>>(
             static_cast<char *>(parts[i].base), h->rows_per_layer * parts[i].row, dst, live * parts[i].row,
             (uint32_t)(parts[i].row / 4), live, cv, seq, 0, 0);
@@ -994,6 +1194,7 @@ int nd_attn_prefix_restore(nd_attn *h, uint32_t seq, const nd_attn_prefix *p) {
     char *src = static_cast<char *>(p->dev);
     struct Part { void *base; size_t row; } parts[4] = {{h->kc, krow}, {h->vc, vrow}, {h->ks, srow}, {h->vs, srow}};
     for (int i = 0; i < (sc ? 4 : 2); i++) {
+        note_writer(h, kAllLayers);
         rows_copy_kernel<<<dim3(std::min<uint32_t>(p->live, 1024u), c.n_layers), 128, 0, h->stream>>>(
             static_cast<char *>(parts[i].base), h->rows_per_layer * parts[i].row, src, p->live * parts[i].row,
             (uint32_t)(parts[i].row / 4), p->live, cv, seq, 0, 1);
@@ -1054,6 +1255,7 @@ static int cache_io(nd_attn *h, uint32_t layer, uint32_t seq, uint32_t slot0, ui
         if (!parts[i].user) continue;
         const size_t nb = n_slots * parts[i].row;
         char *dense = to_cache ? static_cast<char *>(parts[i].user) : d + off;
+        note_writer(h, kAllLayers);
         rows_copy_kernel<<<dim3(std::min<uint32_t>(n_slots, 4096u), 1), 128, 0, h->stream>>>(
             static_cast<char *>(parts[i].cache), 0, dense, 0, (uint32_t)(parts[i].row / 4), n_slots, cv, seq,
             slot0, to_cache);

@@ -28,6 +28,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 namespace nda {
 
 enum : int { DT_I8 = 0, DT_F32 = 1, DT_F16 = 2, DT_BF16 = 3 };
@@ -74,8 +76,16 @@ struct AttnParams {
     uint32_t n_spans;            //   token i = sequence i, offset 0, row i
     uint32_t n_tok, n_heads, rep;
     float scale_log2;            // log2(e) / sqrtf(qk_hd)
-    uint32_t chunk;              // visit rows per split
+    uint32_t chunk;              // visit rows per split (implicit grid)
     uint32_t max_splits;         // split stride of the scratch
+    const uint32_t *split_cu;    // exact grid: prefix sum of splits per token (n_tok+1), or nullptr;
+                                 //   balanced grid: n_kv x prefix sum of 64-row tiles per token
+    const uint32_t *cta_tok;     // balanced grid: token holding each unit's first tile
+    uint32_t n_cta, n_tiles;     // balanced grid: CTAs, tiles of the call
+    uint32_t lean_s, lean_ch;    // balanced grid: tiles per static unit, per dynamic unit
+    uint32_t n_units, work_slot; // balanced grid: units; counters[work_slot..+1] = unit / done counters
+    uint32_t lean_ahead;         // balanced grid: dynamic units a producer holds ahead (1..4)
+    int early_kv;                // balanced grid: K/V may be streamed before the previous kernel ends
     int fuse_append;
     float *part_o, *part_ml;
     int *counters;
@@ -231,6 +241,45 @@ __device__ __forceinline__ void warp_norm_rope(RopePairs<QK> &x, const float2 *c
         const int i = lane + 32 * c;
         if (i < HALF) {
             const float2 t = cs[i];
+            const float a = x.a[c], b = x.b[c];
+            x.a[c] = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(b, t.y));
+            x.b[c] = __fadd_rn(__fmul_rn(b, t.x), __fmul_rn(a, t.y));
+        }
+    }
+}
+
+// Same, with this lane's (cos, sin) pairs already loaded: csv[c] belongs to
+// pair lane + 32 c.
+template <int QK>
+__device__ __forceinline__ void warp_norm_rope_v(RopePairs<QK> &x, const float2 (&csv)[RopePairs<QK>::PPL],
+                                                 const float *norm, int lane) {
+    constexpr int HALF = QK / 2;
+    constexpr int PPL = RopePairs<QK>::PPL;
+    static_assert(QK % 2 == 0, "even head dim");
+    if (norm) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < QK; i++) {
+            const int ii = i < HALF ? i : i - HALF;
+            const float xi = i < HALF ? __shfl_sync(0xffffffffu, x.a[ii / 32], ii % 32)
+                                      : __shfl_sync(0xffffffffu, x.b[ii / 32], ii % 32);
+            ss = __fadd_rn(ss, __fmul_rn(xi, xi));
+        }
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)QK), 1e-6f)));
+#pragma unroll
+        for (int c = 0; c < PPL; c++) {
+            const int i = lane + 32 * c;
+            if (i < HALF) {
+                x.a[c] = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, norm[i]), x.a[c]), inv);
+                x.b[c] = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, norm[i + HALF]), x.b[c]), inv);
+            }
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < PPL; c++) {
+        const int i = lane + 32 * c;
+        if (i < HALF) {
+            const float2 t = csv[c];
             const float a = x.a[c], b = x.b[c];
             x.a[c] = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(b, t.y));
             x.b[c] = __fadd_rn(__fmul_rn(b, t.x), __fmul_rn(a, t.y));
@@ -536,6 +585,106 @@ __device__ __forceinline__ void consume(const float (&qr)[NQ][AttendShape<QK, VD
     }
 }
 
+// Merge of one CTA's warps and of the splits of a (token, KV head): warps
+// 0..NW-1 hold per-warp (m, l, acc) over the rows they consumed; every thread
+// of the CTA calls this (the barriers are CTA-wide), threads of warps >= NW
+// only take part in the barriers. With one split the CTA writes the output;
+// otherwise it writes its partial and the last CTA to take a ticket merges all
+// splits (nothing waits for anything).
+template <int QK, int VD, typename KVT, int NQ, int NW>
+__device__ __forceinline__ void attend_finish(const AttnParams &P, float (&m)[NQ], float (&l)[NQ],
+                                              float (&acc)[NQ][AttendShape<QK, VD, KVT, NQ>::EV],
+                                              float (*sm_o)[NQ][VD], float (*sm_m)[NQ], float (*sm_l)[NQ],
+                                              int *s_last_p, uint32_t item, uint32_t split, uint32_t nsplit,
+                                              uint32_t g, uint32_t out_row, int tid) {
+    using S = AttendShape<QK, VD, KVT, NQ>;
+    constexpr int LPR = S::LPR, EV = S::EV;
+    const int lane = tid & 31, warp = tid >> 5, sub = lane % LPR, rl = lane / LPR;
+    const uint32_t rep = P.rep;
+    int &s_last = *s_last_p;
+    // Reduce across the row lanes of the warp (m is warp-uniform).
+#pragma unroll
+    for (int qi = 0; qi < NQ; qi++) {
+#pragma unroll
+        for (int o = LPR; o < 32; o <<= 1) {
+            l[qi] += __shfl_xor_sync(0xffffffffu, l[qi], o);
+#pragma unroll
+            for (int e = 0; e < EV; e++) acc[qi][e] += __shfl_xor_sync(0xffffffffu, acc[qi][e], o);
+        }
+    }
+    if (warp < NW && rl == 0) {
+#pragma unroll
+        for (int qi = 0; qi < NQ; qi++)
+#pragma unroll
+            for (int e = 0; e < EV; e++) sm_o[warp][qi][sub * EV + e] = acc[qi][e];
+    }
+    if (warp < NW && lane == 0) {
+#pragma unroll
+        for (int qi = 0; qi < NQ; qi++) {
+            sm_m[warp][qi] = m[qi];
+            sm_l[warp][qi] = l[qi];
+        }
+    }
+    __syncthreads();
+
+    const size_t out_base = (size_t)out_row * P.n_heads;
+    const size_t part_base = ((size_t)item * P.max_splits + split) * NQ;
+    for (int idx = tid; tid < NW * 32 && idx < (int)rep * VD; idx += NW * 32) {
+        const int qi = idx / VD, d = idx % VD;
+        float M = sm_m[0][qi];
+#pragma unroll
+        for (int w = 1; w < NW; w++) M = fmaxf(M, sm_m[w][qi]);
+        float o = 0.0f, L = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; w++) {
+            const float f = ex2(sm_m[w][qi] - M);
+            o += sm_o[w][qi][d] * f;
+            L += sm_l[w][qi] * f;
+        }
+        if (nsplit == 1) {
+            const uint32_t h = g * rep + qi;
+            float val = o / L;
+            if (P.gate) val *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, (out_base + h) * VD + d) *
+                                                 1.4426950408889634f));
+            act_store(P.out, P.out_dt, (out_base + h) * VD + d, val);
+        } else {
+            P.part_o[(part_base + qi) * VD + d] = o;
+            if (d == 0) {
+                P.part_ml[(part_base + qi) * 2 + 0] = M;
+                P.part_ml[(part_base + qi) * 2 + 1] = L;
+            }
+        }
+    }
+    if (nsplit == 1) return;
+
+    // Last CTA of this (token, group) merges the splits. No CTA ever waits.
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&P.counters[item], 1) == (int)nsplit - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const size_t item_base = (size_t)item * P.max_splits * NQ;
+    for (int idx = tid; tid < NW * 32 && idx < (int)rep * VD; idx += NW * 32) {
+        const int qi = idx / VD, d = idx % VD;
+        float M = -INFINITY;
+        for (uint32_t s = 0; s < nsplit; s++)
+            M = fmaxf(M, __ldcg(&P.part_ml[(item_base + (size_t)s * NQ + qi) * 2]));
+        float o = 0.0f, L = 0.0f;
+        for (uint32_t s = 0; s < nsplit; s++) {
+            const size_t b = item_base + (size_t)s * NQ + qi;
+            const float f = ex2(__ldcg(&P.part_ml[b * 2]) - M);
+            o += __ldcg(&P.part_o[b * VD + d]) * f;
+            L += __ldcg(&P.part_ml[b * 2 + 1]) * f;
+        }
+        const uint32_t h = g * rep + qi;
+        float val = o / L;
+        if (P.gate) val *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, (out_base + h) * VD + d) *
+                                             1.4426950408889634f));
+        act_store(P.out, P.out_dt, (out_base + h) * VD + d, val);
+    }
+    if (tid == 0) P.counters[item] = 0;
+}
 template <int QK, int VD, typename KVT, int NQ>
 __global__ void __launch_bounds__(128) attend_kernel(const AttnParams P) {
     using S = AttendShape<QK, VD, KVT, NQ>;
@@ -551,9 +700,25 @@ __global__ void __launch_bounds__(128) attend_kernel(const AttnParams P) {
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int sub = lane % LPR, rl = lane / LPR;
-    const uint32_t item = blockIdx.x, split = blockIdx.y;
     const uint32_t n_kv = P.c.n_kv, W = P.c.window;
-    const uint32_t tok = item / n_kv, g = item % n_kv;
+    uint32_t tok, g, split;
+    if (P.split_cu) {
+        // Exact grid: blockIdx.x enumerates the (token, split) pairs of the call.
+        uint32_t lo = 0, hi = P.n_tok;
+        while (hi - lo > 1) {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (P.split_cu[mid] <= blockIdx.x) lo = mid;
+            else hi = mid;
+        }
+        tok = lo;
+        split = blockIdx.x - P.split_cu[lo];
+        g = blockIdx.y;
+    } else {
+        tok = blockIdx.x / n_kv;
+        g = blockIdx.x % n_kv;
+        split = blockIdx.y;
+    }
+    const uint32_t item = tok * n_kv + g;
     const TokMeta tm = token_meta(P, tok);
     const SeqState st = P.state[tm.seq];
     const uint32_t pos = st.pos + tm.off, n_sink = st.n_sink;
@@ -563,10 +728,17 @@ __global__ void __launch_bounds__(128) attend_kernel(const AttnParams P) {
     }
     const Runs runs = make_runs(pos, n_sink, W);
     const uint32_t J = runs.sinks + runs.rcount;
-    const uint32_t nsplit = (J + P.chunk - 1) / P.chunk;
+    uint32_t nsplit, chunk;
+    if (P.split_cu) {
+        nsplit = P.split_cu[tok + 1] - P.split_cu[tok];
+        chunk = (J + nsplit - 1) / nsplit;
+    } else {
+        chunk = P.chunk;
+        nsplit = (J + chunk - 1) / chunk;
+    }
     if (split >= nsplit) return;
-    const uint32_t j0 = split * P.chunk;
-    const uint32_t j1 = min(J, j0 + P.chunk);
+    const uint32_t j0 = split * chunk;
+    const uint32_t j1 = min(J, j0 + chunk);
     const bool appender = P.fuse_append && split == nsplit - 1;
     const uint32_t rep = P.rep;
     const float2 *cs = P.rope + (size_t)pos * (QK / 2);
@@ -660,88 +832,7 @@ __global__ void __launch_bounds__(128) attend_kernel(const AttnParams P) {
         consume<QK, VD, KVT, NQ, 1>(qr, kw, vw, ksc, vsc, valid, m, l, acc);
     }
 
-    // Reduce across the row lanes of the warp (m is warp-uniform).
-#pragma unroll
-    for (int qi = 0; qi < NQ; qi++) {
-#pragma unroll
-        for (int o = LPR; o < 32; o <<= 1) {
-            l[qi] += __shfl_xor_sync(0xffffffffu, l[qi], o);
-#pragma unroll
-            for (int e = 0; e < EV; e++) acc[qi][e] += __shfl_xor_sync(0xffffffffu, acc[qi][e], o);
-        }
-    }
-    if (rl == 0) {
-#pragma unroll
-        for (int qi = 0; qi < NQ; qi++)
-#pragma unroll
-            for (int e = 0; e < EV; e++) sm_o[warp][qi][sub * EV + e] = acc[qi][e];
-    }
-    if (lane == 0) {
-#pragma unroll
-        for (int qi = 0; qi < NQ; qi++) {
-            sm_m[warp][qi] = m[qi];
-            sm_l[warp][qi] = l[qi];
-        }
-    }
-    __syncthreads();
-
-    const size_t out_base = (size_t)tm.row * P.n_heads;
-    const size_t part_base = ((size_t)item * P.max_splits + split) * NQ;
-    for (int idx = tid; idx < (int)rep * VD; idx += NW * 32) {
-        const int qi = idx / VD, d = idx % VD;
-        float M = sm_m[0][qi];
-#pragma unroll
-        for (int w = 1; w < NW; w++) M = fmaxf(M, sm_m[w][qi]);
-        float o = 0.0f, L = 0.0f;
-#pragma unroll
-        for (int w = 0; w < NW; w++) {
-            const float f = ex2(sm_m[w][qi] - M);
-            o += sm_o[w][qi][d] * f;
-            L += sm_l[w][qi] * f;
-        }
-        if (nsplit == 1) {
-            const uint32_t h = g * rep + qi;
-            float val = o / L;
-            if (P.gate) val *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, (out_base + h) * VD + d) *
-                                                 1.4426950408889634f));
-            act_store(P.out, P.out_dt, (out_base + h) * VD + d, val);
-        } else {
-            P.part_o[(part_base + qi) * VD + d] = o;
-            if (d == 0) {
-                P.part_ml[(part_base + qi) * 2 + 0] = M;
-                P.part_ml[(part_base + qi) * 2 + 1] = L;
-            }
-        }
-    }
-    if (nsplit == 1) return;
-
-    // Last CTA of this (token, group) merges the splits. No CTA ever waits.
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = atomicAdd(&P.counters[item], 1) == (int)nsplit - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    const size_t item_base = (size_t)item * P.max_splits * NQ;
-    for (int idx = tid; idx < (int)rep * VD; idx += NW * 32) {
-        const int qi = idx / VD, d = idx % VD;
-        float M = -INFINITY;
-        for (uint32_t s = 0; s < nsplit; s++)
-            M = fmaxf(M, __ldcg(&P.part_ml[(item_base + (size_t)s * NQ + qi) * 2]));
-        float o = 0.0f, L = 0.0f;
-        for (uint32_t s = 0; s < nsplit; s++) {
-            const size_t b = item_base + (size_t)s * NQ + qi;
-            const float f = ex2(__ldcg(&P.part_ml[b * 2]) - M);
-            o += __ldcg(&P.part_o[b * VD + d]) * f;
-            L += __ldcg(&P.part_ml[b * 2 + 1]) * f;
-        }
-        const uint32_t h = g * rep + qi;
-        float val = o / L;
-        if (P.gate) val *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, (out_base + h) * VD + d) *
-                                             1.4426950408889634f));
-        act_store(P.out, P.out_dt, (out_base + h) * VD + d, val);
-    }
-    if (tid == 0) P.counters[item] = 0;
+    attend_finish<QK, VD, KVT, NQ, NW>(P, m, l, acc, sm_o, sm_m, sm_l, &s_last, item, split, nsplit, g, tm.row, tid);
 }
 
 }  // namespace nda

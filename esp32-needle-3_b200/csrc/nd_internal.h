@@ -14,13 +14,21 @@ inline bool head_dims_supported(unsigned qk, unsigned vd) {
 }
 inline int nq_for_rep(unsigned rep) { return rep <= 1 ? 1 : rep <= 2 ? 2 : rep <= 4 ? 4 : 8; }
 
+// Rows per TMA box of the TMA-staged decode kernel; its splits are multiples.
+#ifndef ND_TMA_ROWS_DEFINED
+#define ND_TMA_ROWS_DEFINED
+constexpr int kTmaRows = 64;
+#endif
+
 // Rows one attend CTA consumes per loop iteration (a split is a multiple).
-int attend_rows_per_iter(int kv_dt, int vd);
+int attend_rows_per_iter(int kv_dt, int vd, int nq);
 
 #define ND_DECLARE_KV(SUF)                                                                  \
     cudaError_t attend_launch_##SUF(int qk, int vd, int nq, const AttnParams &P, dim3 grid, \
                                     cudaStream_t s);                                        \
-    cudaError_t append_launch_##SUF(int qk, int vd, const AttnParams &P, cudaStream_t s);
+    cudaError_t append_launch_##SUF(int qk, int vd, const AttnParams &P, cudaStream_t s);                \
+    cudaError_t attend_lean_launch_##SUF(int hd, int nq, const void *kmap, const void *vmap,            \
+                                         const AttnParams &P, int *blocks_per_sm, cudaStream_t s);
 ND_DECLARE_KV(i8)
 ND_DECLARE_KV(f32)
 ND_DECLARE_KV(f16)

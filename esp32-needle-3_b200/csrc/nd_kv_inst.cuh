@@ -2,6 +2,7 @@
 // element type; included once per nd_kv_*.cu so the four dtypes compile in
 // parallel.
 #pragma once
+#include "nd_decode_tma.cuh"
 #include "nd_internal.h"
 
 namespace nda {
@@ -52,6 +53,47 @@ cudaError_t append_launch_t(int qk, int vd, const AttnParams &P, cudaStream_t s)
     return cudaErrorInvalidValue;
 }
 
+// Balanced TMA-staged attend (nd_decode_tma.cuh), launched with programmatic
+// stream serialization (it may start under the previous kernel's tail; the
+// kernel itself waits where it depends on it). With blocks_per_sm set, only
+// raises the kernel's dynamic shared memory limit and reports how many CTAs of
+// the instantiation one SM holds (no launch); the host asks once per handle
+// and instantiation before the first launch.
+template <typename KVT>
+cudaError_t attend_lean_launch_t(int hd, int nq, const void *kmap, const void *vmap, const AttnParams &P,
+                                 int *blocks_per_sm, cudaStream_t s) {
+    if constexpr (KvT<KVT>::dt == DT_F16 || KvT<KVT>::dt == DT_BF16) {
+#define ND_CASE(H, N)                                                                                   \
+        if (hd == H && nq == N) {                                                                       \
+            constexpr uint32_t smem = attend_lean_smem_bytes<H, KVT, N>();                              \
+            if (blocks_per_sm) { /* once per handle: sets the smem limit on the handle's device */      \
+                cudaError_t e = cudaFuncSetAttribute(attend_lean_kernel<H, KVT, N>,                     \
+                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+                if (e != cudaSuccess) return e;                                                         \
+                return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm,                     \
+                                                                     attend_lean_kernel<H, KVT, N>, 224, smem); \
+            }                                                                                           \
+            cudaLaunchConfig_t cfg = {};                                                                \
+            cfg.gridDim = dim3(P.n_cta);                                                                \
+            cfg.blockDim = dim3(224);                                                                   \
+            cfg.dynamicSmemBytes = smem;                                                                \
+            cfg.stream = s;                                                                             \
+            cudaLaunchAttribute at[1];                                                                  \
+            at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;                              \
+            at[0].val.programmaticStreamSerializationAllowed = 1;                                       \
+            cfg.attrs = at;                                                                             \
+            cfg.numAttrs = 1;                                                                           \
+            return cudaLaunchKernelEx(&cfg, attend_lean_kernel<H, KVT, N>,                              \
+                                      *static_cast<const CUtensorMap *>(kmap),                          \
+                                      *static_cast<const CUtensorMap *>(vmap), P);                      \
+        }
+        ND_CASE(64, 1) ND_CASE(64, 2) ND_CASE(64, 4) ND_CASE(64, 8)
+        ND_CASE(128, 1) ND_CASE(128, 2) ND_CASE(128, 4)
+#undef ND_CASE
+    }
+    return cudaErrorInvalidValue;
+}
+
 }  // namespace nda
 
 #define ND_DEFINE_KV(SUF, KVT)                                                                  \
@@ -62,5 +104,9 @@ cudaError_t append_launch_t(int qk, int vd, const AttnParams &P, cudaStream_t s)
     }                                                                                           \
     cudaError_t append_launch_##SUF(int qk, int vd, const AttnParams &P, cudaStream_t s) {      \
         return append_launch_t<KVT>(qk, vd, P, s);                                              \
+    }                                                                                           \
+    cudaError_t attend_lean_launch_##SUF(int hd, int nq, const void *kmap, const void *vmap,    \
+                                         const AttnParams &P, int *blocks_per_sm, cudaStream_t s) { \
+        return attend_lean_launch_t<KVT>(hd, nq, kmap, vmap, P, blocks_per_sm, s);              \
     }                                                                                           \
     }

@@ -45,6 +45,7 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "nd_async.cuh"
 #include "nd_internal.h"
 
 namespace nda {
@@ -59,7 +60,6 @@ constexpr uint32_t Q_BYTES = BM * HD * 2;    // 16 KB
 constexpr uint32_t KV_BYTES = BN * HD * 2;   // 8 KB per K or V tile
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t COL_S = 0, COL_O = 128, COL_QHI = 192, COL_QLO = 224;
-constexpr long long kTimeoutCycles = 4000000000LL;   // ~2 s at 1.9 GHz
 
 // Dynamic shared memory: Q landing tile, K and V stage rings (1024-byte
 // aligned tiles for the 128-byte swizzle), then the barrier block.
@@ -80,59 +80,6 @@ struct Bars {
     int abort_flag;
 };
 constexpr uint32_t SMEM_BYTES = OFF_BAR + sizeof(Bars);
-
-__device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t n) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
-}
-__device__ __forceinline__ bool mbar_test(uint64_t *b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(su32(b)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait for the phase of parity `parity`. False when the CTA is
-// aborting (another role timed out) or this wait timed out (then it raises
-// the abort itself).
-__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag) {
-    if (mbar_test(b, parity)) return true;
-    const long long t0 = clock64();
-    while (!mbar_test(b, parity)) {
-        if (*abort_flag) return false;
-        if (clock64() - t0 > kTimeoutCycles) {
-            *abort_flag = 1;
-            return false;
-        }
-    }
-    return true;
-}
-__device__ __forceinline__ void mbar_drain(uint64_t *b, uint32_t parity) {
-    const long long t0 = clock64();
-    while (!mbar_test(b, parity) && clock64() - t0 < kTimeoutCycles) {
-    }
-}
-
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            su32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(su32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // Shared-memory matrix descriptor, 128-byte swizzle, sm100 version bits.
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
