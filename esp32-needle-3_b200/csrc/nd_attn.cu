@@ -1328,3 +1328,14 @@ const char *nd_attn_version(void) {
 }
 
 }  // extern "C"
+
+const nd_attn_ops *nd_attn_cuda_ops(void) {
+    static const nd_attn_ops ops = {
+        ND_ATTN_OPS_VERSION,   nd_attn_open,          nd_attn_close,        nd_attn_set_head_norm,
+        nd_attn_reset,         nd_attn_set_sink,      nd_attn_snapshot,     nd_attn_rewind,
+        nd_attn_advance,       nd_attn_decode,        nd_attn_prefill,      nd_attn_decode_host,
+        nd_attn_prefill_host,  nd_attn_prefix_save,   nd_attn_prefix_restore, nd_attn_prefix_free,
+        nd_attn_sync,          nd_attn_last_error,
+    };
+    return &ops;
+}

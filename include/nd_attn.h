@@ -20,6 +20,11 @@
  *    stream-ordered on the handle's CUDA stream; the plain entry points return
  *    after enqueueing, `*_host` entry points and state/prefix calls return after
  *    the stream has drained. nd_attn_sync() waits explicitly.
+ *  - Decode and non-wrapping prefill kernels of 16-bit caches are launched with
+ *    programmatic stream serialization: one may begin under the tail of the
+ *    previous kernel on the stream and stream its own layer's K/V early, but it
+ *    reads the caller's tensors and writes `out` only after that kernel has
+ *    completed, so stream order holds for everything the caller can see.
  *  - No torch or C++ types cross this boundary: plain pointers and sizes.
  *
  * Tensor layouts (row-major, elements of `act_dtype` unless stated):
@@ -221,6 +226,41 @@ ND_ATTN_API int  nd_attn_write_cache(nd_attn *h, uint32_t layer, uint32_t seq, u
  * window/block_size page ids, each < n_blocks). Pages may be shared between
  * sequences (a common schema prefix). */
 ND_ATTN_API int  nd_attn_set_block_table(nd_attn *h, uint32_t seq, const int32_t *pages);
+
+/* ---- hook table ------------------------------------------------------------ */
+/* The engine's attention() seam calls through a table of function pointers that
+ * defaults to its own C path and is swapped at link or run time, the pattern of
+ * the nd_parallel_rows hook (engine/include/nd_quant.h:229-230,
+ * engine/src/nd_quant.c:717). nd_attn_cuda_ops() returns this library's table;
+ * its members are the entry points declared above. No reference counterpart
+ * for the accessor itself. */
+#define ND_ATTN_OPS_VERSION 1u
+typedef struct nd_attn_ops {
+    uint32_t version;   /* ND_ATTN_OPS_VERSION */
+    int  (*open)(const nd_attn_config *cfg, nd_attn **out);
+    void (*close)(nd_attn *h);
+    int  (*set_head_norm)(nd_attn *h, uint32_t layer, const float *q_scale, const float *k_scale);
+    int  (*reset)(nd_attn *h, uint32_t seq);
+    int  (*set_sink)(nd_attn *h, uint32_t seq, uint32_t n);
+    int  (*snapshot)(nd_attn *h, uint32_t seq);
+    int  (*rewind)(nd_attn *h, uint32_t seq);
+    int  (*advance)(nd_attn *h, uint32_t n, const uint32_t *seq_ids, const uint32_t *len);
+    int  (*decode)(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const void *q,
+                   const void *k, const void *v, const void *gate, void *out);
+    int  (*prefill)(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const uint32_t *len,
+                    const void *q, const void *k, const void *v, const void *gate, void *out);
+    int  (*decode_host)(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const void *q,
+                        const void *k, const void *v, const void *gate, void *out);
+    int  (*prefill_host)(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids,
+                         const uint32_t *len, const void *q, const void *k, const void *v,
+                         const void *gate, void *out);
+    nd_attn_prefix *(*prefix_save)(nd_attn *h, uint32_t seq);
+    int  (*prefix_restore)(nd_attn *h, uint32_t seq, const nd_attn_prefix *p);
+    void (*prefix_free)(nd_attn_prefix *p);
+    int  (*sync)(nd_attn *h);
+    const char *(*last_error)(void);
+} nd_attn_ops;
+ND_ATTN_API const nd_attn_ops *nd_attn_cuda_ops(void);
 
 /* ---- misc ------------------------------------------------------------------ */
 /* Waits for all work enqueued on the handle's stream; reports device-side

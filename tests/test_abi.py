@@ -95,3 +95,23 @@ def test_oracle_half_conversions_match_numpy():
     assert np.array_equal(bf, O.to_bf16_bits(x))
     back = np.array([o.ndo_f16_to_f32(int(b)) for b in f16], np.float32)
     assert np.array_equal(back, f16.view(np.float16).astype(np.float32))
+
+
+def test_hook_table_points_at_the_entry_points(tmp_path):
+    """nd_attn_cuda_ops() (the engine's swap-in hook, nd_quant.h:229-230 pattern)
+    returns a table whose every member is the exported entry point of the same
+    name; built as a C program against the header and linked to the library."""
+    members = ["open", "close", "set_head_norm", "reset", "set_sink", "snapshot", "rewind", "advance", "decode",
+               "prefill", "decode_host", "prefill_host", "prefix_save", "prefix_restore", "prefix_free", "sync",
+               "last_error"]
+    checks = "\n".join(f'    bad += (void *)o->{m} != (void *)nd_attn_{m};' for m in members)
+    src = tmp_path / "ops.c"
+    src.write_text('#include <stdio.h>\n#include "nd_attn.h"\nint main(void){\n'
+                   '    const nd_attn_ops *o = nd_attn_cuda_ops(); int bad = o->version != ND_ATTN_OPS_VERSION;\n'
+                   + checks + '\n    printf("%d\\n", bad); return bad;\n}\n')
+    exe = tmp_path / "ops"
+    libdir = os.path.dirname(ndattn.LIB_PATH)
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-Wno-pedantic", "-I", os.path.join(ROOT, "include"),
+                    str(src), "-o", str(exe), "-L", libdir, "-lndattn", f"-Wl,-rpath,{libdir}"], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0 and r.stdout.strip() == "0", (r.returncode, r.stdout, r.stderr)
