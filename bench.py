@@ -46,6 +46,10 @@ METRIC = "decode tok/s (config 2: 8-layer decode attention, B=64/GPU, ctx U[256,
 # config 3 (prefill)
 P_SEQS, P_TOK, P_H, P_HKV, P_HD = 512, 1024, 16, 4, 64
 P_METRIC = "prefill tok/s (config 3: 512 seq x 1024 tok x 8 layers, GQA 16/4, hd 64, bf16)"
+# config 4 (long-context paged decode)
+L_SEQS, L_CTX, L_H, L_HD, L_BLOCK, L_STEPS = 256, 32768, 8, 128, 64, 64
+L_METRIC = ("decode tok/s (config 4: B=256/GPU x 32768 cached, 8x128 MHA, fp16 KV, 64-slot pages in a "
+            "shuffled block table, 1 layer)")
 
 
 def peaks():
@@ -166,6 +170,24 @@ def cpu_prefill(target_s: float):
     sample = (f"{n} sequences x {P_TOK} tokens x 1 layer of config 3, reference C attention one token at a "
               f"time (int8 KV), {threads} threads; 8 layers extrapolated linearly")
     return tok_s, threads, sample
+
+
+def cpu_long(target_s: float):
+    """Config 4 on the host cores: the reference's int8 attention over a fixed
+    subset of `threads` sequences at the full 32 768-token context, one decode
+    step each, grown until ~target_s; tok/s of that subset (per-sequence work
+    is the same for every sequence of the config)."""
+    O = _oracle()
+    threads = os.cpu_count() or 1
+    n, steps = threads, 1
+    window = L_CTX + 64
+    secs = O.ref_decode_bench(L_H, L_H, L_HD, L_HD, window, [L_CTX] * n, steps, 1, 10000.0, threads)
+    while secs < target_s / 2 and steps < 16:
+        steps *= 2
+        secs = O.ref_decode_bench(L_H, L_H, L_HD, L_HD, window, [L_CTX] * n, steps, 1, 10000.0, threads)
+    sample = (f"{n} sequences x {steps} decode steps at 32768 cached tokens, 8x128, 1 layer, reference C "
+              f"attention (int8 KV), {threads} threads")
+    return n * steps / secs, threads, sample
 
 
 def run_reference(args):
@@ -309,6 +331,85 @@ def run_decode(args, world, rank, local, dist):
     }
 
 
+# ------------------------------------------------------------ GPU: long decode
+def run_long(args, world, rank, local, dist):
+    """Config 4: 256 sequences per GPU at 32 768 cached tokens, hd 128, fp16 KV
+    in 64-slot pages placed by a shuffled block table (seed 3), K/V ~ N(0,1)
+    0.25 with 1 % of K rows x8, 64 decode steps of one layer."""
+    import numpy as np
+    import torch
+
+    import ndattn
+
+    K, Wm = args.long_steps, 3
+    window = (L_CTX + K + Wm + 2 + L_BLOCK - 1) // L_BLOCK * L_BLOCK
+    a = ndattn.Attn(n_layers=1, n_heads=L_H, n_kv_heads=L_H, qk_head_dim=L_HD, v_head_dim=L_HD, window=window,
+                    max_seqs=L_SEQS, block_size=L_BLOCK, kv_dtype="f16", act_dtype="f16", out_dtype="f16",
+                    device=local)
+    stream = torch.cuda.ExternalStream(a.stream)
+    nb = window // L_BLOCK
+    pages = np.random.default_rng(3 + rank).permutation(L_SEQS * nb)
+    for s in range(L_SEQS):
+        a.set_block_table(s, pages[s * nb:(s + 1) * nb])
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(3000 + rank)
+    kv = L_H * L_HD
+    for s in range(L_SEQS):                       # cached contexts, straight into the pages
+        kk = torch.randn((L_CTX, kv), generator=gen, device="cuda") * 0.25
+        peaky = torch.rand((L_CTX, 1), generator=gen, device="cuda") < 0.01
+        kk = torch.where(peaky, kk * 8.0, kk).half()
+        vv = (torch.randn((L_CTX, kv), generator=gen, device="cuda") * 0.25).half()
+        torch.cuda.synchronize()
+        a.write_cache(0, s, 0, L_CTX, kk, vv)
+        a.set_state(s, L_CTX, 0)
+    del kk, vv, peaky
+    q = torch.randn((K + Wm, L_SEQS, L_H * L_HD), generator=gen, device="cuda").half()
+    k = (torch.randn((K + Wm, L_SEQS, kv), generator=gen, device="cuda") * 0.25).half()
+    v = (torch.randn((K + Wm, L_SEQS, kv), generator=gen, device="cuda") * 0.25).half()
+    out = torch.empty((L_SEQS, L_H * L_HD), dtype=torch.float16, device="cuda")
+    for i in range(Wm):
+        a.decode(0, L_SEQS, q[i], k[i], v[i], out)
+        a.advance(L_SEQS)
+    a.sync()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = a.launches
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        t0.record(stream)
+        for i in range(K):
+            a.decode(0, L_SEQS, q[Wm + i], k[Wm + i], v[Wm + i], out)
+            a.advance(L_SEQS)
+        t1.record(stream)
+        a.sync()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+    launches = a.launches - launches0
+    ms = t0.elapsed_time(t1)
+    a.close()
+    times = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms = float(times[0])
+    # Every visited K and V row once per step (positions 0..pos, the new one
+    # included) plus q/k/v in and out; the block table is ~2 KB per sequence.
+    kv_bytes = sum(float(L_SEQS) * (L_CTX + Wm + i + 1) for i in range(K)) / K * L_H * L_HD * 2 * 2
+    bytes_per_step = kv_bytes + L_SEQS * (4 * L_H * L_HD) * 2
+    pk, peak_kind = peaks()
+    achieved = bytes_per_step / (ms / 1e3 / K) / 1e9
+    return {"metric": L_METRIC, "value": L_SEQS * world * K / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms / K,
+            "steps": K, "warmup": Wm, "gpu_launches": int(launches),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_kind": f"{peak_kind} copy bandwidth",
+                         "kernel": "attend_lean_kernel<128,half,1>", "bytes_per_launch": bytes_per_step},
+            "config": {"workload": "config4-long-decode", "seqs_per_gpu": L_SEQS, "ctx": L_CTX, "layers": 1,
+                       "heads": "8x128 MHA", "kv_dtype": "fp16", "paging": f"{L_BLOCK}-slot pages, shuffled (seed 3)",
+                       "l2": "inputs larger than L2 (~34 GB of KV read per step)"},
+            "clocks": clk.summary()}
+
+
 # ------------------------------------------------------------ GPU: prefill
 def run_prefill(args, world, rank, local, dist, seqs=P_SEQS):
     import torch
@@ -408,6 +509,7 @@ def run_ours(args):
     else:
         dec = run_decode(args, world, rank, local, dist)
         pre = run_prefill(args, world, rank, local, dist) if args.prefill_steps > 0 else None
+        lng = run_long(args, world, rank, local, dist) if args.long_steps > 0 else None
         cpu = None
         if rank == 0 and world == 1 and not args.no_cpu:
             v_cpu, cores, sample = cpu_decode(10.0, 0)
@@ -416,6 +518,10 @@ def run_ours(args):
                 pv, pcores, psample = cpu_prefill(10.0)
                 pre["cpu_baseline"] = {"value": pv, "unit": "tok/s", "cores": pcores, "kind": "reference",
                                        "sample": psample}
+            if lng is not None:
+                lv, lcores, lsample = cpu_long(10.0)
+                lng["cpu_baseline"] = {"value": lv, "unit": "tok/s", "cores": lcores, "kind": "reference",
+                                       "sample": lsample}
         if rank == 0:
             line = {"metric": METRIC, "value": dec["value"], "unit": "tok/s", "n_gpus": world, "steps": dec["steps"],
                     "warmup": dec["warmup"], "ms_per_step": dec["ms_per_step"], "higher_is_better": True,
@@ -425,8 +531,9 @@ def run_ours(args):
                                "l2": "inputs larger than L2 (~1.3 GB of KV read per step)",
                                "parallelism": f"batch-sharded x{world} (no collective)"},
                     "roofline": dec["roofline"], "cpu_baseline": cpu, "e2e": dec["e2e"],
-                    "gpu_launches": dec["gpu_launches"] + (pre["gpu_launches"] if pre else 0),
-                    "clocks": dec["clocks"], "prefill": pre}
+                    "gpu_launches": dec["gpu_launches"] + (pre["gpu_launches"] if pre else 0)
+                    + (lng["gpu_launches"] if lng else 0),
+                    "clocks": dec["clocks"], "prefill": pre, "long_decode": lng}
             print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -442,6 +549,8 @@ def main():
     ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
                     help="decode: config 2 line with the config 3 prefill inside; prefill: config 3 alone")
     ap.add_argument("--prefill-steps", type=int, default=5, help="timed config-3 steps (0 skips the prefill leg)")
+    ap.add_argument("--long-steps", type=int, default=L_STEPS,
+                    help="timed config-4 decode steps (0 skips the long-context leg)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling only: fewer layers than the config")
     ap.add_argument("--seqs", type=int, default=0, help="profiling only: fewer config-3 sequences")
     args = ap.parse_args()

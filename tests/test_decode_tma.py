@@ -131,3 +131,54 @@ def test_config2_full_size_decode():
             s.advance()
     assert worst <= TOL
     a.close()
+
+
+def test_config4_geometry_long_context_paged():
+    """Config 4's geometry at its full context: 32 768 cached tokens per
+    sequence (8 sequences instead of 256), 8x128 MHA, fp16 KV ~ N(0,1) 0.25
+    with 1 % of K rows x8, 64-slot pages in a shuffled block table (seed 3),
+    two decode steps. Items hold 512 tiles here, so they span several static
+    and dynamic units of the balanced grid."""
+    import torch
+    rng = np.random.default_rng(3)
+    B, H, HD, CTX, BS = 8, 8, 128, 32768, 64
+    W = CTX + 64
+    a = ndattn.Attn(n_layers=1, n_heads=H, n_kv_heads=H, qk_head_dim=HD, v_head_dim=HD, window=W, max_seqs=B,
+                    block_size=BS, kv_dtype="f16", act_dtype="f16", out_dtype="f32", max_pos=W)
+    nb = W // BS
+    pages = rng.permutation(B * nb)
+    for s in range(B):
+        a.set_block_table(s, pages[s * nb:(s + 1) * nb])
+    seqs = [O.OracleSeq(1, H, H, HD, HD, W, O.F16, max_pos=W) for _ in range(B)]
+    for s in range(B):
+        k = rng.standard_normal((CTX, H * HD), dtype=np.float32) * 0.25
+        k[rng.random(CTX) < 0.01] *= 8.0
+        k = k.astype(np.float16)
+        v = (rng.standard_normal((CTX, H * HD), dtype=np.float32) * 0.25).astype(np.float16)
+        a.write_cache(0, s, 0, CTX, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
+        seqs[s].k[0, :CTX] = k.view(np.uint16)
+        seqs[s].v[0, :CTX] = v.view(np.uint16)
+        a.set_state(s, CTX, 0)
+        seqs[s].pos = CTX
+    worst = 0.0
+    for _ in range(2):
+        q = rng.standard_normal((B, H * HD)).astype(np.float32)
+        k = (rng.standard_normal((B, H * HD)) * 0.25).astype(np.float32)
+        v = (rng.standard_normal((B, H * HD)) * 0.25).astype(np.float32)
+        out = torch.zeros((B, H * HD), dtype=torch.float32, device="cuda")
+        a.decode(0, B, dev(q, O.F16), dev(k, O.F16), dev(v, O.F16), out)
+        a.sync()
+        got = out.cpu().numpy()
+        for s in range(B):
+            want = seqs[s].step(0, O.round_act(q[s], O.F16), O.round_act(k[s], O.F16), O.round_act(v[s], O.F16))
+            worst = max(worst, rel_err(got[s].reshape(H, HD), want))
+        a.advance(B)
+        for s in seqs:
+            s.advance()
+    assert worst <= TOL
+    for s in (0, B - 1):   # the appended rows, read back through the block table
+        gk, gv, _, _ = a.read_cache(0, s, CTX, 2)
+        ok, ov = oracle_cache(seqs[s], 0, O.F16)
+        assert np.array_equal(cache_bits(gk), cache_bits(ok[CTX:CTX + 2]))
+        assert np.array_equal(cache_bits(gv), cache_bits(ov[CTX:CTX + 2]))
+    a.close()
