@@ -331,6 +331,70 @@ def run_decode(args, world, rank, local, dist):
     }
 
 
+# ------------------------------------------------------- GPU: head-sharded decode
+def run_decode_heads(args, world, rank, local, dist):
+    """Config 2 head-sharded over the ranks (strong scaling): every rank holds
+    all 64 sequences (contexts of seed 1) for its H/world KV heads; per layer it
+    decodes its heads, then one NCCL all-gather (on the handle's stream) puts
+    out[64, 8, 64] together on every rank."""
+    import torch
+
+    import ndshard
+
+    K, Wm = args.steps, args.warmup
+    ctx = ctx_lengths(0)
+    window = (CTX_HI + K + Wm + 2 + 63) // 64 * 64
+    sh = ndshard.HeadShardedAttn(rank, world, H, HKV, n_layers=LAYERS, qk_head_dim=QK, v_head_dim=VD,
+                                 window=window, max_seqs=BATCH, kv_dtype="f16", act_dtype="f16", out_dtype="f16",
+                                 device=local)
+    a = sh.attn
+    hq, hkv = sh.q1 - sh.q0, sh.kv1 - sh.kv0
+    stream = torch.cuda.ExternalStream(a.stream)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(2000 + rank)
+    for l in range(LAYERS):
+        for s in range(BATCH):
+            n = int(ctx[s])
+            kk = (torch.randn((n, hkv * QK), generator=gen, device="cuda") * 0.5).half()
+            vv = (torch.randn((n, hkv * VD), generator=gen, device="cuda") * 0.5).half()
+            torch.cuda.synchronize()
+            a.write_cache(l, s, 0, n, kk, vv)
+    for s in range(BATCH):
+        a.set_state(s, int(ctx[s]), 0)
+    nsteps = K + Wm
+    q = torch.randn((nsteps, LAYERS, BATCH, hq * QK), generator=gen, device="cuda").half()
+    k = (torch.randn((nsteps, LAYERS, BATCH, hkv * QK), generator=gen, device="cuda") * 0.5).half()
+    v = (torch.randn((nsteps, LAYERS, BATCH, hkv * VD), generator=gen, device="cuda") * 0.5).half()
+    out = torch.empty((LAYERS, BATCH, hq * VD), dtype=torch.float16, device="cuda")
+
+    def step(i):
+        for l in range(LAYERS):
+            sh.decode(l, BATCH, q[i, l], k[i, l], v[i, l], out[l])
+        a.advance(BATCH)
+
+    for i in range(Wm):
+        step(i)
+    a.sync()
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(K):
+        step(Wm + i)
+    t1.record(stream)
+    a.sync()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    sh.close()
+    times = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms = float(times[0])
+    return {"value": BATCH * K / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms / K, "scaling": "strong",
+            "parallelism": f"head-sharded x{world}: {hkv} KV heads per GPU, NCCL all-gather of out per layer",
+            "allgather_bytes_per_layer": BATCH * H * VD * 2}
+
+
 # ------------------------------------------------------------ GPU: long decode
 def run_long(args, world, rank, local, dist):
     """Config 4: 256 sequences per GPU at 32 768 cached tokens, hd 128, fp16 KV
@@ -508,6 +572,7 @@ def run_ours(args):
                                   data="synthetic")), flush=True)
     else:
         dec = run_decode(args, world, rank, local, dist)
+        heads = run_decode_heads(args, world, rank, local, dist) if world > 1 and HKV % world == 0 else None
         pre = run_prefill(args, world, rank, local, dist) if args.prefill_steps > 0 else None
         lng = run_long(args, world, rank, local, dist) if args.long_steps > 0 else None
         cpu = None
@@ -533,7 +598,7 @@ def run_ours(args):
                     "roofline": dec["roofline"], "cpu_baseline": cpu, "e2e": dec["e2e"],
                     "gpu_launches": dec["gpu_launches"] + (pre["gpu_launches"] if pre else 0)
                     + (lng["gpu_launches"] if lng else 0),
-                    "clocks": dec["clocks"], "prefill": pre, "long_decode": lng}
+                    "clocks": dec["clocks"], "prefill": pre, "long_decode": lng, "head_sharded": heads}
             print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -21,7 +21,7 @@
 // attend_kernel, rows read from shared memory); 4 = producer: takes units,
 // publishes a descriptor per segment (maximal run of one item inside a unit)
 // into a SQ-deep slot ring and issues the TMA boxes (2D maps over
-// [rows][n_kv * hd], box hd x 64, no multicast) into a STAGES-deep ring;
+// [rows][n_kv * hd], box hd x 64, each CTA loading its own) into a STAGES-deep ring;
 // 5 = prep: query rows of each segment (norm + RoPE) and the fused append of
 // the newest row; 6 = finisher: merges the consumers' per-warp results of a
 // segment and writes the output, or the item's partial and a note of it in

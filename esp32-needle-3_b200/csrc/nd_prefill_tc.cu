@@ -39,7 +39,7 @@
 //
 // Every mbarrier wait is bounded (~2 s of SM clock); on expiry the CTA raises
 // the error word, drains what it issued (bounded), frees TMEM and returns.
-// No TMA multicast anywhere.
+// Every TMA box is loaded by the CTA that reads it.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
