@@ -46,6 +46,12 @@ METRIC = "decode tok/s (config 2: 8-layer decode attention, B=64/GPU, ctx U[256,
 # config 3 (prefill)
 P_SEQS, P_TOK, P_H, P_HKV, P_HD = 512, 1024, 16, 4, 64
 P_METRIC = "prefill tok/s (config 3: 512 seq x 1024 tok x 8 layers, GQA 16/4, hd 64, bf16)"
+# DRAM bytes (read + write) per launch from one ncu capture of the same kernel:
+# the decode launch on the one-layer case (per-launch work equals a launch
+# here), the prefill launch on 64 sequences scaled by 8 to 512 (traffic grows
+# with the sequences processed).
+DECODE_TRAFFIC = (157.5e6 + 3.9e6)
+PREFILL_TRAFFIC = (318.5e6 + 102.9e6) * 8
 # config 4 (long-context paged decode)
 L_SEQS, L_CTX, L_H, L_HD, L_BLOCK, L_STEPS = 256, 32768, 8, 128, 64, 64
 L_METRIC = ("decode tok/s (config 4: B=256/GPU x 32768 cached, 8x128 MHA, fp16 KV, 64-slot pages in a "
@@ -318,7 +324,8 @@ def run_decode(args, world, rank, local, dist):
     return {
         "value": BATCH * world * K / (ms / 1e3), "ms_per_step": ms / K, "steps": K, "warmup": Wm,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_kind": f"{peak_kind} copy bandwidth",
+                     "frac": achieved / pk["hbm_gbs"], "traffic": DECODE_TRAFFIC, "traffic_unit": "B/launch",
+                     "peak_kind": f"{peak_kind} copy bandwidth",
                      "kernel": "attend_lean_kernel<64,half,1> (balanced TMA split-KV: RoPE + KV append + "
                                "merge; consecutive launches overlap)",
                      "avg_launch_us": avg_kern_s * 1e6, "isolated_launch_us": iso_s * 1e6,
@@ -545,7 +552,7 @@ def run_prefill(args, world, rank, local, dist, seqs=P_SEQS):
         "config": {"workload": "config3-prefill", "seqs_per_gpu": seqs, "tokens": P_TOK, "layers": LAYERS,
                    "heads": "16 q / 4 kv x 64", "l2": "inputs larger than L2 (1.6 GB of q/k/v per layer)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": None,
+                     "frac": achieved / peak, "traffic": PREFILL_TRAFFIC * seqs / P_SEQS, "traffic_unit": "B/launch",
                      "peak_kind": f"{peak_kind} cuBLAS bf16, sustained (kernel runs inside a long step)",
                      "unit_of_work": "one layer call = K1 append + tcgen05 prefill, causal FLOPs",
                      "avg_layer_ms": layer_ms, "flops_per_layer": flops_layer},
