@@ -402,6 +402,125 @@ def run_decode_heads(args, world, rank, local, dist):
             "allgather_bytes_per_layer": BATCH * H * VD * 2}
 
 
+# ------------------------------------------------------------ GPU: shared-prefix serving
+S_REQ, S_PREFIX, S_SUF_LO, S_SUF_HI, S_STEPS, S_BLOCK = 4096, 213, 8, 64, 16, 64
+S_METRIC = ("serving tok/s (config 5: 4096 requests over the GPUs sharing one 213-token prefix, suffix "
+            "U[8,64] prefilled then 16 decode steps, 8 layers, 8x64, fp16 KV)")
+
+
+def run_serve(args, world, rank, local, dist):
+    """Config 5 on this rank's 4096 / world requests (strong scaling). The
+    213-token prefix is prefilled once into a template sequence, saved, and
+    restored into every request (untimed set-up); the requests' block tables
+    map their first three 64-slot pages to the template's pages, so the prefix
+    rows are stored (and read, from L2) once per GPU. Timed: one serving round
+    = the suffix prefill of every request, then 16 decode steps, 8 layers."""
+    import numpy as np
+    import torch
+
+    import ndattn
+
+    R = S_REQ // world
+    rng = np.random.default_rng(4)
+    suf = rng.integers(S_SUF_LO, S_SUF_HI + 1, size=S_REQ)[rank * R:(rank + 1) * R]
+    window = (S_PREFIX + S_SUF_HI + S_STEPS + 3 + S_BLOCK - 1) // S_BLOCK * S_BLOCK
+    nb = window // S_BLOCK
+    shared = S_PREFIX // S_BLOCK                      # whole prefix pages every request maps
+    tpl = R                                           # template sequence id
+    n_blocks = nb + R * (nb - shared)
+    a = ndattn.Attn(n_layers=LAYERS, n_heads=H, n_kv_heads=HKV, qk_head_dim=QK, v_head_dim=VD, window=window,
+                    max_seqs=R + 1, block_size=S_BLOCK, n_blocks=n_blocks, kv_dtype="f16", act_dtype="f16",
+                    out_dtype="f16", device=local)
+    stream = torch.cuda.ExternalStream(a.stream)
+    a.set_block_table(tpl, np.arange(nb))
+    for r in range(R):
+        own = nb + r * (nb - shared) + np.arange(nb - shared)
+        a.set_block_table(r, np.concatenate([np.arange(shared), own]))
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(4000)                             # the same prefix on every rank
+    d = H * QK
+    pq = torch.randn((S_PREFIX, d), generator=gen, device="cuda").half()
+    pk = (torch.randn((S_PREFIX, HKV * QK), generator=gen, device="cuda") * 0.5).half()
+    pv = (torch.randn((S_PREFIX, HKV * VD), generator=gen, device="cuda") * 0.5).half()
+    pout = torch.empty((S_PREFIX, H * VD), dtype=torch.float16, device="cuda")
+    for l in range(LAYERS):
+        a.prefill(l, [S_PREFIX], pq, pk, pv, pout, seq_ids=[tpl])
+    a.advance(1, seq_ids=[tpl], lens=[S_PREFIX])
+    a.snapshot(tpl)
+    pre = a.prefix_save(tpl)
+    for r in range(R):
+        a.prefix_restore(r, pre)
+    pre.free()
+    gen.manual_seed(4100 + rank)
+    T = int(suf.sum())
+    sq = torch.randn((LAYERS, T, d), generator=gen, device="cuda").half()
+    sk = (torch.randn((LAYERS, T, HKV * QK), generator=gen, device="cuda") * 0.5).half()
+    sv = (torch.randn((LAYERS, T, HKV * VD), generator=gen, device="cuda") * 0.5).half()
+    sout = torch.empty((T, H * VD), dtype=torch.float16, device="cuda")
+    dq = torch.randn((S_STEPS, LAYERS, R, d), generator=gen, device="cuda").half()
+    dk = (torch.randn((S_STEPS, LAYERS, R, HKV * QK), generator=gen, device="cuda") * 0.5).half()
+    dv = (torch.randn((S_STEPS, LAYERS, R, HKV * VD), generator=gen, device="cuda") * 0.5).half()
+    dout = torch.empty((R, H * VD), dtype=torch.float16, device="cuda")
+    lens = [int(x) for x in suf]
+
+    def serve_round(ev=None):
+        for l in range(LAYERS):
+            a.prefill(l, lens, sq[l], sk[l], sv[l], sout)
+        a.advance(R, lens=lens)
+        if ev is not None:
+            ev.record(stream)
+        for i in range(S_STEPS):
+            for l in range(LAYERS):
+                a.decode(l, R, dq[i, l], dk[i, l], dv[i, l], dout)
+            a.advance(R)
+
+    serve_round()                                     # warm-up round, then back to the prefix
+    for r in range(R):
+        a.rewind(r)
+    a.sync()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = a.launches
+    t0, tm, t1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    with Clocks(local) as clk:
+        t0.record(stream)
+        serve_round(tm)
+        t1.record(stream)
+        a.sync()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+    launches = a.launches - launches0
+    ms, pre_ms = t0.elapsed_time(t1), t0.elapsed_time(tm)
+    a.close()
+    times = torch.tensor([ms, pre_ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, pre_ms = float(times[0]), float(times[1])
+    dec_ms = (ms - pre_ms) / S_STEPS
+    row = HKV * (QK + VD) * 2                         # bytes of one K+V row, all heads
+    uniq = (S_PREFIX + float(np.sum(suf)) + R * (S_STEPS / 2 + 1)) * row * LAYERS
+    logical = float(np.sum(S_PREFIX + suf + S_STEPS / 2 + 1)) * row * LAYERS
+    pk_, peak_kind = peaks()
+    return {"metric": S_METRIC, "value": (T + R * S_STEPS) * world / (ms / 1e3), "unit": "tok/s",
+            "ms_per_round": ms, "prefill_ms": pre_ms, "decode_ms_per_step": dec_ms,
+            "prefill_tok_s": T * world / (pre_ms / 1e3), "decode_tok_s": R * world / (dec_ms / 1e3),
+            "scaling": "strong", "requests_per_gpu": R, "suffix_tokens_per_gpu": T, "gpu_launches": int(launches),
+            "roofline": {"bound": "hbm (prefix rows from L2)", "unit": "GB/s", "peak": pk_["hbm_gbs"],
+                         "decode_unique_gbs": uniq / (dec_ms / 1e3) / 1e9,
+                         "decode_unique_frac": uniq / (dec_ms / 1e3) / 1e9 / pk_["hbm_gbs"],
+                         "decode_logical_gbs": logical / (dec_ms / 1e3) / 1e9,
+                         "note": "unique = prefix once + each request's own rows; logical counts the shared "
+                                 "prefix once per request (served from L2, not an HBM figure)",
+                         "peak_kind": f"{peak_kind} copy bandwidth"},
+            "config": {"workload": "config5-shared-prefix", "requests": S_REQ, "prefix": S_PREFIX,
+                       "suffix": f"U[{S_SUF_LO},{S_SUF_HI}] seed 4", "decode_steps": S_STEPS, "layers": LAYERS,
+                       "heads": "8x64 MHA", "kv_dtype": "fp16",
+                       "paging": f"{S_BLOCK}-slot pages; {shared} prefix pages shared by every request"},
+            "clocks": clk.summary()}
+
+
 # ------------------------------------------------------------ GPU: long decode
 def run_long(args, world, rank, local, dist):
     """Config 4: 256 sequences per GPU at 32 768 cached tokens, hd 128, fp16 KV
@@ -582,6 +701,7 @@ def run_ours(args):
         heads = run_decode_heads(args, world, rank, local, dist) if world > 1 and HKV % world == 0 else None
         pre = run_prefill(args, world, rank, local, dist) if args.prefill_steps > 0 else None
         lng = run_long(args, world, rank, local, dist) if args.long_steps > 0 else None
+        srv = run_serve(args, world, rank, local, dist) if args.serve else None
         cpu = None
         if rank == 0 and world == 1 and not args.no_cpu:
             v_cpu, cores, sample = cpu_decode(10.0, 0)
@@ -604,8 +724,9 @@ def run_ours(args):
                                "parallelism": f"batch-sharded x{world} (no collective)"},
                     "roofline": dec["roofline"], "cpu_baseline": cpu, "e2e": dec["e2e"],
                     "gpu_launches": dec["gpu_launches"] + (pre["gpu_launches"] if pre else 0)
-                    + (lng["gpu_launches"] if lng else 0),
-                    "clocks": dec["clocks"], "prefill": pre, "long_decode": lng, "head_sharded": heads}
+                    + (lng["gpu_launches"] if lng else 0) + (srv["gpu_launches"] if srv else 0),
+                    "clocks": dec["clocks"], "prefill": pre, "long_decode": lng, "serving": srv,
+                    "head_sharded": heads}
             print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -623,6 +744,7 @@ def main():
     ap.add_argument("--prefill-steps", type=int, default=5, help="timed config-3 steps (0 skips the prefill leg)")
     ap.add_argument("--long-steps", type=int, default=L_STEPS,
                     help="timed config-4 decode steps (0 skips the long-context leg)")
+    ap.add_argument("--serve", type=int, default=1, help="1 runs the config-5 shared-prefix serving leg, 0 skips it")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling only: fewer layers than the config")
     ap.add_argument("--seqs", type=int, default=0, help="profiling only: fewer config-3 sequences")
     args = ap.parse_args()

@@ -149,6 +149,7 @@ struct nd_attn {
     int *d_err = nullptr;
     void *pin = nullptr;
     size_t pin_cap = 0;
+    int *err_pin = nullptr;   // pinned host copy of d_err, read once per sync
     void *dio = nullptr;
     size_t dio_cap = 0;
     uint64_t launches = 0;
@@ -564,7 +565,7 @@ int make_map(CUtensorMap *m, bool bf16, const void *base, uint64_t inner, uint64
 bool tc_prefill_ok(const nd_attn *h, const void *q) {
     const nd_attn_config &c = h->cfg;
     return (c.kv_dtype == ND_DT_BF16 || c.kv_dtype == ND_DT_F16) && c.act_dtype == c.kv_dtype &&
-           c.qk_head_dim == 64 && c.v_head_dim == 64 && c.block_size == 0 &&
+           c.qk_head_dim == 64 && c.v_head_dim == 64 && (c.block_size == 0 || c.block_size % 64 == 0) &&
            (reinterpret_cast<uintptr_t>(q) & 15u) == 0;
 }
 
@@ -625,6 +626,9 @@ int run_prefill_tc(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
     P.n_heads = c.n_heads;
     P.rep = h->rep;
     P.window = c.window;
+    P.btab = cv.btab;
+    P.blocks_per_seq = cv.blocks_per_seq;
+    P.block_shift = cv.block_shift;
     P.scale_log2 = 1.4426950408889634f / sqrtf((float)c.qk_head_dim);
     P.err = h->d_err;
     note_writer(h, kNoLayer);
@@ -746,7 +750,8 @@ int nd_attn_open(const nd_attn_config *cfg_in, nd_attn **out) {
     }
     if (cudaMalloc(&h->norms, (size_t)cfg.n_layers * 2 * cfg.qk_head_dim * sizeof(float)) != cudaSuccess ||
         cudaMalloc(&h->d_state, cfg.max_seqs * sizeof(SeqState)) != cudaSuccess ||
-        cudaMalloc(&h->d_err, sizeof(int)) != cudaSuccess)
+        cudaMalloc(&h->d_err, sizeof(int)) != cudaSuccess ||
+        cudaHostAlloc(reinterpret_cast<void **>(&h->err_pin), sizeof(int), cudaHostAllocDefault) != cudaSuccess)
         return bail(fail(ND_ATTN_ERR_NOMEM, "state allocation failed"));
     cudaMemsetAsync(h->d_state, 0, cfg.max_seqs * sizeof(SeqState), h->stream);
     cudaMemsetAsync(h->d_err, 0, sizeof(int), h->stream);
@@ -790,6 +795,7 @@ void nd_attn_close(nd_attn *h) {
     cudaFree(h->part_o); cudaFree(h->part_ml); cudaFree(h->counters);
     cudaFree(h->d_tok); cudaFree(h->d_u32); cudaFree(h->d_lean); cudaFree(h->d_err); cudaFree(h->dio); cudaFree(h->d_work); cudaFree(h->d_spans);
     if (h->pin) cudaFreeHost(h->pin);
+    if (h->err_pin) cudaFreeHost(h->err_pin);
     if (h->own) cudaStreamDestroy(h->own);
     delete h;
 }
@@ -1295,9 +1301,10 @@ int nd_attn_set_block_table(nd_attn *h, uint32_t seq, const int32_t *pages) {
 int nd_attn_sync(nd_attn *h) {
     if (!h) return fail(ND_ATTN_ERR_ARG, "null handle");
     DeviceGuard dg(h->cfg.device);
+    // The error word comes back with the stream's own work: one round trip.
+    ND_CUDA(cudaMemcpyAsync(h->err_pin, h->d_err, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
     ND_CUDA(cudaStreamSynchronize(h->stream));
-    int err = 0;
-    ND_CUDA(cudaMemcpy(&err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    const int err = *h->err_pin;
     if (err) {
         cudaMemset(h->d_err, 0, sizeof(int));
         cudaMemset(h->counters, 0, h->counter_cap * sizeof(int));

@@ -260,12 +260,18 @@ __global__ void __launch_bounds__(192, 2)
             uint32_t issued = 0;
             for (uint32_t j = 0; j < nkv; j++) {
                 const uint32_t st = j % STAGES;
+                // Cache row of key j * BN: contiguous, or through the block
+                // table (a 64-key tile lies in one page of >= 64 slots).
+                const uint32_t key = j * BN;
+                const int row = P.btab ? (int)(((uint32_t)P.btab[(size_t)w.seq * P.blocks_per_seq +
+                                                                   (key >> P.block_shift)]
+                                                << P.block_shift) |
+                                               (key & ((1u << P.block_shift) - 1u)))
+                                       : (int)(kv_row0 + key);
                 if (j >= STAGES && !mbar_wait(&B.kv_empty[st], ((j / STAGES) - 1) & 1, abort_flag)) break;
                 mbar_expect_tx(&B.kv_full[st], 2 * KV_BYTES);
-                tma_load_2d(smem_raw + OFF_K + st * KV_BYTES, &kmap, (int)(g * HD), (int)(kv_row0 + j * BN),
-                            &B.kv_full[st]);
-                tma_load_2d(smem_raw + OFF_V + st * KV_BYTES, &vmap, (int)(g * HD), (int)(kv_row0 + j * BN),
-                            &B.kv_full[st]);
+                tma_load_2d(smem_raw + OFF_K + st * KV_BYTES, &kmap, (int)(g * HD), row, &B.kv_full[st]);
+                tma_load_2d(smem_raw + OFF_V + st * KV_BYTES, &vmap, (int)(g * HD), row, &B.kv_full[st]);
                 issued = j + 1;
             }
             if (*abort_flag) {

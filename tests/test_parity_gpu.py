@@ -423,3 +423,16 @@ def test_tensor_core_prefill_ragged(dt, norm, gate):
     assert worst <= TOL
     check_caches(a, seqs, dt, 2, 1024)
     a.close()
+
+
+@pytest.mark.parametrize("dt", [O.BF16, O.F16])
+@pytest.mark.parametrize("block_size", [64, 128])
+def test_tensor_core_prefill_paged(dt, block_size):
+    """The tcgen05 prefill through a shuffled block table: key tiles fetched
+    page by page, a second prefill over the cached first (sinks pinned in
+    between), then decode steps on the balanced kernel; caches bit-exact."""
+    worst, a, seqs = run_session(dt, dt, 16, 4, 64, 64, 512, 2, [200, 77], seed=31, n_seqs=3, sink_after=1,
+                                 decode_steps=3, block_size=block_size, shuffle_pages=True)
+    assert worst <= TOL
+    check_caches(a, seqs, dt, 2, 512)
+    a.close()
