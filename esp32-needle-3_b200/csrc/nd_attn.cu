@@ -543,21 +543,46 @@ EncodeTiledFn encode_tiled() {
 
 // 2D map over rows of `inner` 16-bit elements (row stride `stride_bytes`), box
 // 64 elements x box_rows rows, 128-byte swizzle, out-of-range rows read as zero.
-int make_map(CUtensorMap *m, bool bf16, const void *base, uint64_t inner, uint64_t rows, uint64_t stride_bytes,
-             uint32_t box_rows, uint32_t box_inner, bool swizzle) {
+// 2D tensor map of `dt` elements (ND_DT_*): rows of `inner` elements,
+// `stride_bytes` apart; box `box_inner` x `box_rows`.
+int make_map_dt(CUtensorMap *m, int dt, const void *base, uint64_t inner, uint64_t rows, uint64_t stride_bytes,
+                uint32_t box_rows, uint32_t box_inner, bool swizzle) {
     EncodeTiledFn fn = encode_tiled();
     if (!fn) return fail(ND_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     const cuuint64_t dims[2] = {inner, rows};
     const cuuint64_t strides[1] = {stride_bytes};
     const cuuint32_t box[2] = {box_inner, box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                          const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+    const CUtensorMapDataType t = dt == ND_DT_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                  : dt == ND_DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const CUresult r = fn(m, t, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                           swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(ND_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return ND_ATTN_OK;
+}
+// The RoPE table (hd 64: 32 (cos, sin) pairs = 256 B per position) as a 3D
+// map [max_pos][2 halves][32 floats] with the 128-byte swizzle, box 32 x 2 x
+// 128: one prefill tile's 128 consecutive positions.
+int make_rope_map(CUtensorMap *m, const void *rope, uint32_t max_pos) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return fail(ND_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[3] = {32, 2, max_pos};
+    const cuuint64_t strides[2] = {128, 256};
+    const cuuint32_t box[3] = {32, 2, 128};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void *>(rope), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ND_ATTN_ERR_CUDA, "cuTensorMapEncodeTiled (rope) failed (%d)", (int)r);
+    return ND_ATTN_OK;
+}
+int make_map(CUtensorMap *m, bool bf16, const void *base, uint64_t inner, uint64_t rows, uint64_t stride_bytes,
+             uint32_t box_rows, uint32_t box_inner, bool swizzle) {
+    return make_map_dt(m, bf16 ? ND_DT_BF16 : ND_DT_F16, base, inner, rows, stride_bytes, box_rows, box_inner,
+                       swizzle);
 }
 
 // The tensor-core prefill serves 16-bit caches of head dim 64 in the
@@ -614,9 +639,17 @@ int run_prefill_tc(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
     int rc = make_map(&qm, bf16, q, (uint64_t)c.n_heads * 64, total, (uint64_t)c.n_heads * 64 * 2, 128, 64, true);
     if (!rc) rc = make_map(&km, bf16, cv.k, h->k_dim, h->rows_per_layer, (uint64_t)h->k_dim * 2, 64, 64, true);
     if (!rc) rc = make_map(&vm, bf16, cv.v, h->v_dim, h->rows_per_layer, (uint64_t)h->v_dim * 2, 64, 64, true);
+    // Output (and gate) tiles go through shared memory and TMA: 128 rows x 64
+    // elements of one head, 128-byte swizzle (f32 out: two 32-element boxes).
+    CUtensorMap om, csm;
+    const bool o32 = c.out_dtype == ND_DT_F32;
+    const uint64_t ocols = (uint64_t)c.n_heads * 64;
+    if (!rc) rc = make_map_dt(&om, c.out_dtype, out, ocols, total, ocols * (o32 ? 4 : 2), 128, o32 ? 32 : 64, true);
+    if (!rc) rc = make_rope_map(&csm, h->rope, c.max_pos);
     if (rc) return rc;
     nda::PrefillTcParams P;
     P.work = h->d_work;
+    P.n_work = h->n_work;
     P.rope = h->rope;
     P.qnorm = h->has_norm[layer] ? h->norms + (size_t)layer * 2 * c.qk_head_dim : nullptr;
     P.gate = gate;
@@ -632,7 +665,8 @@ int run_prefill_tc(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
     P.scale_log2 = 1.4426950408889634f / sqrtf((float)c.qk_head_dim);
     P.err = h->d_err;
     note_writer(h, kNoLayer);
-    ND_CUDA(nda::prefill_tc_launch(bf16, &qm, &km, &vm, P, h->n_work, h->stream));
+    const uint32_t grid = std::min<uint32_t>(h->n_work, 2u * (uint32_t)h->sm_count);   // persistent, 2 per SM
+    ND_CUDA(nda::prefill_tc_launch(bf16, &qm, &km, &vm, &om, &csm, P, grid, h->stream));
     h->launches++;
     return ND_ATTN_OK;
 }

@@ -44,6 +44,7 @@ struct PrefillWork {
 
 struct PrefillTcParams {
     const PrefillWork *work;
+    uint32_t n_work;
     const float2 *rope;
     const float *qnorm;
     const void *gate;
@@ -59,7 +60,10 @@ struct PrefillTcParams {
 size_t prefill_tc_smem_bytes();
 // qmap/kmap/vmap point to CUtensorMap objects (2D, 16-bit, box 64 x 128,
 // 128-byte swizzle) over q [tokens][n_heads*64], and one layer's K and V cache.
-cudaError_t prefill_tc_launch(bool bf16, const void *qmap, const void *kmap, const void *vmap,
-                              const PrefillTcParams &P, uint32_t n_work, cudaStream_t s);
+// omap: the output [tokens][n_heads*64] (box 64 x 128, f32: 32 x 128); csmap:
+// the RoPE table as [max_pos][2][32 floats] (box 32 x 2 x 128, 128-byte
+// swizzle). `grid` persistent CTAs walk the P.n_work items.
+cudaError_t prefill_tc_launch(bool bf16, const void *qmap, const void *kmap, const void *vmap, const void *omap,
+                              const void *csmap, const PrefillTcParams &P, uint32_t grid, cudaStream_t s);
 
 }  // namespace nda

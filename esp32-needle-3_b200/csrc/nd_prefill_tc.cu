@@ -8,23 +8,22 @@
 // first and guarantees the call does not wrap the ring, so slot == position).
 //
 // One CTA = one work item = 128 consecutive query tokens of one sequence for
-// one query head h (KV head g = h / rep), walking 128-key tiles. 6 warps:
+// one query head h (KV head g = h / rep), walking 64-key tiles. 6 warps:
 //   warps 0-3  one thread per query row (= TMEM lane): RoPE(+norm) of the Q
 //              row, per-row online softmax on S read from TMEM, P written back
 //              over S, lazy O rescaling (only when a row max grows by more than
 //              2^8), epilogue
-//   warp 4     TMA producer: Q tile once, then K/V tiles through a 2-stage ring
+//   warp 4     TMA producer: Q tile once, then K/V tiles through a 4-stage ring
+//              (contiguous cache rows, or page by page through the block table)
 //   warp 5     TMEM allocator + single-thread MMA issuer, an event loop that
 //              issues each PV as soon as its P is written and each S as soon
 //              as its K tile has landed and its buffer is free:
-//                S_j = Q K_j^T  (M=128, N=128, K=64; A = Q from TMEM, B = K smem)
-//                O  += P_j V_j  (M=128, N=64, K=128; A = P from TMEM, B = V smem,
+//                S_j = Q K_j^T  (M=128, N=64, K=64; A = Q from TMEM, B = K smem)
+//                O  += P_j V_j  (M=128, N=64, K=64; A = P from TMEM, B = V smem,
 //                                MN-major)
-// TMEM columns (256 per CTA, 2 CTAs per SM): the S/P buffer [0,128), O
-// [128,192), Q_hi [192,224), Q_lo [224,256). A tcgen05.mma costs at least ~46
-// cycles whatever its N, and reaches the tensor core's peak only from N=128 on,
-// so S uses 128-key tiles; the two CTAs of an SM overlap one CTA's softmax
-// with the other's MMAs.
+// TMEM columns (256 per CTA, 2 CTAs per SM): the S/P double buffer [0,128),
+// O [128,192), Q_hi [192,224), Q_lo [224,256). The two CTAs of an SM overlap
+// one CTA's softmax with the other's MMAs.
 //
 // Precision: bf16 rounds a value by up to 2^-9, which rows attending to few
 // keys (P) or normed rows with larger |q||k| (Q) turn into output errors above
@@ -62,18 +61,24 @@ constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t COL_S = 0, COL_O = 128, COL_QHI = 192, COL_QLO = 224;
 
 // Dynamic shared memory: Q landing tile, K and V stage rings (1024-byte
-// aligned tiles for the 128-byte swizzle), then the barrier block.
+// aligned tiles for the 128-byte swizzle), a 32 KB block, then the barrier
+// block. The 32 KB block first holds the tile's 128 RoPE table rows (256 B
+// each, 16-byte chunks XOR-swizzled by row so per-row reads are conflict-free),
+// then the gate tile (TMA) and the output tile for the TMA store (128 rows of
+// 128 B, 128-byte swizzle; f32 output: two such boxes).
 constexpr uint32_t OFF_Q = 0;
 constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
 constexpr uint32_t OFF_V = OFF_K + STAGES * KV_BYTES;
-constexpr uint32_t OFF_BAR = OFF_V + STAGES * KV_BYTES;
+constexpr uint32_t OFF_X = OFF_V + STAGES * KV_BYTES;
+constexpr uint32_t X_BYTES = BM * 256;       // 32 KB
+constexpr uint32_t OFF_BAR = OFF_X + X_BYTES;
 
 // Per S/P buffer b (tiles j with j % NB == b, phase j / NB): s_full (S
 // landed), p_full (P written), pv_done (PV read P and wrote O). Every wait
 // below is for the next phase to complete or the one just completed, never
 // further away, which is what makes the parity test exact.
 struct Bars {
-    uint64_t q_full, q_ready, drain;
+    uint64_t q_full, cs_full, q_ready, stage_full, x_free, drain;
     uint64_t s_full[NB], p_full[NB], pv_done[NB];
     uint64_t kv_full[STAGES], kv_empty[STAGES];
     uint32_t tmem_base;
@@ -207,11 +212,32 @@ __device__ __forceinline__ void write_p_chunk(const uint32_t (&sv)[32], uint32_t
 
 // Offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled tile.
 __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) { return r * 128u + ((c ^ (r & 7u)) << 4); }
+// Offset of 16-byte chunk `c` (0..15) of RoPE row `r` in the 32 KB block, as
+// the 3D map [pos][2 halves][32 floats] with the 128-byte swizzle lays it out:
+// 128-byte line 2r + half, chunk XOR (line & 7).
+__device__ __forceinline__ uint32_t cs_off(uint32_t r, uint32_t c) {
+    const uint32_t line = 2 * r + (c >> 3);
+    return line * 128u + (((c & 7u) ^ (line & 7u)) << 4);
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+            su32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(su32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+                 "r"(su32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
 
 template <bool BF16>
 __global__ void __launch_bounds__(192, 2)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                      const __grid_constant__ CUtensorMap vmap, const PrefillTcParams P) {
+                      const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap omap,
+                      const __grid_constant__ CUtensorMap csmap, const PrefillTcParams P) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (su32(smem_raw) & 1023u) {          // the swizzled tiles need 1024-byte alignment
@@ -221,14 +247,17 @@ __global__ void __launch_bounds__(192, 2)
     uint8_t *sq = smem_raw + OFF_Q;
     Bars &B = *reinterpret_cast<Bars *>(smem_raw + OFF_BAR);
     volatile int *abort_flag = &B.abort_flag;
-    const PrefillWork w = P.work[blockIdx.x];
-    const uint32_t g = w.head / P.rep;
-    const uint32_t nkv = (w.pos0 + w.t0 + w.rows + BN - 1) / BN;   // KV tiles this item reads
-    const uint32_t kv_row0 = w.seq * P.window;                      // cache row of position 0
+    // This CTA's items: blockIdx.x, + gridDim.x, ... of the longest-first list.
+    const uint32_t n_items = blockIdx.x < P.n_work ? (P.n_work - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    auto item = [&](uint32_t k) { return P.work[blockIdx.x + k * gridDim.x]; };
+    auto tiles_of = [](const PrefillWork &w) { return (w.pos0 + w.t0 + w.rows + BN - 1) / BN; };
 
     if (tid == 0) {
         mbar_init(&B.q_full, 1);
+        mbar_init(&B.cs_full, 1);
         mbar_init(&B.q_ready, BM / 32);       // one arrive per softmax warp
+        mbar_init(&B.stage_full, BM / 32);
+        mbar_init(&B.x_free, 1);
         mbar_init(&B.drain, 1);
         for (int b = 0; b < NB; b++) {
             mbar_init(&B.s_full[b], 1);
@@ -253,90 +282,109 @@ __global__ void __launch_bounds__(192, 2)
     const uint32_t tbase = B.tmem_base;
 
     if (warp == 4) {
-        // ---------------- TMA producer
+        // ---------------- TMA producer: per item its Q tile and RoPE rows, then
+        // its K/V tiles through the ring (global tile count gt)
         if (lane == 0) {
-            mbar_expect_tx(&B.q_full, Q_BYTES);
-            tma_load_2d(sq, &qmap, (int)(w.head * HD), (int)(w.tok_base + w.t0), &B.q_full);
-            uint32_t issued = 0;
-            for (uint32_t j = 0; j < nkv; j++) {
-                const uint32_t st = j % STAGES;
-                // Cache row of key j * BN: contiguous, or through the block
-                // table (a 64-key tile lies in one page of >= 64 slots).
-                const uint32_t key = j * BN;
-                const int row = P.btab ? (int)(((uint32_t)P.btab[(size_t)w.seq * P.blocks_per_seq +
-                                                                   (key >> P.block_shift)]
-                                                << P.block_shift) |
-                                               (key & ((1u << P.block_shift) - 1u)))
-                                       : (int)(kv_row0 + key);
-                if (j >= STAGES && !mbar_wait(&B.kv_empty[st], ((j / STAGES) - 1) & 1, abort_flag)) break;
-                mbar_expect_tx(&B.kv_full[st], 2 * KV_BYTES);
-                tma_load_2d(smem_raw + OFF_K + st * KV_BYTES, &kmap, (int)(g * HD), row, &B.kv_full[st]);
-                tma_load_2d(smem_raw + OFF_V + st * KV_BYTES, &vmap, (int)(g * HD), row, &B.kv_full[st]);
-                issued = j + 1;
+            uint32_t gt = 0, issued = 0, qi = 0, ci = 0;
+            for (uint32_t k = 0; k < n_items && !*abort_flag; k++) {
+                const PrefillWork w = item(k);
+                // Q landing tile: free once item k-1's rows are in TMEM.
+                if (k > 0 && !mbar_wait(&B.q_ready, (k - 1) & 1, abort_flag)) break;
+                mbar_expect_tx(&B.q_full, Q_BYTES);
+                tma_load_2d(sq, &qmap, (int)(w.head * HD), (int)(w.tok_base + w.t0), &B.q_full);
+                qi++;
+                // RoPE rows: the 32 KB block is free once item k-2's output
+                // tile has been read out of it (x_free, one phase per item).
+                if (k > 1 && !mbar_wait(&B.x_free, (k - 2) & 1, abort_flag)) break;
+                mbar_expect_tx(&B.cs_full, X_BYTES);
+                tma_load_3d(smem_raw + OFF_X, &csmap, 0, 0, (int)(w.pos0 + w.t0), &B.cs_full);
+                ci++;
+                const uint32_t nkv = tiles_of(w), g = w.head / P.rep, kv_row0 = w.seq * P.window;
+                for (uint32_t j = 0; j < nkv; j++, gt++) {
+                    const uint32_t st = gt % STAGES;
+                    // Cache row of key j * BN: contiguous, or through the block
+                    // table (a 64-key tile lies in one page of >= 64 slots).
+                    const uint32_t key = j * BN;
+                    const int row = P.btab ? (int)(((uint32_t)P.btab[(size_t)w.seq * P.blocks_per_seq +
+                                                                       (key >> P.block_shift)]
+                                                    << P.block_shift) |
+                                                   (key & ((1u << P.block_shift) - 1u)))
+                                           : (int)(kv_row0 + key);
+                    if (gt >= STAGES && !mbar_wait(&B.kv_empty[st], ((gt / STAGES) - 1) & 1, abort_flag)) break;
+                    mbar_expect_tx(&B.kv_full[st], 2 * KV_BYTES);
+                    tma_load_2d(smem_raw + OFF_K + st * KV_BYTES, &kmap, (int)(g * HD), row, &B.kv_full[st]);
+                    tma_load_2d(smem_raw + OFF_V + st * KV_BYTES, &vmap, (int)(g * HD), row, &B.kv_full[st]);
+                    issued = gt + 1;
+                }
             }
             if (*abort_flag) {
                 // Let the copies this thread issued land before the CTA goes away.
-                mbar_drain(&B.q_full, 0);
+                if (qi) mbar_drain(&B.q_full, (qi - 1) & 1);
+                if (ci) mbar_drain(&B.cs_full, (ci - 1) & 1);
                 if (issued) mbar_drain(&B.kv_full[(issued - 1) % STAGES], ((issued - 1) / STAGES) & 1);
             }
         }
     } else if (warp == 5) {
-        // ---------------- MMA issuer: S one tile ahead of PV
+        // ---------------- MMA issuer: per item, S one tile ahead of PV
         if (lane == 0) {
             constexpr uint32_t fmt = BF16 ? 1u : 0u;
             constexpr uint32_t id_s = idesc_f16(fmt, BM, BN, 0);
             constexpr uint32_t id_o = idesc_f16(fmt, BM, HD, 1);
-            bool ok = mbar_wait(&B.q_ready, 0, abort_flag);
-            uint32_t issued = 0;
-            // Event loop: issue whatever is ready, PV first (it frees an S
-            // buffer), then the next S. A barrier is only tested once the
-            // operation it tracks has been issued, so each test is for the
-            // next phase or the one just completed (the parity test is exact).
-            uint32_t sj = 0, pi = 0;                 // next S to issue, next PV to issue
-            long long idle_since = clock64();
-            while (ok && pi < nkv) {
-                bool progressed = false;
-                if (pi < sj && mbar_test(&B.p_full[pi % NB], (pi / NB) & 1)) {
-                    // O += P_pi V_pi (P in S buffer pi % NB, V in stage pi % STAGES).
-                    const uint32_t b = pi % NB, st = pi % STAGES;
-                    fence_after();
-                    const uint32_t v_addr = su32(smem_raw + OFF_V + st * KV_BYTES);
+            bool ok = true;
+            uint32_t issued = 0, gs = 0, gp = 0;     // next S / next PV to issue (global tiles)
+            for (uint32_t k = 0; ok && k < n_items; k++) {
+                const uint32_t g0 = gp, gend = gp + tiles_of(item(k));
+                ok = mbar_wait(&B.q_ready, k & 1, abort_flag);
+                // Event loop: issue whatever is ready, PV first (it frees an S
+                // buffer), then the next S. A barrier is only tested once the
+                // operation it tracks has been issued, so each test is for the
+                // next phase or the one just completed (the parity test is exact).
+                long long idle_since = clock64();
+                while (ok && gp < gend) {
+                    bool progressed = false;
+                    if (gp < gs && mbar_test(&B.p_full[gp % NB], (gp / NB) & 1)) {
+                        // O += P V (P in S buffer gp % NB, V in stage gp % STAGES).
+                        const uint32_t b = gp % NB, st = gp % STAGES;
+                        fence_after();
+                        const uint32_t v_addr = su32(smem_raw + OFF_V + st * KV_BYTES);
 #pragma unroll
-                    for (uint32_t kk = 0; kk < BN / 16; kk++) {
-                        const uint64_t vd = sdesc(v_addr + kk * 2048, KV_BYTES, 1024);
-                        const uint32_t pc = tbase + COL_S + b * BN + 32 * (kk / 2) + 8 * (kk % 2);
-                        umma_ts(tbase + COL_O, pc, vd, id_o, (pi > 0 || kk > 0) ? 1u : 0u);
-                        if constexpr (BF16) umma_ts(tbase + COL_O, pc + 16, vd, id_o, 1u);
+                        for (uint32_t kk = 0; kk < BN / 16; kk++) {
+                            const uint64_t vd = sdesc(v_addr + kk * 2048, KV_BYTES, 1024);
+                            const uint32_t pc = tbase + COL_S + b * BN + 32 * (kk / 2) + 8 * (kk % 2);
+                            umma_ts(tbase + COL_O, pc, vd, id_o, (gp > g0 || kk > 0) ? 1u : 0u);
+                            if constexpr (BF16) umma_ts(tbase + COL_O, pc + 16, vd, id_o, 1u);
+                        }
+                        umma_commit(&B.kv_empty[st]);
+                        umma_commit(&B.pv_done[b]);
+                        gp++;
+                        progressed = true;
                     }
-                    if (pi + STAGES < nkv) umma_commit(&B.kv_empty[st]);
-                    umma_commit(&B.pv_done[b]);
-                    pi++;
-                    progressed = true;
-                }
-                if (sj < nkv && (sj < NB || (pi > sj - NB && mbar_test(&B.pv_done[sj % NB], (sj / NB - 1) & 1))) &&
-                    mbar_test(&B.kv_full[sj % STAGES], (sj / STAGES) & 1)) {
-                    // S_sj = Q K_sj^T into buffer sj % NB (its previous P was read).
-                    const uint32_t b = sj % NB, st = sj % STAGES;
-                    fence_after();
-                    const uint32_t k_addr = su32(smem_raw + OFF_K + st * KV_BYTES);
+                    if (gs < gend && (gs < NB || (gp > gs - NB && mbar_test(&B.pv_done[gs % NB], (gs / NB - 1) & 1))) &&
+                        mbar_test(&B.kv_full[gs % STAGES], (gs / STAGES) & 1)) {
+                        // S = Q K^T into buffer gs % NB (its previous P was read).
+                        const uint32_t b = gs % NB, st = gs % STAGES;
+                        fence_after();
+                        const uint32_t k_addr = su32(smem_raw + OFF_K + st * KV_BYTES);
 #pragma unroll
-                    for (uint32_t kk = 0; kk < HD / 16; kk++) {
-                        const uint64_t kd = sdesc(k_addr + kk * 32, 16, 1024);
-                        umma_ts(tbase + COL_S + b * BN, tbase + COL_QHI + kk * 8, kd, id_s, kk > 0);
-                        if constexpr (BF16) umma_ts(tbase + COL_S + b * BN, tbase + COL_QLO + kk * 8, kd, id_s, 1u);
+                        for (uint32_t kk = 0; kk < HD / 16; kk++) {
+                            const uint64_t kd = sdesc(k_addr + kk * 32, 16, 1024);
+                            umma_ts(tbase + COL_S + b * BN, tbase + COL_QHI + kk * 8, kd, id_s, kk > 0);
+                            if constexpr (BF16)
+                                umma_ts(tbase + COL_S + b * BN, tbase + COL_QLO + kk * 8, kd, id_s, 1u);
+                        }
+                        umma_commit(&B.s_full[b]);
+                        gs++;
+                        issued = 1;
+                        progressed = true;
                     }
-                    umma_commit(&B.s_full[b]);
-                    sj++;
-                    issued = 1;
-                    progressed = true;
-                }
-                if (progressed) {
-                    idle_since = clock64();
-                } else if (*abort_flag) {
-                    ok = false;
-                } else if (clock64() - idle_since > kTimeoutCycles) {
-                    *abort_flag = 1;
-                    ok = false;
+                    if (progressed) {
+                        idle_since = clock64();
+                    } else if (*abort_flag) {
+                        ok = false;
+                    } else if (clock64() - idle_since > kTimeoutCycles) {
+                        *abort_flag = 1;
+                        ok = false;
+                    }
                 }
             }
             if (*abort_flag && issued) {
@@ -348,24 +396,28 @@ __global__ void __launch_bounds__(192, 2)
         // ---------------- softmax / correction / epilogue: thread = query row
         const uint32_t r = tid;
         const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
-        const uint32_t qpos = w.pos0 + w.t0 + r;                  // this row's position
-        const bool row_valid = r < w.rows;
-        bool ok = __all_sync(0xffffffffu, mbar_wait(&B.q_full, 0, abort_flag));
-        if (ok) {
-            // RoPE (after the optional per-head norm) of this row, split hi/lo
-            // into TMEM as the A operand of S = Q K^T.
-            const uint32_t pos_tab = row_valid ? qpos : w.pos0 + w.t0;
-            const float2 *cs = P.rope + (size_t)pos_tab * (HD / 2);
+        const float c = P.scale_log2;
+        bool ok = true, store_pending = false;
+        uint32_t n_stores = 0;
+
+        // Set-up of item k: RoPE (after the optional per-head norm) of this
+        // row, split hi/lo into TMEM as the A operand of S = Q K^T. The Q TMEM
+        // columns are free: the previous item's last S has completed.
+        auto setup = [&](uint32_t k) {
+            const PrefillWork w = item(k);
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(&B.q_full, k & 1, abort_flag));
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(&B.cs_full, k & 1, abort_flag));
+            if (!ok) return;
             float x[HD];
 #pragma unroll
-            for (int c = 0; c < 8; c++) {
-                const uint4 u = *reinterpret_cast<const uint4 *>(sq + swz(r, c));
+            for (int cq = 0; cq < 8; cq++) {
+                const uint4 u = *reinterpret_cast<const uint4 *>(sq + swz(r, cq));
                 const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
                     const float2 f = unpack2<BF16>(uu[e]);
-                    x[c * 8 + 2 * e] = f.x;
-                    x[c * 8 + 2 * e + 1] = f.y;
+                    x[cq * 8 + 2 * e] = f.x;
+                    x[cq * 8 + 2 * e + 1] = f.y;
                 }
             }
             float inv = 1.0f;
@@ -382,7 +434,8 @@ __global__ void __launch_bounds__(192, 2)
                     a = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, P.qnorm[i]), a), inv);
                     b = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, P.qnorm[i + HD / 2]), b), inv);
                 }
-                const float2 t = cs[i];
+                const float4 t4 = *reinterpret_cast<const float4 *>(smem_raw + OFF_X + cs_off(r, i >> 1));
+                const float2 t = (i & 1) ? make_float2(t4.z, t4.w) : make_float2(t4.x, t4.y);
                 x[i] = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(b, t.y));
                 x[i + HD / 2] = __fadd_rn(__fmul_rn(b, t.x), __fmul_rn(a, t.y));
             }
@@ -395,120 +448,205 @@ __global__ void __launch_bounds__(192, 2)
             fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&B.q_ready);
-        }
-        const float c = P.scale_log2;
-        float m = -INFINITY;
-        float2 l2 = make_float2(0.0f, 0.0f);   // row sum of P, two partial sums
-        for (uint32_t j = 0; ok && j < nkv; j++) {
-            const uint32_t b = j % NB, sbuf = lane_addr + COL_S + b * BN;
-            if (!__all_sync(0xffffffffu, mbar_wait(&B.s_full[b], (j / NB) & 1, abort_flag))) {
-                ok = false;
-                break;
+        };
+        // The previous output tile has been read out of the 32 KB block.
+        auto release_x = [&]() {
+            if (tid == 0 && store_pending) {
+                asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                mbar_arrive(&B.x_free);
+                store_pending = false;
             }
-            fence_after();
-            const int lim = (int)qpos - (int)(j * BN);   // keys [0, lim] of this tile are visible
-            const bool masked = !__all_sync(0xffffffffu, lim >= BN - 1);   // tile crosses the warp's diagonal
-            // Pass 1: the tile's row max (8 independent chains per 32 columns).
-            float mx[8];
-#pragma unroll
-            for (int k = 0; k < 8; k++) mx[k] = -INFINITY;
-#pragma unroll
-            for (int c2 = 0; c2 < BN / 32; c2++) {
-                uint32_t sv[32];
-                tmem_ld32(sbuf + 32 * c2, sv);
-                if (masked) {
-#pragma unroll
-                    for (int e = 0; e < 32; e++)
-                        if (c2 * 32 + e > lim) sv[e] = 0xff800000u;
-                }
-#pragma unroll
-                for (int e = 0; e < 32; e++) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(sv[e]));
-            }
-#pragma unroll
-            for (int w2 = 4; w2 > 0; w2 >>= 1)
-#pragma unroll
-                for (int k = 0; k < w2; k++) mx[k] = fmaxf(mx[k], mx[k + w2]);
-            const float tmax = mx[0] * c;
-            // Lazy rescale: keep the running max unless a row's max grew by more
-            // than 2^8; then O and l move to the new max (PV_{j-1} is done: S_j
-            // was issued after it).
-            const bool grow = j == 0 || tmax > m + 8.0f;
-            if (j > 0 && __any_sync(0xffffffffu, grow)) {
-                if (!__all_sync(0xffffffffu, mbar_wait(&B.pv_done[(j - 1) % NB], ((j - 1) / NB) & 1, abort_flag))) {
+        };
+
+        if (n_items) setup(0);
+        uint32_t gt = 0;
+        for (uint32_t k = 0; ok && k < n_items; k++) {
+            const PrefillWork w = item(k);
+            const uint32_t nkv = tiles_of(w), g0 = gt;
+            const uint32_t qpos = w.pos0 + w.t0 + r;                  // this row's position
+            const bool row_valid = r < w.rows;
+            float m = -INFINITY;
+            float2 l2 = make_float2(0.0f, 0.0f);   // row sum of P, two partial sums
+            for (uint32_t j = 0; j < nkv; j++, gt++) {
+                const uint32_t b = gt % NB, sbuf = lane_addr + COL_S + b * BN;
+                if (!__all_sync(0xffffffffu, mbar_wait(&B.s_full[b], (gt / NB) & 1, abort_flag))) {
                     ok = false;
                     break;
                 }
                 fence_after();
-                const float alpha = grow ? ex2(m - tmax) : 1.0f;
-                l2 = __fmul2_rn(l2, make_float2(alpha, alpha));
-                uint32_t ov[32];
+                const int lim = (int)qpos - (int)(j * BN);   // keys [0, lim] of this tile are visible
+                const bool masked = !__all_sync(0xffffffffu, lim >= BN - 1);   // tile crosses the warp's diagonal
+                // Pass 1: the tile's row max (8 independent chains per 32 columns).
+                float mx[8];
 #pragma unroll
-                for (int h2 = 0; h2 < HD / 32; h2++) {
-                    tmem_ld32(lane_addr + COL_O + h2 * 32, ov);
+                for (int kq = 0; kq < 8; kq++) mx[kq] = -INFINITY;
 #pragma unroll
-                    for (int e = 0; e < 32; e++) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-                    tmem_st32(lane_addr + COL_O + h2 * 32, ov);
+                for (int c2 = 0; c2 < BN / 32; c2++) {
+                    uint32_t sv[32];
+                    tmem_ld32(sbuf + 32 * c2, sv);
+                    if (masked) {
+#pragma unroll
+                        for (int e = 0; e < 32; e++)
+                            if (c2 * 32 + e > lim) sv[e] = 0xff800000u;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 32; e++) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(sv[e]));
                 }
-            }
-            if (grow) m = tmax;
-            // Pass 2: P = 2^(S*c - m) in hi/lo pairs over the S columns.
 #pragma unroll
-            for (int c2 = 0; c2 < BN / 32; c2++) {
-                uint32_t sv[32];
-                tmem_ld32(sbuf + 32 * c2, sv);
-                if (masked) {
+                for (int w2 = 4; w2 > 0; w2 >>= 1)
 #pragma unroll
-                    for (int e = 0; e < 32; e++)
-                        if (c2 * 32 + e > lim) sv[e] = 0xff800000u;
-                }
-                write_p_chunk<BF16>(sv, sbuf + 32 * c2, c, m, l2);
-            }
-            tmem_wait_st();
-            fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&B.p_full[b]);
-        }
-        // O is final once the last PV of every buffer is done.
-        for (uint32_t t = nkv > NB ? nkv - NB : 0; ok && t < nkv; t++)
-            if (!__all_sync(0xffffffffu, mbar_wait(&B.pv_done[t % NB], (t / NB) & 1, abort_flag))) ok = false;
-        if (ok) {
-            fence_after();
-            const float inv_l = 1.0f / (l2.x + l2.y);
-            const size_t obase = ((size_t)(w.tok_base + w.t0 + r) * P.n_heads + w.head) * HD;
+                    for (int kq = 0; kq < w2; kq++) mx[kq] = fmaxf(mx[kq], mx[kq + w2]);
+                const float tmax = mx[0] * c;
+                // Lazy rescale: keep the running max unless a row's max grew by
+                // more than 2^8; then O and l move to the new max (the previous
+                // PV is done: this S was issued after it).
+                const bool grow = j == 0 || tmax > m + 8.0f;
+                if (j > 0 && __any_sync(0xffffffffu, grow)) {
+                    if (!__all_sync(0xffffffffu,
+                                    mbar_wait(&B.pv_done[(gt - 1) % NB], ((gt - 1) / NB) & 1, abort_flag))) {
+                        ok = false;
+                        break;
+                    }
+                    fence_after();
+                    const float alpha = grow ? ex2(m - tmax) : 1.0f;
+                    l2 = __fmul2_rn(l2, make_float2(alpha, alpha));
+                    uint32_t ov[32];
 #pragma unroll
-            for (int h2 = 0; h2 < HD / 32; h2++) {
-                uint32_t ov[32];
-                tmem_ld32(lane_addr + COL_O + h2 * 32, ov);
-                if (!row_valid) continue;
-                float val[32];
+                    for (int h2 = 0; h2 < HD / 32; h2++) {
+                        tmem_ld32(lane_addr + COL_O + h2 * 32, ov);
 #pragma unroll
-                for (int e = 0; e < 32; e++) {
-                    val[e] = __uint_as_float(ov[e]) * inv_l;
-                    if (P.gate)
-                        val[e] *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, obase + h2 * 32 + e) *
-                                                    1.4426950408889634f));
-                }
-                if (P.out_dt == DT_F32) {
-                    float4 *o4 = reinterpret_cast<float4 *>(static_cast<float *>(P.out) + obase + h2 * 32);
-#pragma unroll
-                    for (int e = 0; e < 8; e++)
-                        o4[e] = make_float4(val[4 * e], val[4 * e + 1], val[4 * e + 2], val[4 * e + 3]);
-                } else {
-                    uint4 *o4 = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(P.out) + obase + h2 * 32);
-                    const bool obf = P.out_dt == DT_BF16;
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        uint32_t wd[4];
-#pragma unroll
-                        for (int f = 0; f < 4; f++) {
-                            const float a = val[8 * e + 2 * f], bb = val[8 * e + 2 * f + 1];
-                            wd[f] = obf ? pack2<true>(a, bb) : pack2<false>(a, bb);
-                        }
-                        o4[e] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+                        for (int e = 0; e < 32; e++) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+                        tmem_st32(lane_addr + COL_O + h2 * 32, ov);
                     }
                 }
+                if (grow) m = tmax;
+                // Pass 2: P = 2^(S*c - m) over the S columns.
+#pragma unroll
+                for (int c2 = 0; c2 < BN / 32; c2++) {
+                    uint32_t sv[32];
+                    tmem_ld32(sbuf + 32 * c2, sv);
+                    if (masked) {
+#pragma unroll
+                        for (int e = 0; e < 32; e++)
+                            if (c2 * 32 + e > lim) sv[e] = 0xff800000u;
+                    }
+                    write_p_chunk<BF16>(sv, sbuf + 32 * c2, c, m, l2);
+                }
+                tmem_wait_st();
+                fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&B.p_full[b]);
+                if (j == 0) release_x();
             }
+            if (!ok) break;
+            // The next item's queries go into TMEM now (its first S can run
+            // under this item's epilogue).
+            if (k + 1 < n_items) setup(k + 1);
+            // O is final once the last PV of every buffer is done.
+            for (uint32_t t = gt - g0 > NB ? gt - NB : g0; ok && t < gt; t++)
+                if (!__all_sync(0xffffffffu, mbar_wait(&B.pv_done[t % NB], (t / NB) & 1, abort_flag))) ok = false;
+            if (!ok) break;
+            fence_after();
+            const float inv_l = 1.0f / (l2.x + l2.y);
+            if (w.rows == BM) {
+                // Whole tile: this row's output into the 32 KB block (128-byte
+                // swizzle, the layout of the output map), then one TMA store.
+                const size_t obase = ((size_t)(w.tok_base + w.t0 + r) * P.n_heads + w.head) * HD;
+#pragma unroll
+                for (int h2 = 0; h2 < HD / 32; h2++) {
+                    uint32_t ov[32];
+                    tmem_ld32(lane_addr + COL_O + h2 * 32, ov);
+                    float val[32];
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        val[e] = __uint_as_float(ov[e]) * inv_l;
+                        if (P.gate)
+                            val[e] *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, obase + h2 * 32 + e) *
+                                                        1.4426950408889634f));
+                    }
+                    if (P.out_dt == DT_F32) {
+#pragma unroll
+                        for (int e = 0; e < 8; e++)
+                            *reinterpret_cast<float4 *>(smem_raw + OFF_X + h2 * Q_BYTES + swz(r, e)) =
+                                make_float4(val[4 * e], val[4 * e + 1], val[4 * e + 2], val[4 * e + 3]);
+                    } else {
+                        const bool obf = P.out_dt == DT_BF16;
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            uint32_t wd[4];
+#pragma unroll
+                            for (int f = 0; f < 4; f++) {
+                                const float a = val[8 * e + 2 * f], bb = val[8 * e + 2 * f + 1];
+                                wd[f] = obf ? pack2<true>(a, bb) : pack2<false>(a, bb);
+                            }
+                            *reinterpret_cast<uint4 *>(smem_raw + OFF_X + swz(r, 4 * h2 + e)) =
+                                make_uint4(wd[0], wd[1], wd[2], wd[3]);
+                        }
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> TMA reads
+                fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&B.stage_full);
+                if (tid == 0) {
+                    if (!mbar_wait(&B.stage_full, n_stores & 1, abort_flag)) {
+                        ok = false;
+                    } else {
+                        const int y = (int)(w.tok_base + w.t0);
+                        tma_store_2d(&omap, smem_raw + OFF_X, (int)(w.head * HD), y);
+                        if (P.out_dt == DT_F32)
+                            tma_store_2d(&omap, smem_raw + OFF_X + Q_BYTES, (int)(w.head * HD + 32), y);
+                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                        store_pending = true;
+                    }
+                }
+                n_stores++;
+            } else {
+                // Partial tile (the end of a sequence): direct row stores.
+                const size_t obase = ((size_t)(w.tok_base + w.t0 + r) * P.n_heads + w.head) * HD;
+#pragma unroll
+                for (int h2 = 0; h2 < HD / 32; h2++) {
+                    uint32_t ov[32];
+                    tmem_ld32(lane_addr + COL_O + h2 * 32, ov);
+                    if (!row_valid) continue;
+                    float val[32];
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        val[e] = __uint_as_float(ov[e]) * inv_l;
+                        if (P.gate)
+                            val[e] *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, obase + h2 * 32 + e) *
+                                                        1.4426950408889634f));
+                    }
+                    if (P.out_dt == DT_F32) {
+                        float4 *o4 = reinterpret_cast<float4 *>(static_cast<float *>(P.out) + obase + h2 * 32);
+#pragma unroll
+                        for (int e = 0; e < 8; e++)
+                            o4[e] = make_float4(val[4 * e], val[4 * e + 1], val[4 * e + 2], val[4 * e + 3]);
+                    } else {
+                        uint4 *o4 = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(P.out) + obase + h2 * 32);
+                        const bool obf = P.out_dt == DT_BF16;
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            uint32_t wd[4];
+#pragma unroll
+                            for (int f = 0; f < 4; f++) {
+                                const float a = val[8 * e + 2 * f], bb = val[8 * e + 2 * f + 1];
+                                wd[f] = obf ? pack2<true>(a, bb) : pack2<false>(a, bb);
+                            }
+                            o4[e] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+                        }
+                    }
+                }
+                // The 32 KB block was not used: released at once.
+                fence_before();
+                __syncwarp();
+                if (tid == 0) mbar_arrive(&B.x_free);
+            }
+            // O is read: the next item's first PV may overwrite it (its P is
+            // only written after this point).
+            tmem_wait_ld();
         }
+        if (tid == 0 && store_pending) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
     }
 
     fence_before();
@@ -524,22 +662,24 @@ __global__ void __launch_bounds__(192, 2)
 
 size_t prefill_tc_smem_bytes() { return SMEM_BYTES; }
 
-cudaError_t prefill_tc_launch(bool bf16, const void *qmap, const void *kmap, const void *vmap,
-                              const PrefillTcParams &P, uint32_t n_work, cudaStream_t s) {
+cudaError_t prefill_tc_launch(bool bf16, const void *qmap, const void *kmap, const void *vmap, const void *omap,
+                              const void *csmap, const PrefillTcParams &P, uint32_t grid, cudaStream_t s) {
     const CUtensorMap &q = *static_cast<const CUtensorMap *>(qmap);
     const CUtensorMap &k = *static_cast<const CUtensorMap *>(kmap);
     const CUtensorMap &v = *static_cast<const CUtensorMap *>(vmap);
+    const CUtensorMap &o = *static_cast<const CUtensorMap *>(omap);
+    const CUtensorMap &cs = *static_cast<const CUtensorMap *>(csmap);
     const size_t smem = prefill_tc_smem_bytes();
     if (bf16) {
         cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
         if (e != cudaSuccess) return e;
-        prefill_tc_kernel<true><<<n_work, 192, smem, s>>>(q, k, v, P);
+        prefill_tc_kernel<true><<<grid, 192, smem, s>>>(q, k, v, o, cs, P);
     } else {
         cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
         if (e != cudaSuccess) return e;
-        prefill_tc_kernel<false><<<n_work, 192, smem, s>>>(q, k, v, P);
+        prefill_tc_kernel<false><<<grid, 192, smem, s>>>(q, k, v, o, cs, P);
     }
     return cudaGetLastError();
 }
