@@ -436,3 +436,41 @@ def test_tensor_core_prefill_paged(dt, block_size):
     assert worst <= TOL
     check_caches(a, seqs, dt, 2, 512)
     a.close()
+
+
+@pytest.mark.parametrize("dt", [O.BF16, O.F16])
+@pytest.mark.parametrize("gate", [False, True])
+def test_tensor_core_prefill_16bit_out(dt, gate):
+    """The tcgen05 prefill writing 16-bit outputs: whole 128-row tiles leave
+    through shared memory and a TMA store, the last partial tile through row
+    stores. Bar: TOL plus the output dtype's own rounding (half an ulp)."""
+    import torch
+    from harness import torch_dtype
+    rng = np.random.default_rng(41)
+    H, HKV, D, W, n_seqs = 16, 4, 64, 512, 2
+    lens = [300, 256]
+    a = ndattn.Attn(n_layers=1, n_heads=H, n_kv_heads=HKV, qk_head_dim=D, v_head_dim=D, window=W,
+                    max_seqs=n_seqs, kv_dtype=dt, act_dtype=dt, out_dtype=dt, max_pos=W)
+    seqs = [O.OracleSeq(1, H, HKV, D, D, W, dt, max_pos=W) for _ in range(n_seqs)]
+    T = sum(lens)
+    q = (rng.standard_normal((T, H * D)) * 0.5).astype(np.float32)
+    k = (rng.standard_normal((T, HKV * D)) * 0.5).astype(np.float32)
+    v = (rng.standard_normal((T, HKV * D)) * 0.5).astype(np.float32)
+    gt = rng.standard_normal((T, H * D)).astype(np.float32) if gate else None
+    out = torch.zeros((T, H * D), dtype=torch_dtype(dt), device="cuda")
+    a.prefill(0, lens, dev(q, dt), dev(k, dt), dev(v, dt), out, gate=None if gt is None else dev(gt, dt))
+    a.sync()
+    got = out.float().cpu().numpy()
+    ulp = 2.0 ** (-8 if dt == O.BF16 else -11)   # half an ulp relative, 8 / 11 significand bits
+    worst = 0.0
+    r0 = 0
+    for s, n in enumerate(lens):
+        for t in range(n):
+            r = r0 + t
+            want = np.asarray(seqs[s].step(0, O.round_act(q[r], dt), O.round_act(k[r], dt), O.round_act(v[r], dt),
+                                           None if gt is None else O.round_act(gt[r], dt), off=t)).reshape(H, D)
+            err = np.abs(got[r].reshape(H, D) - want) - ulp * np.abs(want)
+            worst = max(worst, float(np.max(err / np.maximum(1.0, np.abs(want)))))
+        r0 += n
+    assert worst <= TOL
+    a.close()
