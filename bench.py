@@ -306,11 +306,19 @@ def run_decode(args, world, rank, local, dist):
     a.sync()
     if world > 1:
         dist.barrier()
+    # The host pointers a C caller would hold, taken before the timed region;
+    # each call is the C entry point itself (copies in, kernel, copies out, wait).
+    lib = ndattn.load()
+    ptrs = [[(qh[i, l].data_ptr(), kh[i, l].data_ptr(), vh[i, l].data_ptr(), oh[l].data_ptr())
+             for l in range(LAYERS)] for i in range(e2e_steps)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(e2e_steps):
         for l in range(LAYERS):
-            a.decode_host(l, BATCH, qh[i, l].numpy(), kh[i, l].numpy(), vh[i, l].numpy(), oh[l].numpy())
+            qp, kp, vp, op = ptrs[i][l]
+            rc = lib.nd_attn_decode_host(a.h, l, BATCH, None, qp, kp, vp, None, op)
+            if rc:
+                raise RuntimeError(f"nd_attn_decode_host failed ({rc}): {lib.nd_attn_last_error()}")
         a.advance(BATCH)
     e1.record(stream)
     a.sync()
