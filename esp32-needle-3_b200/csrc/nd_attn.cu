@@ -85,19 +85,28 @@ __global__ void advance_kernel(SeqState *st, uint32_t n, const uint32_t *ids, co
 // Copies whole cache rows between a (layer-strided) cache and a dense buffer:
 // dense row (l, r) <-> cache row phys_row(seq, slot0 + r) of layer l.
 // `to_cache` selects the direction. Row sizes are multiples of 4 bytes.
+// vbig: when copying into a bf16 V cache, the flag of the first layer copied
+// (layer blockIdx.y's flag is vbig[blockIdx.y]); nullptr otherwise.
 __global__ void rows_copy_kernel(char *cache, size_t layer_stride, char *dense, size_t dense_layer_stride,
                                  uint32_t row_words, uint32_t n_rows, CacheView c, uint32_t seq,
-                                 uint32_t slot0, int to_cache) {
+                                 uint32_t slot0, int to_cache, int *vbig) {
     const uint32_t l = blockIdx.y;
+    bool big = false;
     for (uint32_t r = blockIdx.x; r < n_rows; r += gridDim.x) {
         const size_t pr = nda::phys_row(c, seq, slot0 + r);
         uint32_t *cw = reinterpret_cast<uint32_t *>(cache + l * layer_stride) + pr * row_words;
         uint32_t *dw = reinterpret_cast<uint32_t *>(dense + l * dense_layer_stride) + (size_t)r * row_words;
         for (uint32_t w = threadIdx.x; w < row_words; w += blockDim.x) {
-            if (to_cache) cw[w] = dw[w];
-            else dw[w] = cw[w];
+            if (to_cache) {
+                const uint32_t x = dw[w];
+                cw[w] = x;
+                big |= vbig != nullptr && nda::bf16x2_big(x);
+            } else {
+                dw[w] = cw[w];
+            }
         }
     }
+    if (big) atomicOr(vbig + l, 1);
 }
 
 }  // namespace
@@ -150,6 +159,7 @@ struct nd_attn {
     void *pin = nullptr;
     size_t pin_cap = 0;
     int *err_pin = nullptr;   // pinned host copy of d_err, read once per sync
+    int *d_vbig = nullptr;    // per layer: a bf16 V value f16 cannot represent was stored (sticky)
     void *dio = nullptr;
     size_t dio_cap = 0;
     uint64_t launches = 0;
@@ -196,6 +206,7 @@ CacheView layer_view(const nd_attn *h, uint32_t layer) {
     c.btab = h->cfg.block_size ? h->d_btab : nullptr;
     c.blocks_per_seq = h->blocks_per_seq;
     c.block_shift = h->block_shift;
+    c.vbig = h->cfg.kv_dtype == ND_DT_BF16 ? h->d_vbig + layer : nullptr;
     return c;
 }
 
@@ -660,6 +671,7 @@ int run_prefill_tc(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
     P.rep = h->rep;
     P.window = c.window;
     P.btab = cv.btab;
+    P.vbig = cv.vbig;
     P.blocks_per_seq = cv.blocks_per_seq;
     P.block_shift = cv.block_shift;
     P.scale_log2 = 1.4426950408889634f / sqrtf((float)c.qk_head_dim);
@@ -667,7 +679,7 @@ int run_prefill_tc(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
     note_writer(h, kNoLayer);
     const uint32_t grid = std::min<uint32_t>(h->n_work, 2u * (uint32_t)h->sm_count);   // persistent, 2 per SM
     ND_CUDA(nda::prefill_tc_launch(bf16, &qm, &km, &vm, &om, &csm, P, grid, h->stream));
-    h->launches++;
+    h->launches += bf16 ? 2 : 1;
     return ND_ATTN_OK;
 }
 
@@ -785,10 +797,12 @@ int nd_attn_open(const nd_attn_config *cfg_in, nd_attn **out) {
     if (cudaMalloc(&h->norms, (size_t)cfg.n_layers * 2 * cfg.qk_head_dim * sizeof(float)) != cudaSuccess ||
         cudaMalloc(&h->d_state, cfg.max_seqs * sizeof(SeqState)) != cudaSuccess ||
         cudaMalloc(&h->d_err, sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&h->d_vbig, cfg.n_layers * sizeof(int)) != cudaSuccess ||
         cudaHostAlloc(reinterpret_cast<void **>(&h->err_pin), sizeof(int), cudaHostAllocDefault) != cudaSuccess)
         return bail(fail(ND_ATTN_ERR_NOMEM, "state allocation failed"));
     cudaMemsetAsync(h->d_state, 0, cfg.max_seqs * sizeof(SeqState), h->stream);
     cudaMemsetAsync(h->d_err, 0, sizeof(int), h->stream);
+    cudaMemsetAsync(h->d_vbig, 0, cfg.n_layers * sizeof(int), h->stream);
     if (cfg.block_size) {
         const size_t nb = (size_t)cfg.max_seqs * h->blocks_per_seq;
         std::vector<int32_t> ident(nb);
@@ -827,7 +841,7 @@ void nd_attn_close(nd_attn *h) {
     cudaFree(h->kc); cudaFree(h->vc); cudaFree(h->ks); cudaFree(h->vs);
     cudaFree(h->rope); cudaFree(h->norms); cudaFree(h->d_state); cudaFree(h->d_btab);
     cudaFree(h->part_o); cudaFree(h->part_ml); cudaFree(h->counters);
-    cudaFree(h->d_tok); cudaFree(h->d_u32); cudaFree(h->d_lean); cudaFree(h->d_err); cudaFree(h->dio); cudaFree(h->d_work); cudaFree(h->d_spans);
+    cudaFree(h->d_tok); cudaFree(h->d_u32); cudaFree(h->d_lean); cudaFree(h->d_vbig); cudaFree(h->d_err); cudaFree(h->dio); cudaFree(h->d_work); cudaFree(h->d_spans);
     if (h->pin) cudaFreeHost(h->pin);
     if (h->err_pin) cudaFreeHost(h->err_pin);
     if (h->own) cudaStreamDestroy(h->own);
@@ -1206,7 +1220,7 @@ nd_attn_prefix *nd_attn_prefix_save(nd_attn *h, uint32_t seq) {
         note_writer(h, kAllLayers);
         rows_copy_kernel<<<dim3(std::min<uint32_t>(live, 1024u), c.n_layers), 128, 0, h->stream>>>(
             static_cast<char *>(parts[i].base), h->rows_per_layer * parts[i].row, dst, live * parts[i].row,
-            (uint32_t)(parts[i].row / 4), live, cv, seq, 0, 0);
+            (uint32_t)(parts[i].row / 4), live, cv, seq, 0, 0, nullptr);
         h->launches++;
         dst += (size_t)c.n_layers * live * parts[i].row;
     }
@@ -1237,7 +1251,8 @@ int nd_attn_prefix_restore(nd_attn *h, uint32_t seq, const nd_attn_prefix *p) {
         note_writer(h, kAllLayers);
         rows_copy_kernel<<<dim3(std::min<uint32_t>(p->live, 1024u), c.n_layers), 128, 0, h->stream>>>(
             static_cast<char *>(parts[i].base), h->rows_per_layer * parts[i].row, src, p->live * parts[i].row,
-            (uint32_t)(parts[i].row / 4), p->live, cv, seq, 0, 1);
+            (uint32_t)(parts[i].row / 4), p->live, cv, seq, 0, 1,
+            i == 1 && c.kv_dtype == ND_DT_BF16 ? h->d_vbig : nullptr);
         h->launches++;
         src += (size_t)c.n_layers * p->live * parts[i].row;
     }
@@ -1298,7 +1313,7 @@ static int cache_io(nd_attn *h, uint32_t layer, uint32_t seq, uint32_t slot0, ui
         note_writer(h, kAllLayers);
         rows_copy_kernel<<<dim3(std::min<uint32_t>(n_slots, 4096u), 1), 128, 0, h->stream>>>(
             static_cast<char *>(parts[i].cache), 0, dense, 0, (uint32_t)(parts[i].row / 4), n_slots, cv, seq,
-            slot0, to_cache);
+            slot0, to_cache, to_cache && i == 1 ? cv.vbig : nullptr);
         h->launches++;
         ND_CUDA(cudaGetLastError());
         if (!to_cache) ND_CUDA(cudaMemcpyAsync(parts[i].user, d + off, nb, cudaMemcpyDeviceToHost, h->stream));

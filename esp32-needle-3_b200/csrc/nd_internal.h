@@ -52,6 +52,7 @@ struct PrefillTcParams {
     int act_dt, out_dt;
     uint32_t n_heads, rep, window;
     const int32_t *btab;        // paged cache: block table [seq][blocks_per_seq], or nullptr
+    const int *vbig;            // bf16: the layer's flag (V holds a value f16 cannot represent)
     uint32_t blocks_per_seq, block_shift;   // pages of 2^block_shift (>= 64) slots
     float scale_log2;
     int *err;

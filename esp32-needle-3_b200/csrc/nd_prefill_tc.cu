@@ -180,9 +180,31 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t 
     lo = pack2<BF16>(a - h.x, b - h.y);
 }
 
-// P = 2^(S*c - m) for 32 keys of a row, written over their S columns as
-// hi/lo 16-bit pairs (16 columns of hi, then 16 of lo); the row sum goes into l2.
-template <bool BF16>
+// 2^t for a pair on the FMA pipe, to take load off the MUFU unit (which the
+// softmax warps otherwise saturate): t = n + f with n = RN(t) (the 1.5 * 2^23
+// addition leaves n in the low mantissa bits), 2^f on [-1/2, 1/2] by a cubic
+// fitted to 2^f by least squares on the relative error at Chebyshev nodes
+// (max relative error 7.7e-5 in float32, below f16's own 4.9e-4 rounding of
+// P), then n added to the exponent field. t is clamped at -125 first, so the
+// exponent stays in range (masked scores, t = -inf, give 2^-125 ~ 0).
+__device__ __forceinline__ float2 exp2_poly2(float2 t) {
+    t = make_float2(fmaxf(t.x, -125.0f), fmaxf(t.y, -125.0f));
+    const float2 magic = make_float2(12582912.0f, 12582912.0f);
+    const float2 y = __fadd2_rn(t, magic);
+    const float2 f = __fadd2_rn(t, __fadd2_rn(magic, make_float2(-y.x, -y.y)));
+    float2 p = __ffma2_rn(make_float2(0.05508868396282196f, 0.05508868396282196f), f,
+                          make_float2(0.24260404706001282f, 0.24260404706001282f));
+    p = __ffma2_rn(p, f, make_float2(0.6932762265205383f, 0.6932762265205383f));
+    p = __ffma2_rn(p, f, make_float2(0.9999289512634277f, 0.9999289512634277f));
+    return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(y.x) << 23)),
+                       __int_as_float(__float_as_int(p.y) + (__float_as_int(y.y) << 23)));
+}
+
+// P = 2^(S*c - m) for 32 keys of a row, written over their S columns: with
+// PSPLIT as hi/lo bf16 pairs (16 columns of hi, then 16 of lo), else as single
+// f16 pairs (16 columns; one pair in four through exp2_poly2). The row sum
+// goes into l2.
+template <bool PSPLIT>
 __device__ __forceinline__ void write_p_chunk(const uint32_t (&sv)[32], uint32_t taddr, float c, float m, float2 &l2) {
     const float2 c2v = make_float2(c, c), nm2 = make_float2(-m, -m), neg1 = make_float2(-1.0f, -1.0f);
     float2 acc[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
@@ -191,9 +213,15 @@ __device__ __forceinline__ void write_p_chunk(const uint32_t (&sv)[32], uint32_t
     for (int e = 0; e < 32; e += 2) {
         const float2 sp = make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
         const float2 t = __ffma2_rn(sp, c2v, nm2);
-        const float2 pp = make_float2(ex2(t.x), ex2(t.y));
+        float2 pp;
+        if constexpr (!PSPLIT) {
+            if ((e / 2) % 4 == 3) pp = exp2_poly2(t);
+            else pp = make_float2(ex2(t.x), ex2(t.y));
+        } else {
+            pp = make_float2(ex2(t.x), ex2(t.y));
+        }
         acc[(e >> 1) & 1] = __fadd2_rn(acc[(e >> 1) & 1], pp);
-        if constexpr (BF16) {
+        if constexpr (PSPLIT) {
             // hi = the upper halves (truncated bf16), lo = RN(p - hi): p - hi is
             // exact in fp32, so hi + lo keeps ~16 bits of p.
             const uint32_t u0 = __float_as_uint(pp.x), u1 = __float_as_uint(pp.y);
@@ -205,7 +233,7 @@ __device__ __forceinline__ void write_p_chunk(const uint32_t (&sv)[32], uint32_t
             pk[e / 2] = pack2<false>(pp.x, pp.y);
         }
     }
-    if constexpr (BF16) tmem_st32(taddr, pk);
+    if constexpr (PSPLIT) tmem_st32(taddr, pk);
     else tmem_st16(taddr, pk);
     l2 = __fadd2_rn(l2, __fadd2_rn(acc[0], acc[1]));
 }
@@ -233,11 +261,21 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void 
                  : "memory");
 }
 
-template <bool BF16>
+// BF16 = 16-bit type of the cache and activations. PVF16 (bf16 only): P and
+// V in f16 for PV, V tiles converted in shared memory by the softmax warps
+// (exact while the layer's V holds no value of |x| >= 2^16, Inf or NaN);
+// otherwise P goes as a bf16 hi/lo pair. Both bf16 variants are launched one
+// after the other; each exits at once unless the layer's flag selects it.
+template <bool BF16, bool PVF16>
 __global__ void __launch_bounds__(192, 2)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap omap,
                       const __grid_constant__ CUtensorMap csmap, const PrefillTcParams P) {
+    constexpr bool PSPLIT = BF16 && !PVF16;   // P as a bf16 hi/lo pair (two PV MMAs per k-step)
+    if constexpr (BF16) {
+        const bool big = P.vbig == nullptr || *reinterpret_cast<const volatile int *>(P.vbig) != 0;
+        if (big == PVF16) return;   // the other variant serves this call
+    }
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (su32(smem_raw) & 1023u) {          // the swizzled tiles need 1024-byte alignment
@@ -329,7 +367,7 @@ __global__ void __launch_bounds__(192, 2)
         if (lane == 0) {
             constexpr uint32_t fmt = BF16 ? 1u : 0u;
             constexpr uint32_t id_s = idesc_f16(fmt, BM, BN, 0);
-            constexpr uint32_t id_o = idesc_f16(fmt, BM, HD, 1);
+            constexpr uint32_t id_o = idesc_f16(PSPLIT ? 1u : 0u, BM, HD, 1);   // P and V: bf16 pair or f16
             bool ok = true;
             uint32_t issued = 0, gs = 0, gp = 0;     // next S / next PV to issue (global tiles)
             for (uint32_t k = 0; ok && k < n_items; k++) {
@@ -352,7 +390,7 @@ __global__ void __launch_bounds__(192, 2)
                             const uint64_t vd = sdesc(v_addr + kk * 2048, KV_BYTES, 1024);
                             const uint32_t pc = tbase + COL_S + b * BN + 32 * (kk / 2) + 8 * (kk % 2);
                             umma_ts(tbase + COL_O, pc, vd, id_o, (gp > g0 || kk > 0) ? 1u : 0u);
-                            if constexpr (BF16) umma_ts(tbase + COL_O, pc + 16, vd, id_o, 1u);
+                            if constexpr (PSPLIT) umma_ts(tbase + COL_O, pc + 16, vd, id_o, 1u);
                         }
                         umma_commit(&B.kv_empty[st]);
                         umma_commit(&B.pv_done[b]);
@@ -530,7 +568,22 @@ __global__ void __launch_bounds__(192, 2)
                         for (int e = 0; e < 32; e++)
                             if (c2 * 32 + e > lim) sv[e] = 0xff800000u;
                     }
-                    write_p_chunk<BF16>(sv, sbuf + 32 * c2, c, m, l2);
+                    write_p_chunk<PSPLIT>(sv, sbuf + 32 * c2, c, m, l2);
+                }
+                if constexpr (BF16 && PVF16) {
+                    // V tile of this stage to f16 in place (exact: the layer's
+                    // V holds no value f16 cannot represent), a quarter per warp.
+                    uint4 *vt = reinterpret_cast<uint4 *>(smem_raw + OFF_V + (gt % STAGES) * KV_BYTES);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        uint4 u = vt[r + i * BM];
+                        uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                        for (int e = 0; e < 4; e++)
+                            wv[e] = pack2<false>(__uint_as_float(wv[e] << 16), __uint_as_float(wv[e] & 0xffff0000u));
+                        vt[r + i * BM] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> MMA reads
                 }
                 tmem_wait_st();
                 fence_before();
@@ -551,37 +604,54 @@ __global__ void __launch_bounds__(192, 2)
             if (w.rows == BM) {
                 // Whole tile: this row's output into the 32 KB block (128-byte
                 // swizzle, the layout of the output map), then one TMA store.
-                const size_t obase = ((size_t)(w.tok_base + w.t0 + r) * P.n_heads + w.head) * HD;
+                // Both halves of the row first, then straight-line packing and
+                // stores with the output type and the gate decided outside the
+                // loops (the per-element form of this epilogue cost ~5x more).
+                uint32_t oa[32], ob[32];
+                tmem_ld32_async(lane_addr + COL_O, oa);
+                tmem_ld32_async(lane_addr + COL_O + 32, ob);
+                tmem_wait_ld();
+                float va[32], vb[32];
 #pragma unroll
-                for (int h2 = 0; h2 < HD / 32; h2++) {
-                    uint32_t ov[32];
-                    tmem_ld32(lane_addr + COL_O + h2 * 32, ov);
-                    float val[32];
+                for (int e = 0; e < 32; e++) {
+                    va[e] = __uint_as_float(oa[e]) * inv_l;
+                    vb[e] = __uint_as_float(ob[e]) * inv_l;
+                }
+                if (P.gate) {
+                    const size_t obase = ((size_t)(w.tok_base + w.t0 + r) * P.n_heads + w.head) * HD;
 #pragma unroll
                     for (int e = 0; e < 32; e++) {
-                        val[e] = __uint_as_float(ov[e]) * inv_l;
-                        if (P.gate)
-                            val[e] *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, obase + h2 * 32 + e) *
-                                                        1.4426950408889634f));
+                        va[e] *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, obase + e) * 1.4426950408889634f));
+                        vb[e] *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, obase + 32 + e) * 1.4426950408889634f));
                     }
-                    if (P.out_dt == DT_F32) {
+                }
+                if (P.out_dt == DT_F32) {
 #pragma unroll
-                        for (int e = 0; e < 8; e++)
-                            *reinterpret_cast<float4 *>(smem_raw + OFF_X + h2 * Q_BYTES + swz(r, e)) =
-                                make_float4(val[4 * e], val[4 * e + 1], val[4 * e + 2], val[4 * e + 3]);
-                    } else {
-                        const bool obf = P.out_dt == DT_BF16;
+                    for (int e = 0; e < 8; e++) {
+                        *reinterpret_cast<float4 *>(smem_raw + OFF_X + swz(r, e)) =
+                            make_float4(va[4 * e], va[4 * e + 1], va[4 * e + 2], va[4 * e + 3]);
+                        *reinterpret_cast<float4 *>(smem_raw + OFF_X + Q_BYTES + swz(r, e)) =
+                            make_float4(vb[4 * e], vb[4 * e + 1], vb[4 * e + 2], vb[4 * e + 3]);
+                    }
+                } else if (P.out_dt == DT_BF16) {
 #pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            uint32_t wd[4];
+                    for (int e = 0; e < 4; e++) {
+                        *reinterpret_cast<uint4 *>(smem_raw + OFF_X + swz(r, e)) =
+                            make_uint4(pack2<true>(va[8 * e], va[8 * e + 1]), pack2<true>(va[8 * e + 2], va[8 * e + 3]),
+                                       pack2<true>(va[8 * e + 4], va[8 * e + 5]), pack2<true>(va[8 * e + 6], va[8 * e + 7]));
+                        *reinterpret_cast<uint4 *>(smem_raw + OFF_X + swz(r, 4 + e)) =
+                            make_uint4(pack2<true>(vb[8 * e], vb[8 * e + 1]), pack2<true>(vb[8 * e + 2], vb[8 * e + 3]),
+                                       pack2<true>(vb[8 * e + 4], vb[8 * e + 5]), pack2<true>(vb[8 * e + 6], vb[8 * e + 7]));
+                    }
+                } else {
 #pragma unroll
-                            for (int f = 0; f < 4; f++) {
-                                const float a = val[8 * e + 2 * f], bb = val[8 * e + 2 * f + 1];
-                                wd[f] = obf ? pack2<true>(a, bb) : pack2<false>(a, bb);
-                            }
-                            *reinterpret_cast<uint4 *>(smem_raw + OFF_X + swz(r, 4 * h2 + e)) =
-                                make_uint4(wd[0], wd[1], wd[2], wd[3]);
-                        }
+                    for (int e = 0; e < 4; e++) {
+                        *reinterpret_cast<uint4 *>(smem_raw + OFF_X + swz(r, e)) =
+                            make_uint4(pack2<false>(va[8 * e], va[8 * e + 1]), pack2<false>(va[8 * e + 2], va[8 * e + 3]),
+                                       pack2<false>(va[8 * e + 4], va[8 * e + 5]), pack2<false>(va[8 * e + 6], va[8 * e + 7]));
+                        *reinterpret_cast<uint4 *>(smem_raw + OFF_X + swz(r, 4 + e)) =
+                            make_uint4(pack2<false>(vb[8 * e], vb[8 * e + 1]), pack2<false>(vb[8 * e + 2], vb[8 * e + 3]),
+                                       pack2<false>(vb[8 * e + 4], vb[8 * e + 5]), pack2<false>(vb[8 * e + 6], vb[8 * e + 7]));
                     }
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> TMA reads
@@ -662,6 +732,18 @@ __global__ void __launch_bounds__(192, 2)
 
 size_t prefill_tc_smem_bytes() { return SMEM_BYTES; }
 
+template <bool BF16, bool PVF16>
+cudaError_t prefill_tc_launch_t(const CUtensorMap &q, const CUtensorMap &k, const CUtensorMap &v,
+                                const CUtensorMap &o, const CUtensorMap &cs, const PrefillTcParams &P, uint32_t grid,
+                                cudaStream_t s) {
+    const size_t smem = prefill_tc_smem_bytes();
+    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<BF16, PVF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    prefill_tc_kernel<BF16, PVF16><<<grid, 192, smem, s>>>(q, k, v, o, cs, P);
+    return cudaGetLastError();
+}
+
 cudaError_t prefill_tc_launch(bool bf16, const void *qmap, const void *kmap, const void *vmap, const void *omap,
                               const void *csmap, const PrefillTcParams &P, uint32_t grid, cudaStream_t s) {
     const CUtensorMap &q = *static_cast<const CUtensorMap *>(qmap);
@@ -669,19 +751,12 @@ cudaError_t prefill_tc_launch(bool bf16, const void *qmap, const void *kmap, con
     const CUtensorMap &v = *static_cast<const CUtensorMap *>(vmap);
     const CUtensorMap &o = *static_cast<const CUtensorMap *>(omap);
     const CUtensorMap &cs = *static_cast<const CUtensorMap *>(csmap);
-    const size_t smem = prefill_tc_smem_bytes();
-    if (bf16) {
-        cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-        prefill_tc_kernel<true><<<grid, 192, smem, s>>>(q, k, v, o, cs, P);
-    } else {
-        cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-        prefill_tc_kernel<false><<<grid, 192, smem, s>>>(q, k, v, o, cs, P);
-    }
-    return cudaGetLastError();
+    if (!bf16) return prefill_tc_launch_t<false, false>(q, k, v, o, cs, P, grid, s);
+    // bf16: the f16-PV variant, then the hi/lo variant; the layer's flag on
+    // the device makes one of them exit at once.
+    cudaError_t e = prefill_tc_launch_t<true, true>(q, k, v, o, cs, P, grid, s);
+    if (e != cudaSuccess) return e;
+    return prefill_tc_launch_t<true, false>(q, k, v, o, cs, P, grid, s);
 }
 
 }  // namespace nda

@@ -474,3 +474,35 @@ def test_tensor_core_prefill_16bit_out(dt, gate):
         r0 += n
     assert worst <= TOL
     a.close()
+
+
+def test_tensor_core_prefill_bf16_v_beyond_f16():
+    """bf16 V values that f16 cannot represent (2^17 here) take the hi/lo
+    variant: the append that stores one sets the layer's flag on the device,
+    and both that call's prefill and later calls over the cached row stay
+    within the bar (the f16-PV variant would turn the value into Inf)."""
+    import torch
+    rng = np.random.default_rng(43)
+    H, HKV, D, W = 8, 2, 64, 512
+    a = ndattn.Attn(n_layers=1, n_heads=H, n_kv_heads=HKV, qk_head_dim=D, v_head_dim=D, window=W, max_seqs=1,
+                    kv_dtype=O.BF16, act_dtype=O.BF16, out_dtype="f32", max_pos=W)
+    seq = O.OracleSeq(1, H, HKV, D, D, W, O.BF16, max_pos=W)
+    worst = 0.0
+    for call, n in enumerate((200, 77)):
+        q = (rng.standard_normal((n, H * D)) * 0.5).astype(np.float32)
+        k = (rng.standard_normal((n, HKV * D)) * 0.5).astype(np.float32)
+        v = (rng.standard_normal((n, HKV * D)) * 0.5).astype(np.float32)
+        if call == 0:
+            v[57, 1 * D + 3] = 2.0 ** 17
+        out = torch.zeros((n, H * D), dtype=torch.float32, device="cuda")
+        a.prefill(0, [n], dev(q, O.BF16), dev(k, O.BF16), dev(v, O.BF16), out)
+        a.sync()
+        got = out.cpu().numpy()
+        for t in range(n):
+            want = seq.step(0, O.round_act(q[t], O.BF16), O.round_act(k[t], O.BF16), O.round_act(v[t], O.BF16), off=t)
+            assert np.all(np.isfinite(got[t]))
+            worst = max(worst, rel_err(got[t].reshape(H, D), want))
+        a.advance(1, lens=[n])
+        seq.advance(n)
+    assert worst <= TOL
+    a.close()
