@@ -458,24 +458,27 @@ __global__ void __launch_bounds__(192, 2)
                     x[cq * 8 + 2 * e + 1] = f.y;
                 }
             }
-            float inv = 1.0f;
+            // The queries only need the output tolerance (the bit-exact
+            // statement order matters for the cached K, not here): the norm is
+            // applied once up front, the rotation as packed FMAs, and the
+            // per-element branches stay outside the loops.
             if (P.qnorm) {
                 float ss = 0.0f;
 #pragma unroll
-                for (int i = 0; i < HD; i++) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
-                inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)HD), 1e-6f)));
+                for (int i = 0; i < HD; i++) ss = fmaf(x[i], x[i], ss);
+                const float inv = rsqrtf(ss * (1.0f / HD) + 1e-6f);
+#pragma unroll
+                for (int i = 0; i < HD; i++) x[i] *= (1.0f + P.qnorm[i]) * inv;
             }
 #pragma unroll
-            for (int i = 0; i < HD / 2; i++) {
-                float a = x[i], b = x[i + HD / 2];
-                if (P.qnorm) {
-                    a = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, P.qnorm[i]), a), inv);
-                    b = __fmul_rn(__fmul_rn(__fadd_rn(1.0f, P.qnorm[i + HD / 2]), b), inv);
-                }
+            for (int i = 0; i < HD / 2; i += 2) {
                 const float4 t4 = *reinterpret_cast<const float4 *>(smem_raw + OFF_X + cs_off(r, i >> 1));
-                const float2 t = (i & 1) ? make_float2(t4.z, t4.w) : make_float2(t4.x, t4.y);
-                x[i] = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(b, t.y));
-                x[i + HD / 2] = __fadd_rn(__fmul_rn(b, t.x), __fmul_rn(a, t.y));
+                // pairs i and i+1: (a, b) -> (a c - b s, b c + a s)
+                const float2 a2 = make_float2(x[i], x[i + 1]), b2 = make_float2(x[i + HD / 2], x[i + 1 + HD / 2]);
+                const float2 c2 = make_float2(t4.x, t4.z), s2 = make_float2(t4.y, t4.w);
+                const float2 ra = __ffma2_rn(a2, c2, __fmul2_rn(make_float2(-b2.x, -b2.y), s2));
+                const float2 rb = __ffma2_rn(b2, c2, __fmul2_rn(a2, s2));
+                x[i] = ra.x, x[i + 1] = ra.y, x[i + HD / 2] = rb.x, x[i + 1 + HD / 2] = rb.y;
             }
             uint32_t hi[32], lo[32];
 #pragma unroll
@@ -672,39 +675,46 @@ __global__ void __launch_bounds__(192, 2)
                 }
                 n_stores++;
             } else {
-                // Partial tile (the end of a sequence): direct row stores.
-                const size_t obase = ((size_t)(w.tok_base + w.t0 + r) * P.n_heads + w.head) * HD;
-#pragma unroll
-                for (int h2 = 0; h2 < HD / 32; h2++) {
-                    uint32_t ov[32];
-                    tmem_ld32(lane_addr + COL_O + h2 * 32, ov);
-                    if (!row_valid) continue;
-                    float val[32];
+                // Partial tile (the end of a sequence): direct row stores, with
+                // the gate and the output type decided outside the loops.
+                uint32_t oa[32], ob[32];
+                tmem_ld32_async(lane_addr + COL_O, oa);
+                tmem_ld32_async(lane_addr + COL_O + 32, ob);
+                tmem_wait_ld();
+                if (row_valid) {
+                    const size_t obase = ((size_t)(w.tok_base + w.t0 + r) * P.n_heads + w.head) * HD;
+                    float val[HD];
 #pragma unroll
                     for (int e = 0; e < 32; e++) {
-                        val[e] = __uint_as_float(ov[e]) * inv_l;
-                        if (P.gate)
-                            val[e] *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, obase + h2 * 32 + e) *
-                                                        1.4426950408889634f));
+                        val[e] = __uint_as_float(oa[e]) * inv_l;
+                        val[32 + e] = __uint_as_float(ob[e]) * inv_l;
+                    }
+                    if (P.gate) {
+#pragma unroll
+                        for (int e = 0; e < HD; e++)
+                            val[e] *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, obase + e) * 1.4426950408889634f));
                     }
                     if (P.out_dt == DT_F32) {
-                        float4 *o4 = reinterpret_cast<float4 *>(static_cast<float *>(P.out) + obase + h2 * 32);
+                        float4 *o4 = reinterpret_cast<float4 *>(static_cast<float *>(P.out) + obase);
 #pragma unroll
-                        for (int e = 0; e < 8; e++)
+                        for (int e = 0; e < HD / 4; e++)
                             o4[e] = make_float4(val[4 * e], val[4 * e + 1], val[4 * e + 2], val[4 * e + 3]);
+                    } else if (P.out_dt == DT_BF16) {
+                        uint4 *o4 = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(P.out) + obase);
+#pragma unroll
+                        for (int e = 0; e < HD / 8; e++)
+                            o4[e] = make_uint4(pack2<true>(val[8 * e], val[8 * e + 1]),
+                                               pack2<true>(val[8 * e + 2], val[8 * e + 3]),
+                                               pack2<true>(val[8 * e + 4], val[8 * e + 5]),
+                                               pack2<true>(val[8 * e + 6], val[8 * e + 7]));
                     } else {
-                        uint4 *o4 = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(P.out) + obase + h2 * 32);
-                        const bool obf = P.out_dt == DT_BF16;
+                        uint4 *o4 = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(P.out) + obase);
 #pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            uint32_t wd[4];
-#pragma unroll
-                            for (int f = 0; f < 4; f++) {
-                                const float a = val[8 * e + 2 * f], bb = val[8 * e + 2 * f + 1];
-                                wd[f] = obf ? pack2<true>(a, bb) : pack2<false>(a, bb);
-                            }
-                            o4[e] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
-                        }
+                        for (int e = 0; e < HD / 8; e++)
+                            o4[e] = make_uint4(pack2<false>(val[8 * e], val[8 * e + 1]),
+                                               pack2<false>(val[8 * e + 2], val[8 * e + 3]),
+                                               pack2<false>(val[8 * e + 4], val[8 * e + 5]),
+                                               pack2<false>(val[8 * e + 6], val[8 * e + 7]));
                     }
                 }
                 // The 32 KB block was not used: released at once.
