@@ -238,6 +238,13 @@ __device__ __forceinline__ void write_p_chunk(const uint32_t (&sv)[32], uint32_t
     l2 = __fadd2_rn(l2, __fadd2_rn(acc[0], acc[1]));
 }
 
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 // Offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled tile.
 __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) { return r * 128u + ((c ^ (r & 7u)) << 4); }
 // Offset of 16-byte chunk `c` (0..15) of RoPE row `r` in the 32 KB block, as
@@ -531,7 +538,8 @@ __global__ void __launch_bounds__(192, 2)
                             if (c2 * 32 + e > lim) sv[e] = 0xff800000u;
                     }
 #pragma unroll
-                    for (int e = 0; e < 32; e++) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(sv[e]));
+                    for (int e = 0; e < 32; e += 2)
+                        mx[(e >> 1) & 7] = fmax3(mx[(e >> 1) & 7], __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
                 }
 #pragma unroll
                 for (int w2 = 4; w2 > 0; w2 >>= 1)
