@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "../../include/nd_attn.h"
+#include "nd_async.cuh"
 #include "nd_internal.h"
 
 using nda::AttnParams;
@@ -80,6 +81,58 @@ __global__ void advance_kernel(SeqState *st, uint32_t n, const uint32_t *ids, co
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     st[ids ? ids[i] : i].pos += len ? len[i] : step;
+}
+
+// Host-buffer decode: copies the caller's inputs from mapped host memory into
+// the device buffers the attend kernels read, one unit (16, 4 or 1 bytes, as
+// the segment's alignment allows) per thread so that the whole transfer is in
+// flight at once: about one PCIe round trip plus the bytes at link rate. It
+// lets its dependent launch start at once; that attend kernel streams K/V
+// meanwhile and reads these buffers only after its grid-dependency wait, which
+// returns once this grid has completed and its writes are visible.
+struct IngestSeg {
+    const char *src;
+    char *dst;
+    uint64_t units;   // of 1 << shift bytes
+    uint32_t shift;
+};
+struct IngestParams {
+    IngestSeg seg[4];
+    uint64_t first[5];   // first unit of each segment, then the total
+    uint32_t n;
+};
+
+__global__ void __launch_bounds__(256) ingest_kernel(const IngestParams P) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t j = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; j < P.first[P.n]; j += stride) {
+        uint32_t s = 0;
+        while (j >= P.first[s + 1]) s++;
+        const IngestSeg g = P.seg[s];
+        const uint64_t i = j - P.first[s];
+        if (g.shift == 4)
+            reinterpret_cast<uint4 *>(g.dst)[i] = reinterpret_cast<const uint4 *>(g.src)[i];
+        else if (g.shift == 2)
+            reinterpret_cast<uint32_t *>(g.dst)[i] = reinterpret_cast<const uint32_t *>(g.src)[i];
+        else
+            g.dst[i] = g.src[i];
+    }
+}
+
+// Failure-path diagnostics: one thread waits on an mbarrier that nothing
+// arrives on, for at most `limit` SM cycles, then reports the expiry through
+// the status word as the hot kernels' bounded waits do (code 3).
+__global__ void wait_expiry_kernel(int *err, long long limit) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    nda::mbar_init(&bar, 1);
+    const long long t0 = clock64();
+    while (!nda::mbar_test(&bar, 0)) {
+        if (clock64() - t0 > limit) {
+            nda::set_err(err, 3);
+            return;
+        }
+    }
 }
 
 // Copies whole cache rows between a (layer-strided) cache and a dense buffer:
@@ -148,6 +201,11 @@ struct nd_attn {
     std::vector<uint32_t> lean_last;   // what d_lean holds (uploads skipped when unchanged)
     int lean_occ[8] = {0};             // CTAs per SM of each (dtype, hd, nq) instantiation, 0 = not asked yet
     std::vector<uint32_t> lean_up;     // host staging of the next d_lean image
+    // The plan is a function of the call's per-token {visits, sequence,
+    // position} and of constants of the handle: the key of the last plan
+    // built, and its shape, let calls with the same key skip the rebuild.
+    std::vector<uint32_t> lean_key, lean_key_next;
+    uint64_t lean_nt = 0, lean_g = 0, lean_s = 0, lean_ch = 0, lean_nu = 0;
     std::vector<CUtensorMap> lean_kmap, lean_vmap;   // per layer, built on first use
     std::vector<uint8_t> lean_map_ok;
     uint32_t lean_parity = 0;          // half of counters / partials the next balanced launch uses
@@ -155,10 +213,11 @@ struct nd_attn {
     // a layer, or kAllLayers. A balanced launch may stream K/V before that
     // kernel ends only when it cannot be writing the launch's layer.
     int last_writer = -1;
-    int *d_err = nullptr;
-    void *pin = nullptr;
-    size_t pin_cap = 0;
-    int *err_pin = nullptr;   // pinned host copy of d_err, read once per sync
+    int *err_host = nullptr;  // status word: pinned host memory mapped for the kernels
+    int *d_err = nullptr;     // its device address
+    char *hstage = nullptr;       // host-buffer calls: pinned staging, mapped for the kernels
+    char *hstage_dev = nullptr;   // its device address
+    size_t hstage_cap = 0;
     int *d_vbig = nullptr;    // per layer: a bf16 V value f16 cannot represent was stored (sticky)
     void *dio = nullptr;
     size_t dio_cap = 0;
@@ -349,34 +408,14 @@ bool lean_ok(const nd_attn *h, bool no_wrap) {
 constexpr uint64_t kLeanStaticPct = 75, kLeanUnitMin = 2;
 constexpr uint32_t kLeanAhead = 2;
 
-// Balanced launch: item (t, g) holds T_t = max(1, ceil((vis[t] - fuse_append)
-// / 64)) tiles (the newest row of a fused append is not in the TMA stream).
-// G = the CTAs the GPU holds at once; the NT tiles of the call become G
-// static units of S ~ 3/4 NT / G tiles, then dynamic units of CH tiles (at
-// most ~4 per CTA) that CTAs take as they run dry. Each unit needs two
-// partial slots and one ticket; two more counters drive the unit queue.
-int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, const nda::SeqSpan *d_spans,
-             uint32_t n_spans, const std::vector<uint32_t> &vis, const std::vector<uint32_t> &tok_seq,
-             const std::vector<uint32_t> &tok_pos, int fuse_append, const void *q, const void *k, const void *v,
-             const void *gate, void *out) {
-    const nd_attn_config &cf = h->cfg;
-    const uint32_t n_kv = cf.n_kv_heads, hd = cf.qk_head_dim;
-    const int nq = nda::nq_for_rep(h->rep);
-    const bool bf16 = cf.kv_dtype == ND_DT_BF16;
-    auto launch = [&](const void *km, const void *vm, const nda::AttnParams &P, int *occ) {
-        return bf16 ? nda::attend_lean_launch_bf16((int)hd, nq, km, vm, P, occ, h->stream)
-                    : nda::attend_lean_launch_f16((int)hd, nq, km, vm, P, occ, h->stream);
-    };
-    int &occ = h->lean_occ[(bf16 ? 4 : 0) + (nq == 1 ? 0 : nq == 2 ? 1 : nq == 4 ? 2 : 3)];
-    AttnParams P = base_params(h, layer);
-    if (occ <= 0) {
-        int b = 0;
-        ND_CUDA(launch(nullptr, nullptr, P, &b));
-        if (b <= 0) return fail(ND_ATTN_ERR_CUDA, "balanced attend kernel does not fit on an SM");
-        occ = b;
-    }
-    // Plan: per token {first tile, tiles per item, sequence, position} (and a
-    // sentinel), then per unit the walk state at its first tile.
+// Builds the balanced-launch plan of a call into h->lean_up: per token
+// {first tile, tiles per item, sequence, position} and a sentinel, then per
+// unit the walk state at its first tile. Uploads it when it differs from what
+// the device holds and records its shape (tiles, static units and their
+// size, dynamic unit size, units).
+int build_lean_plan(nd_attn *h, uint32_t ntok, const std::vector<uint32_t> &vis, const std::vector<uint32_t> &tok_seq,
+                    const std::vector<uint32_t> &tok_pos, int fuse_append, int occ) {
+    const uint32_t n_kv = h->cfg.n_kv_heads;
     std::vector<uint32_t> &up = h->lean_up;
     up.assign((size_t)(ntok + 1) * 4, 0u);
     uint64_t nt = 0;
@@ -419,6 +458,55 @@ int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, co
                                 h->stream));
         h->lean_last = up;
     }
+    h->lean_nt = nt, h->lean_g = G, h->lean_s = S, h->lean_ch = CH, h->lean_nu = NU;
+    return ND_ATTN_OK;
+}
+
+// Balanced launch: item (t, g) holds T_t = max(1, ceil((vis[t] - fuse_append)
+// / 64)) tiles (the newest row of a fused append is not in the TMA stream).
+// G = the CTAs the GPU holds at once; the NT tiles of the call become G
+// static units of S ~ 3/4 NT / G tiles, then dynamic units of CH tiles (at
+// most ~4 per CTA) that CTAs take as they run dry. Each unit needs two
+// partial slots and one ticket; two more counters drive the unit queue.
+int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, const nda::SeqSpan *d_spans,
+             uint32_t n_spans, const std::vector<uint32_t> &vis, const std::vector<uint32_t> &tok_seq,
+             const std::vector<uint32_t> &tok_pos, int fuse_append, const void *q, const void *k, const void *v,
+             const void *gate, void *out) {
+    const nd_attn_config &cf = h->cfg;
+    const uint32_t hd = cf.qk_head_dim;
+    const int nq = nda::nq_for_rep(h->rep);
+    const bool bf16 = cf.kv_dtype == ND_DT_BF16;
+    auto launch = [&](const void *km, const void *vm, const nda::AttnParams &P, int *occ) {
+        return bf16 ? nda::attend_lean_launch_bf16((int)hd, nq, km, vm, P, occ, h->stream)
+                    : nda::attend_lean_launch_f16((int)hd, nq, km, vm, P, occ, h->stream);
+    };
+    int &occ = h->lean_occ[(bf16 ? 4 : 0) + (nq == 1 ? 0 : nq == 2 ? 1 : nq == 4 ? 2 : 3)];
+    AttnParams P = base_params(h, layer);
+    if (occ <= 0) {
+        int b = 0;
+        ND_CUDA(launch(nullptr, nullptr, P, &b));
+        if (b <= 0) return fail(ND_ATTN_ERR_CUDA, "balanced attend kernel does not fit on an SM");
+        occ = b;
+    }
+    // Plan: per token {first tile, tiles per item, sequence, position} (and a
+    // sentinel), then per unit the walk state at its first tile. Rebuilt only
+    // when its inputs differ from the last plan's.
+    std::vector<uint32_t> &key = h->lean_key_next;
+    key.resize((size_t)ntok * 3 + 2);
+    key[0] = (uint32_t)fuse_append;
+    key[1] = (uint32_t)occ;
+    for (uint32_t t = 0; t < ntok; t++) {
+        key[2 + 3 * t] = vis[t];
+        key[3 + 3 * t] = tok_seq[t];
+        key[4 + 3 * t] = tok_pos[t];
+    }
+    if (key != h->lean_key) {
+        int rc = build_lean_plan(h, ntok, vis, tok_seq, tok_pos, fuse_append, occ);
+        if (rc) return rc;
+        h->lean_key.swap(key);
+    }
+    const uint64_t nt = h->lean_nt, G = h->lean_g, S = h->lean_s, CH = h->lean_ch, NU = h->lean_nu;
+    const size_t cnt_half = h->counter_cap / 2, slot_half = h->part_slots / 2;
     P.lean_ahead = kLeanAhead;
     P.lean_s = (uint32_t)S;
     P.lean_ch = (uint32_t)CH;
@@ -796,12 +884,18 @@ int nd_attn_open(const nd_attn_config *cfg_in, nd_attn **out) {
     }
     if (cudaMalloc(&h->norms, (size_t)cfg.n_layers * 2 * cfg.qk_head_dim * sizeof(float)) != cudaSuccess ||
         cudaMalloc(&h->d_state, cfg.max_seqs * sizeof(SeqState)) != cudaSuccess ||
-        cudaMalloc(&h->d_err, sizeof(int)) != cudaSuccess ||
         cudaMalloc(&h->d_vbig, cfg.n_layers * sizeof(int)) != cudaSuccess ||
-        cudaHostAlloc(reinterpret_cast<void **>(&h->err_pin), sizeof(int), cudaHostAllocDefault) != cudaSuccess)
+        cudaHostAlloc(reinterpret_cast<void **>(&h->err_host), sizeof(int),
+                      cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess ||
+        cudaHostGetDevicePointer(reinterpret_cast<void **>(&h->d_err), h->err_host, 0) != cudaSuccess)
         return bail(fail(ND_ATTN_ERR_NOMEM, "state allocation failed"));
+    *h->err_host = 0;
     cudaMemsetAsync(h->d_state, 0, cfg.max_seqs * sizeof(SeqState), h->stream);
-    cudaMemsetAsync(h->d_err, 0, sizeof(int), h->stream);
+    // The small kernels between attend launches ask for the shared-memory
+    // carveout the attend kernels need, so an SM that ran one need not be
+    // reconfigured before it takes an attend CTA.
+    cudaFuncSetAttribute(ingest_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    cudaFuncSetAttribute(advance_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     cudaMemsetAsync(h->d_vbig, 0, cfg.n_layers * sizeof(int), h->stream);
     if (cfg.block_size) {
         const size_t nb = (size_t)cfg.max_seqs * h->blocks_per_seq;
@@ -841,9 +935,9 @@ void nd_attn_close(nd_attn *h) {
     cudaFree(h->kc); cudaFree(h->vc); cudaFree(h->ks); cudaFree(h->vs);
     cudaFree(h->rope); cudaFree(h->norms); cudaFree(h->d_state); cudaFree(h->d_btab);
     cudaFree(h->part_o); cudaFree(h->part_ml); cudaFree(h->counters);
-    cudaFree(h->d_tok); cudaFree(h->d_u32); cudaFree(h->d_lean); cudaFree(h->d_vbig); cudaFree(h->d_err); cudaFree(h->dio); cudaFree(h->d_work); cudaFree(h->d_spans);
-    if (h->pin) cudaFreeHost(h->pin);
-    if (h->err_pin) cudaFreeHost(h->err_pin);
+    cudaFree(h->d_tok); cudaFree(h->d_u32); cudaFree(h->d_lean); cudaFree(h->d_vbig); cudaFree(h->dio); cudaFree(h->d_work); cudaFree(h->d_spans);
+    if (h->hstage) cudaFreeHost(h->hstage);
+    if (h->err_host) cudaFreeHost(h->err_host);
     if (h->own) cudaStreamDestroy(h->own);
     delete h;
 }
@@ -1055,6 +1149,108 @@ int nd_attn_prefill(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_
 
 namespace {
 
+// Device address of a host range the device can read and write in place
+// (pinned and mapped, as cudaHostAlloc and cudaHostRegister memory is under
+// unified addressing), checked at both ends; nullptr for pageable (or
+// managed) memory, which the caller stages. Device memory is no host buffer:
+// *bad is set.
+char *mapped_alias(const void *p, size_t bytes, bool *bad) {
+    const char *end[2] = {static_cast<const char *>(p), static_cast<const char *>(p) + bytes - 1};
+    char *dev[2];
+    for (int i = 0; i < 2; i++) {
+        cudaPointerAttributes a;
+        if (cudaPointerGetAttributes(&a, end[i]) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        if (a.type == cudaMemoryTypeDevice) {
+            *bad = true;
+            return nullptr;
+        }
+        if (a.type != cudaMemoryTypeHost || !a.devicePointer) return nullptr;
+        dev[i] = static_cast<char *>(a.devicePointer);
+    }
+    return dev[1] - dev[0] == (ptrdiff_t)(bytes - 1) ? dev[0] : nullptr;
+}
+
+int grow_hstage(nd_attn *h, size_t need) {
+    if (need <= h->hstage_cap) return ND_ATTN_OK;
+    if (h->hstage) cudaFreeHost(h->hstage);
+    h->hstage = h->hstage_dev = nullptr;
+    h->hstage_cap = 0;
+    const size_t n = std::max(need, (size_t)1 << 16);
+    if (cudaHostAlloc(reinterpret_cast<void **>(&h->hstage), n, cudaHostAllocMapped | cudaHostAllocPortable) !=
+            cudaSuccess ||
+        cudaHostGetDevicePointer(reinterpret_cast<void **>(&h->hstage_dev), h->hstage, 0) != cudaSuccess) {
+        if (h->hstage) cudaFreeHost(h->hstage);
+        h->hstage = h->hstage_dev = nullptr;
+        return fail(ND_ATTN_ERR_NOMEM, "pinned staging of %zu bytes failed", n);
+    }
+    h->hstage_cap = n;
+    return ND_ATTN_OK;
+}
+
+// Host-buffer decode. The inputs reach the device through one ingest launch
+// reading mapped host memory: the caller's pinned buffers in place, pageable
+// ones after a host copy into the handle's pinned staging. The attend launch
+// that follows may start under the ingest grid (it streams K/V meanwhile) and
+// writes the output straight into mapped host memory, the caller's own when
+// it is pinned. No copy-engine transfer is on the path.
+int run_host_decode(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const void *q, const void *k,
+                    const void *v, const void *gate, void *out) {
+    const size_t b[5] = {act_bytes(h, n, 0), act_bytes(h, n, 1), act_bytes(h, n, 2), gate ? act_bytes(h, n, 3) : 0,
+                         act_bytes(h, n, 4)};
+    const void *src[5] = {q, k, v, gate, out};
+    char *alias[5] = {};
+    size_t soff[5] = {}, doff[4] = {}, stot = 0, dtot = 0;
+    for (int i = 0; i < 5; i++) {
+        if (!b[i]) continue;
+        bool bad = false;
+        alias[i] = mapped_alias(src[i], b[i], &bad);
+        if (bad) return fail(ND_ATTN_ERR_ARG, "host-buffer call given device memory (argument %d)", i);
+        soff[i] = stot;
+        if (!alias[i]) stot += (b[i] + 255) / 256 * 256;
+        if (i < 4) {
+            doff[i] = dtot;
+            dtot += (b[i] + 255) / 256 * 256;
+        }
+    }
+    int rc = grow_hstage(h, stot);
+    if (!rc) rc = grow(reinterpret_cast<char **>(&h->dio), &h->dio_cap, dtot);
+    if (rc) return rc;
+    char *d = static_cast<char *>(h->dio);
+    IngestParams I;
+    memset(&I, 0, sizeof(I));
+    for (int i = 0; i < 4; i++) {
+        if (!b[i]) continue;
+        const char *from = alias[i];
+        if (!from) {
+            memcpy(h->hstage + soff[i], src[i], b[i]);
+            from = h->hstage_dev + soff[i];
+        }
+        const uintptr_t al = reinterpret_cast<uintptr_t>(from) | b[i];   // dio offsets are 256-aligned
+        const uint32_t shift = (al & 15) == 0 ? 4 : (al & 3) == 0 ? 2 : 0;
+        I.seg[I.n] = IngestSeg{from, d + doff[i], b[i] >> shift, shift};
+        I.first[I.n + 1] = I.first[I.n] + (b[i] >> shift);
+        I.n++;
+    }
+    const uint64_t units = I.first[I.n];
+    const uint32_t grid = (uint32_t)std::min<uint64_t>((units + 255) / 256, (uint64_t)h->sm_count * 8);
+    ingest_kernel<<<grid, 256, 0, h->stream>>>(I);
+    h->launches++;
+    note_writer(h, kNoLayer);
+    rc = cudaGetLastError() == cudaSuccess ? ND_ATTN_OK : fail(ND_ATTN_ERR_CUDA, "ingest launch failed");
+    if (!rc)
+        rc = nd_attn_decode(h, layer, n, seq_ids, d + doff[0], d + doff[1], d + doff[2], gate ? d + doff[3] : nullptr,
+                            alias[4] ? alias[4] : h->hstage_dev + soff[4]);
+    // The staging must not be rewritten while a launch of this call may read it.
+    const int src_rc = nd_attn_sync(h);
+    if (rc) return rc;
+    if (src_rc) return src_rc;
+    if (!alias[4]) memcpy(out, h->hstage + soff[4], b[4]);
+    return ND_ATTN_OK;
+}
+
 // Host-buffer form: q/k/v/gate/out live in host memory.
 int run_host(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const uint32_t *len,
              const void *q, const void *k, const void *v, const void *gate, void *out) {
@@ -1063,6 +1259,7 @@ int run_host(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, co
     if (rc) return rc;
     if (!q || !k || !v || !out) return fail(ND_ATTN_ERR_ARG, "null tensor");
     DeviceGuard dg(h->cfg.device);
+    if (!len) return run_host_decode(h, layer, n, seq_ids, q, k, v, gate, out);
     size_t tokens = 0;
     for (uint32_t i = 0; i < n; i++) tokens += len ? len[i] : 1;
     const size_t b[5] = {act_bytes(h, tokens, 0), act_bytes(h, tokens, 1), act_bytes(h, tokens, 2),
@@ -1350,17 +1547,29 @@ int nd_attn_set_block_table(nd_attn *h, uint32_t seq, const int32_t *pages) {
 int nd_attn_sync(nd_attn *h) {
     if (!h) return fail(ND_ATTN_ERR_ARG, "null handle");
     DeviceGuard dg(h->cfg.device);
-    // The error word comes back with the stream's own work: one round trip.
-    ND_CUDA(cudaMemcpyAsync(h->err_pin, h->d_err, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+    // Kernels store their status straight into mapped host memory: after the
+    // stream has drained it is readable with no copy.
     ND_CUDA(cudaStreamSynchronize(h->stream));
-    const int err = *h->err_pin;
+    const int err = *reinterpret_cast<volatile int *>(h->err_host);
     if (err) {
-        cudaMemset(h->d_err, 0, sizeof(int));
+        *reinterpret_cast<volatile int *>(h->err_host) = 0;
         cudaMemset(h->counters, 0, h->counter_cap * sizeof(int));
         return fail(err == 3 ? ND_ATTN_ERR_TIMEOUT : ND_ATTN_ERR_RANGE,
                     "device reported status %d (position/state out of range or bounded wait expired)", err);
     }
     return ND_ATTN_OK;
+}
+
+int nd_attn_selftest_wait(nd_attn *h, uint32_t limit_us) {
+    if (!h) return fail(ND_ATTN_ERR_ARG, "null handle");
+    if (limit_us == 0 || limit_us > 1000000u) return fail(ND_ATTN_ERR_RANGE, "limit_us %u outside [1, 1000000]", limit_us);
+    DeviceGuard dg(h->cfg.device);
+    // 2000 cycles per microsecond bounds the wait from above at SM clocks up
+    // to 2 GHz (B200: 1965 MHz at most).
+    wait_expiry_kernel<<<1, 32, 0, h->stream>>>(h->d_err, (long long)limit_us * 2000);
+    h->launches++;
+    ND_CUDA(cudaGetLastError());
+    return nd_attn_sync(h);
 }
 
 void *nd_attn_stream(nd_attn *h) { return h ? static_cast<void *>(h->stream) : nullptr; }

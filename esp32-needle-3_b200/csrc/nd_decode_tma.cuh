@@ -350,7 +350,7 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                 }
             }
             if (lane == 0) {
-                if (bad) atomicExch(P.err, 2);
+                if (bad) set_err(P.err, 2);
                 info[i] = LeanInfo{tm.row, pr, bad ? 0u : pos + 1 - (P.fuse_append ? 1u : 0u), tm.seq,
                                    appender ? 1 : 0};
             }
@@ -469,7 +469,7 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                 }
             }
         }
-        if (lane == 0 && abort_flag_s) atomicExch(P.err, 3);
+        if (lane == 0 && abort_flag_s) set_err(P.err, 3);
         return;
     }
 

@@ -98,10 +98,15 @@ struct AttnParams {
     int fuse_append;
     float *part_o, *part_ml;
     int *counters;
-    int *err;
+    int *err;                    // status word in mapped pinned host memory (0 = ok)
 };
 
 // ---------------------------------------------------------------- helpers
+// The status word is host memory mapped into the device's address space, so
+// the host reads it after a stream sync with no copy. A plain store: any
+// nonzero code fails the call, and racing writers need no atomicity.
+__device__ __forceinline__ void set_err(int *err, int code) { *reinterpret_cast<volatile int *>(err) = code; }
+
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -404,7 +409,7 @@ __global__ void __launch_bounds__(128) append_kernel(const AttnParams P) {
     const SeqState st = P.state[tm.seq];
     const uint32_t pos = st.pos + tm.off;
     if (pos >= P.max_pos || st.n_sink >= P.c.window) {
-        if (lane == 0) atomicExch(P.err, 2);
+        if (lane == 0) set_err(P.err, 2);
         return;
     }
     const uint32_t slot = kv_slot(P.c.window, st.n_sink, pos);
@@ -432,7 +437,7 @@ __global__ void __launch_bounds__(256) append_vec_kernel(const AttnParams P) {
     const SeqState st = P.state[tm.seq];
     const uint32_t pos = st.pos + tm.off;
     if (pos >= P.max_pos || st.n_sink >= P.c.window) {
-        if (t == 0) atomicExch(P.err, 2);
+        if (t == 0) set_err(P.err, 2);
         return;
     }
     const size_t row = phys_row(P.c, tm.seq, kv_slot(P.c.window, st.n_sink, pos));
@@ -746,7 +751,7 @@ __global__ void __launch_bounds__(128) attend_kernel(const AttnParams P) {
     const SeqState st = P.state[tm.seq];
     const uint32_t pos = st.pos + tm.off, n_sink = st.n_sink;
     if (pos >= P.max_pos || n_sink >= W) {
-        if (tid == 0) atomicExch(P.err, 2);
+        if (tid == 0) set_err(P.err, 2);
         return;
     }
     const Runs runs = make_runs(pos, n_sink, W);

@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(192, 2)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (su32(smem_raw) & 1023u) {          // the swizzled tiles need 1024-byte alignment
-        if (tid == 0) atomicExch(P.err, 4);
+        if (tid == 0) *reinterpret_cast<volatile int *>(P.err) = 4;
         return;
     }
     uint8_t *sq = smem_raw + OFF_Q;
@@ -739,7 +739,7 @@ __global__ void __launch_bounds__(192, 2)
 
     fence_before();
     __syncthreads();
-    if (tid == 0 && B.abort_flag) atomicExch(P.err, 3);
+    if (tid == 0 && B.abort_flag) *reinterpret_cast<volatile int *>(P.err) = 3;
     if (warp == 5) {
         fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TMEM_COLS));

@@ -91,6 +91,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "nd_attn_write_cache": (c_int, [vp, u32, u32, u32, u32, vp, vp, vp, vp]),
         "nd_attn_set_block_table": (c_int, [vp, u32, vp]),
         "nd_attn_sync": (c_int, [vp]),
+        "nd_attn_selftest_wait": (c_int, [vp, u32]),
         "nd_attn_stream": (vp, [vp]),
         "nd_attn_set_stream": (c_int, [vp, vp]),
         "nd_attn_launch_count": (c_uint64, [vp]),
@@ -294,6 +295,11 @@ class Attn:
     # ---- misc
     def sync(self) -> None:
         _check(load().nd_attn_sync(self.h))
+
+    def selftest_wait(self, limit_us: int = 1000) -> int:
+        """Runs the bounded-wait self-test; returns its status code
+        (ERR_TIMEOUT when the device status path works)."""
+        return load().nd_attn_selftest_wait(self.h, limit_us)
 
     @property
     def stream(self) -> int:

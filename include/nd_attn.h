@@ -266,6 +266,12 @@ ND_ATTN_API const nd_attn_ops *nd_attn_cuda_ops(void);
 /* Waits for all work enqueued on the handle's stream; reports device-side
  * status (ND_ATTN_ERR_TIMEOUT) and asynchronous CUDA errors. */
 ND_ATTN_API int  nd_attn_sync(nd_attn *h);
+/* Failure-path self-test: one device thread waits on an mbarrier that nothing
+ * arrives on, bounded to about `limit_us` microseconds (1..1000000), then
+ * reports the expiry through the device status word as the hot kernels'
+ * bounded waits do. Returns what nd_attn_sync() then reports:
+ * ND_ATTN_ERR_TIMEOUT when the path works. The handle stays usable. */
+ND_ATTN_API int  nd_attn_selftest_wait(nd_attn *h, uint32_t limit_us);
 /* The handle's CUDA stream (a cudaStream_t), for callers that order their own
  * work against it. */
 ND_ATTN_API void *nd_attn_stream(nd_attn *h);

@@ -289,6 +289,63 @@ def test_host_entry_points_match_device():
     del rng
 
 
+@pytest.mark.parametrize("kv", ["f16", "i8"])
+def test_host_decode_pinned_pageable_unaligned(kv):
+    """decode_host reads its inputs from mapped host memory (pinned buffers in
+    place, pageable ones through the handle's pinned staging) and writes the
+    output there. Every form gives the device entry point's bits: pinned,
+    pageable, pinned at an odd element offset (2- or 4-byte aligned, the
+    narrow copy units), and a mix, all with a gate, on the balanced 16-bit
+    kernel and the int8 kernel. Device memory is refused."""
+    import torch
+    H, HKV, HD, W, B = 8, 2, 64, 256, 3
+    act = "f16" if kv == "f16" else "f32"
+    npdt = np.float16 if act == "f16" else np.float32
+    tdt = torch.float16 if act == "f16" else torch.float32
+    rng = np.random.default_rng(8)
+    steps = [[rng.standard_normal((B, n)).astype(npdt) for n in (H * HD, HKV * HD, HKV * HD, H * HD)]
+             for _ in range(3)]
+    plans = {"pinned": ["pinned"] * 5, "pageable": ["pageable"] * 5, "offset": ["offset"] * 5,
+             "mixed": ["pinned", "offset", "pageable", "pinned", "offset"]}
+
+    def place(x, how, keep):
+        if how == "pageable":
+            return x.copy()
+        t = torch.empty(x.size + (how == "offset"), dtype=tdt).pin_memory()
+        keep.append(t)
+        arr = t.numpy()[(how == "offset"):].reshape(x.shape)
+        arr[...] = x
+        return arr
+
+    outs = {}
+    for form in ["device"] + list(plans):
+        a = ndattn.Attn(n_heads=H, n_kv_heads=HKV, window=W, max_seqs=B, kv_dtype=kv, act_dtype=act, out_dtype=act)
+        res = []
+        for q, k, v, g in steps:
+            if form == "device":
+                t = [torch.from_numpy(x).cuda() for x in (q, k, v, g)]
+                o = torch.zeros((B, H * HD), dtype=tdt, device="cuda")
+                a.decode(0, B, t[0], t[1], t[2], o, gate=t[3])
+                a.sync()
+                res.append(o.cpu().numpy())
+            else:
+                keep = []
+                arrs = [place(x, how, keep) for x, how in zip((q, k, v, g, np.zeros((B, H * HD), npdt)), plans[form])]
+                a.decode_host(0, B, arrs[0], arrs[1], arrs[2], arrs[4], gate=arrs[3])
+                res.append(arrs[4].copy())
+            a.advance(B)
+        if form == "pinned":
+            d = torch.zeros((B, H * HD), dtype=tdt, device="cuda")
+            rc = ndattn.load().nd_attn_decode_host(a.h, 0, B, None, d.data_ptr(), d.data_ptr(), d.data_ptr(), None,
+                                                   d.data_ptr())
+            assert rc == ndattn.ERR_ARG
+        outs[form] = res
+        a.close()
+    for form in plans:
+        for want, got in zip(outs["device"], outs[form]):
+            assert np.array_equal(want.view(np.uint8), got.view(np.uint8)), form
+
+
 def test_seq_ids_subset_and_order():
     """A call over a permuted subset of sequences only touches those."""
     import torch
@@ -386,6 +443,37 @@ def test_rewind_and_reset_semantics():
     a.reset(0)
     assert a.state(0) == (0, 0)
     a.close()
+
+
+def test_bounded_wait_expiry_reaches_host():
+    """Failure detection without a fault: a device wait on an mbarrier that
+    nothing arrives on expires after ~1 ms, its status reaches the host through
+    the mapped status word as ERR_TIMEOUT, and the handle then decodes
+    normally (status cleared, results checked against the oracle)."""
+    import torch
+    rng = np.random.default_rng(31)
+    H, HD, W = 4, 64, 64
+    a = ndattn.Attn(n_heads=H, n_kv_heads=H, window=W, max_pos=W, max_seqs=1, kv_dtype="f32")
+    seq = O.OracleSeq(1, H, H, HD, HD, W, O.F32, max_pos=W)
+    for _ in range(2):
+        assert a.selftest_wait(1000) == ndattn.ERR_TIMEOUT
+        a.sync()                                              # the status was cleared
+        q, k, v = (rng.standard_normal(H * HD).astype(np.float32) for _ in range(3))
+        out = torch.zeros((1, H * HD), device="cuda")
+        a.decode(0, 1, *(torch.from_numpy(x[None]).cuda() for x in (q, k, v)), out)
+        a.sync()
+        want = seq.step(0, q, k, v)
+        assert rel_err(out.cpu().numpy().reshape(H, HD), want) <= TOL
+        a.advance(1)
+        seq.advance()
+    with pytest.raises(ndattn.NdAttnError):
+        _check_rc(a.selftest_wait(0))
+    a.close()
+
+
+def _check_rc(rc):
+    if rc < 0:
+        raise ndattn.NdAttnError(rc, "")
 
 
 def test_errors_are_reported_not_hidden():
