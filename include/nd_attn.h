@@ -157,10 +157,16 @@ ND_ATTN_API int  nd_attn_decode(nd_attn *h, uint32_t layer, uint32_t n, const ui
 ND_ATTN_API int  nd_attn_prefill(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids,
                      const uint32_t *len, const void *q, const void *k, const void *v,
                      const void *gate, void *out);
-/* Same as nd_attn_decode / nd_attn_prefill with q/k/v/gate/out in HOST memory:
- * copies in through pinned staging, runs, copies out, waits. This is the form
- * the reference engine's attention() seam calls (its buffers m->q, m->kbuf,
- * m->vbuf, m->gate, m->attn are host floats, nd_model.c:1169-1173). */
+/* Same as nd_attn_decode / nd_attn_prefill with q/k/v/gate/out in HOST memory;
+ * both return after the work has completed. This is the form the reference
+ * engine's attention() seam calls (its buffers m->q, m->kbuf, m->vbuf,
+ * m->gate, m->attn are host floats, nd_model.c:1169-1173).
+ * decode_host: buffers that are pinned and mapped (cudaHostAlloc,
+ * cudaMallocHost, cudaHostRegister) are read and written in place by the
+ * kernels; pageable ones go through the handle's pinned staging with a host
+ * copy. No copy-engine transfer is issued. Device memory is refused
+ * (ND_ATTN_ERR_ARG).
+ * prefill_host: copies in through device staging, runs, copies out. */
 ND_ATTN_API int  nd_attn_decode_host(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids,
                          const void *q, const void *k, const void *v, const void *gate,
                          void *out);
