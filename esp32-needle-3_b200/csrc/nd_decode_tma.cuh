@@ -117,47 +117,61 @@ struct LeanWalk {
     }
 };
 
-// Output element (qi, e) of the item that starts at tile istart and holds T
-// tiles: merges the partials of its pieces (slot 2u + (item starts inside u))
-// eight pieces per load round, rescaling the running sums as the max grows.
+// Output row qi of the item that starts at tile istart and holds T tiles,
+// merged by one warp from the partials of its pieces (slot 2u + (item starts
+// inside u)), rescaling the running sums as the max grows. Lane c holds
+// output elements c, c + 32, ...; every piece's (m, l) and o are loaded in
+// one round of up to eight pieces: one L2 round trip per eight pieces.
 template <int HD, int NQ>
-__device__ __forceinline__ void lean_merge_elem(const AttnParams &P, const LeanUnits &U, uint32_t istart,
-                                                uint32_t T, uint32_t g, uint32_t row, int qi, int e) {
+__device__ __forceinline__ void lean_merge_row(const AttnParams &P, const LeanUnits &U, uint32_t istart,
+                                               uint32_t T, uint32_t g, uint32_t row, int qi, int lane) {
+    constexpr int EPL = HD / 32;
     const uint32_t kf = U.unit_of(istart), kl = U.unit_of(istart + T - 1);
-    float M = -INFINITY, L = 0.0f, o = 0.0f;
+    float M = -INFINITY, L = 0.0f, o[EPL];
+#pragma unroll
+    for (int c = 0; c < EPL; c++) o[c] = 0.0f;
     for (uint32_t u0 = kf; u0 <= kl; u0 += 8) {
-        float mp[8], lp[8], op[8];
+        float mp[8], lp[8], op[8][EPL];
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             mp[j] = -INFINITY;
-            lp[j] = op[j] = 0.0f;
+            lp[j] = 0.0f;
+#pragma unroll
+            for (int c = 0; c < EPL; c++) op[j][c] = 0.0f;
             if (u0 + j <= kl) {
                 const uint32_t uu = u0 + j, sl = 2 * uu + (istart > U.start(uu) ? 1u : 0u);
                 const size_t bq = (size_t)sl * NQ + qi;
                 const float2 ml = __ldcg(reinterpret_cast<const float2 *>(P.part_ml) + bq);
                 mp[j] = ml.x;
                 lp[j] = ml.y;
-                op[j] = __ldcg(&P.part_o[bq * HD + e]);
+#pragma unroll
+                for (int c = 0; c < EPL; c++) op[j][c] = __ldcg(&P.part_o[bq * HD + lane + 32 * c]);
             }
         }
         float Mn = M;
 #pragma unroll
         for (int j = 0; j < 8; j++) Mn = fmaxf(Mn, mp[j]);
         const float sc = ex2(M - Mn);
-        o *= sc;
         L *= sc;
+#pragma unroll
+        for (int c = 0; c < EPL; c++) o[c] *= sc;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             const float f = ex2(mp[j] - Mn);
-            o += op[j] * f;
             L += lp[j] * f;
+#pragma unroll
+            for (int c = 0; c < EPL; c++) o[c] += op[j][c] * f;
         }
         M = Mn;
     }
-    const size_t oi = ((size_t)row * P.n_heads + g * P.rep + qi) * HD + e;
-    float val = o / L;
-    if (P.gate) val *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, oi) * 1.4426950408889634f));
-    act_store(P.out, P.out_dt, oi, val);
+    const size_t ob = ((size_t)row * P.n_heads + g * P.rep + qi) * HD + lane;
+    const float inv = 1.0f / L;
+#pragma unroll
+    for (int c = 0; c < EPL; c++) {
+        float val = o[c] * inv;
+        if (P.gate) val *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, ob + 32 * c) * 1.4426950408889634f));
+        act_store(P.out, P.out_dt, ob + 32 * c, val);
+    }
 }
 
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -224,15 +238,14 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
     __syncthreads();
 
     // At its stop every warp helps merge the items this CTA completed (the
-    // finisher publishes them through settle_bar): flat element index over
-    // all 224 threads, the finisher's lanes first.
+    // finisher publishes them through settle_bar): one (item, query row) per
+    // warp at a time, the finisher's first.
     auto help_merge = [&]() {
         if (!__all_sync(0xffffffffu, mbar_wait(&settle_bar, 0, abort_flag))) return;
         const uint32_t nl = s_nlast;
-        const int mt = warp == FINISH ? lane : 32 + tid;
-        for (int f = mt; f < (int)(nl * rep * HD); f += 32 * (FINISH + 1)) {
-            const int k = f / (int)(rep * HD), r = f % (int)(rep * HD);
-            lean_merge_elem<HD, NQ>(P, U, pend[k][0], pend[k][1], pend[k][2], pend[k][3], r / HD, r % HD);
+        for (uint32_t pr = warp == FINISH ? 0u : (uint32_t)warp + 1u; pr < nl * rep; pr += FINISH + 1) {
+            const uint32_t k = pr / rep;
+            lean_merge_row<HD, NQ>(P, U, pend[k][0], pend[k][1], pend[k][2], pend[k][3], (int)(pr % rep), lane);
         }
     };
 
@@ -242,10 +255,19 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
             if (!P.early_kv) grid_dep_wait();
             uint32_t u = blockIdx.x, seg = 0, tc = 0;
             const int na = (int)P.lean_ahead;
+            // The first dynamic units are taken once the first wave of boxes
+            // is in flight: at launch every CTA's grab hits one counter, and
+            // the first boxes need not wait for that.
             uint32_t ahead[kLeanAheadMax];
+            bool grabbed = false;
+#define ND_LEAN_GRAB_AHEAD()                                                                        \
+    do {                                                                                            \
+        _Pragma("unroll") for (int a = 0; a < kLeanAheadMax; a++)                                  \
+            ahead[a] = a < na && U.NU > U.G ? (uint32_t)atomicAdd(work_ctr, 1) + U.G : U.NU;       \
+        grabbed = true;                                                                             \
+    } while (0)
 #pragma unroll
-            for (int a = 0; a < kLeanAheadMax; a++)
-                ahead[a] = a < na && U.NU > U.G ? (uint32_t)atomicAdd(work_ctr, 1) + U.G : U.NU;
+            for (int a = 0; a < kLeanAheadMax; a++) ahead[a] = U.NU;
             while (u < U.NU && !*abort_flag) {
                 uint32_t x = U.start(u);
                 const uint32_t xe = U.start(u + 1);
@@ -263,6 +285,7 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                     for (uint32_t k2 = 0; k2 < nt; k2++, tc++) {
                         const int y = (int)phys_row(P.c, w.seq, (w.kt + k2) * TR);
                         const uint32_t s2 = tc % STAGES;
+                        if (tc == STAGES && !grabbed) ND_LEAN_GRAB_AHEAD();
                         if (tc >= STAGES && !mbar_wait(&empty[s2], ((tc / STAGES) - 1) & 1, abort_flag)) break;
                         mbar_expect_tx(&full[s2], 2 * TILE_BYTES);
                         tma_load_2d(smem + s2 * TILE_BYTES, &kmap, (int)(w.g * HD), y, &full[s2]);
@@ -272,6 +295,7 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                     w.advance(P, nt);
                     seg++;
                 }
+                if (!grabbed) ND_LEAN_GRAB_AHEAD();
                 u = ahead[0];
 #pragma unroll
                 for (int a = 0; a + 1 < kLeanAheadMax; a++) ahead[a] = ahead[a + 1];
@@ -280,6 +304,7 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                 for (int a = 0; a < kLeanAheadMax; a++)
                     if (a == na - 1) ahead[a] = grab;
             }
+#undef ND_LEAN_GRAB_AHEAD
             // Every unit taken must be counted before the stop lets the finisher
             // report this CTA done (the last CTA out rewinds the counter): wait
             // for the values of the grabs still in flight.
@@ -460,11 +485,9 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                 __syncwarp();
                 if (++npend == 32) {   // rare: the finisher alone merges what completed
                     const uint32_t nl = settle();
-                    for (int f = lane; f < (int)(nl * rep * HD); f += 32) {
-                        const int k = f / (int)(rep * HD), r = f % (int)(rep * HD);
-                        lean_merge_elem<HD, NQ>(P, U, pend[k][0], pend[k][1], pend[k][2], pend[k][3], r / HD,
-                                                r % HD);
-                    }
+                    for (uint32_t pr = 0; pr < nl * rep; pr++)
+                        lean_merge_row<HD, NQ>(P, U, pend[pr / rep][0], pend[pr / rep][1], pend[pr / rep][2],
+                                               pend[pr / rep][3], (int)(pr % rep), lane);
                     __syncwarp();
                 }
             }
