@@ -119,6 +119,68 @@ __global__ void __launch_bounds__(256) ingest_kernel(const IngestParams P) {
     }
 }
 
+// QKV short causal convolution ahead of the path (tap_projection / tap_rows,
+// nd_model.c:2361-2379, 1753-1802). One thread per (span, column) walks the
+// span's tokens in order, so a history slot is never read and written by
+// different threads of a launch. Column i of the token at position p is
+//   0 + w[0][i]*x(p)[i] + w[1][i]*x(p-1)[i] + ...   over min(taps, p+1) taps,
+// each product and sum rounded on its own, in ascending tap order; x(p-j) is
+// the call's own raw row for positions inside the span, else the sequence's
+// history. The raw rows of the span's last min(len, taps) positions then go
+// to history slot p % taps. Columns [0, qd) are q, then k, then v.
+constexpr uint32_t kTapMax = 4;
+struct TapParams {
+    const void *x[3];           // raw q, k, v rows of the call
+    void *y[3];                 // convolved rows (same layout and type)
+    uint32_t dim[3];            // qd, kd, vd
+    const float *w;             // this layer's weights [q: taps][qd] [k: taps][kd] [v: taps][vd]
+    float *hist;                // [max_seqs][hist_seq]
+    size_t hist_seq;
+    size_t hist_off[3];         // this layer's q / k / v history inside a sequence's block
+    const nda::SeqSpan *spans;  // nullptr: span i = sequence i, row i, one token
+    const SeqState *state;      // the span's first position is its sequence's pos
+    uint32_t n_spans, taps, cols;
+    int act_dt;
+};
+
+__global__ void __launch_bounds__(128) tap_kernel(const TapParams P) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const uint32_t col = blockIdx.x * blockDim.x + threadIdx.x;
+    if (col >= P.cols) return;
+    const int which = col < P.dim[0] ? 0 : col < P.dim[0] + P.dim[1] ? 1 : 2;
+    const uint32_t D = P.dim[which];
+    const uint32_t c = col - (which > 0 ? P.dim[0] : 0u) - (which > 1 ? P.dim[1] : 0u);
+    const float *w = P.w + (which > 0 ? (size_t)P.taps * P.dim[0] : 0) + (which > 1 ? (size_t)P.taps * P.dim[1] : 0);
+    float wj[kTapMax];
+#pragma unroll
+    for (uint32_t j = 0; j < kTapMax; j++) wj[j] = j < P.taps ? w[(size_t)j * D + c] : 0.0f;
+    for (uint32_t sp = blockIdx.y; sp < P.n_spans; sp += gridDim.y) {
+        const nda::SeqSpan s = P.spans ? P.spans[sp] : nda::SeqSpan{sp, sp, 1u};
+        const uint32_t p0 = P.state[s.seq].pos;
+        float *hist = P.hist + (size_t)s.seq * P.hist_seq + P.hist_off[which];   // [taps][D]
+        float win[kTapMax];   // win[j] = x(p - 1 - j) before token p, x(p - j) after it
+#pragma unroll
+        for (uint32_t j = 0; j < kTapMax; j++)
+            win[j] = j + 1 < P.taps && p0 >= j + 1 ? hist[(size_t)((p0 - 1 - j) % P.taps) * D + c] : 0.0f;
+        for (uint32_t t = 0; t < s.len; t++) {
+            const uint32_t p = p0 + t;
+            const size_t xi = (size_t)(s.tok_base + t) * D + c;
+            const float x = nda::act_load(P.x[which], P.act_dt, xi);
+            float acc = __fadd_rn(0.0f, __fmul_rn(wj[0], x));
+#pragma unroll
+            for (uint32_t j = 1; j < kTapMax; j++)
+                if (j < P.taps && j <= p) acc = __fadd_rn(acc, __fmul_rn(wj[j], win[j - 1]));
+            nda::act_store(P.y[which], P.act_dt, xi, acc);
+#pragma unroll
+            for (uint32_t j = kTapMax - 1; j > 0; j--) win[j] = win[j - 1];
+            win[0] = x;
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < kTapMax; j++)
+            if (j < P.taps && j < s.len) hist[(size_t)((p0 + s.len - 1 - j) % P.taps) * D + c] = win[j];
+    }
+}
+
 // Failure-path diagnostics: one thread waits on an mbarrier that nothing
 // arrives on, for at most `limit` SM cycles, then reports the expiry through
 // the status word as the hot kernels' bounded waits do (code 3).
@@ -215,6 +277,18 @@ struct nd_attn {
     int last_writer = -1;
     int *err_host = nullptr;  // status word: pinned host memory mapped for the kernels
     int *d_err = nullptr;     // its device address
+    // QKV short causal convolution (qkv_conv_taps > 0). Tap weights per layer
+    // [q: taps][qd] [k: taps][kd] [v: taps][vd]; per sequence the history of
+    // raw projections [q: layers][taps][qd], then k, then v (the reference's
+    // q_hist / k_hist / v_hist, slot = position % taps) and its snapshot
+    // copy; the convolved rows of a call in the activation type, sized for
+    // max_seqs tokens at open (grown for larger prefills).
+    float *d_tapw = nullptr, *d_hist = nullptr, *d_snaphist = nullptr;
+    size_t hist_seq = 0;       // floats of history per sequence
+    char *d_tapio = nullptr;
+    size_t tapio_cap = 0;
+    nda::SeqSpan *d_tspans = nullptr;
+    size_t tspans_cap = 0;
     char *hstage = nullptr;       // host-buffer calls: pinned staging, mapped for the kernels
     char *hstage_dev = nullptr;   // its device address
     size_t hstage_cap = 0;
@@ -391,6 +465,55 @@ int upload_tok(nd_attn *h, const std::vector<TokMeta> &tok) {
 
 int make_map(CUtensorMap *m, bool bf16, const void *base, uint64_t inner, uint64_t rows, uint64_t stride_bytes,
              uint32_t box_rows, uint32_t box_inner, bool swizzle);
+
+// History block offsets of `layer` inside a sequence's [q | k | v] history.
+void tap_offsets(const nd_attn *h, uint32_t layer, size_t off[3]) {
+    const size_t T = h->cfg.qkv_conv_taps, L = h->cfg.n_layers;
+    const size_t qd = (size_t)h->cfg.n_heads * h->cfg.qk_head_dim, kd = h->k_dim, vd = h->v_dim;
+    off[0] = layer * T * qd;
+    off[1] = L * T * qd + layer * T * kd;
+    off[2] = L * T * (qd + kd) + layer * T * vd;
+}
+
+// Convolves the call's raw q/k/v rows into the handle's tap buffer
+// (tap_kernel) and points q/k/v at the result. spans: per sequence of the
+// call {sequence, first row, rows} (host); nullptr = sequence i is row i,
+// one token each. `rows` = rows of the call.
+int run_taps(nd_attn *h, uint32_t layer, uint32_t n_spans, const nda::SeqSpan *spans, uint32_t rows,
+             const void **q, const void **k, const void **v) {
+    const nd_attn_config &c = h->cfg;
+    const size_t qd = (size_t)c.n_heads * c.qk_head_dim, kd = h->k_dim, vd = h->v_dim, es = dt_size(c.act_dtype);
+    const size_t off1 = ((size_t)rows * qd * es + 255) / 256 * 256, off2 = off1 + ((size_t)rows * kd * es + 255) / 256 * 256;
+    const size_t need = off2 + (size_t)rows * vd * es;
+    int rc = grow(&h->d_tapio, &h->tapio_cap, need);
+    if (rc) return rc;
+    TapParams P;
+    memset(&P, 0, sizeof(P));
+    if (spans) {
+        rc = grow(&h->d_tspans, &h->tspans_cap, n_spans);
+        if (rc) return rc;
+        ND_CUDA(cudaMemcpyAsync(h->d_tspans, spans, n_spans * sizeof(nda::SeqSpan), cudaMemcpyHostToDevice, h->stream));
+        P.spans = h->d_tspans;
+    }
+    P.x[0] = *q, P.x[1] = *k, P.x[2] = *v;
+    P.y[0] = h->d_tapio, P.y[1] = h->d_tapio + off1, P.y[2] = h->d_tapio + off2;
+    P.dim[0] = (uint32_t)qd, P.dim[1] = (uint32_t)kd, P.dim[2] = (uint32_t)vd;
+    P.taps = c.qkv_conv_taps;
+    P.cols = (uint32_t)(qd + kd + vd);
+    P.w = h->d_tapw + (size_t)layer * P.taps * P.cols;
+    P.hist = h->d_hist;
+    P.hist_seq = h->hist_seq;
+    tap_offsets(h, layer, P.hist_off);
+    P.state = h->d_state;
+    P.n_spans = n_spans;
+    P.act_dt = c.act_dtype;
+    note_writer(h, kNoLayer);
+    tap_kernel<<<dim3((P.cols + 127) / 128, std::min<uint32_t>(n_spans, 65535u)), 128, 0, h->stream>>>(P);
+    h->launches++;
+    ND_CUDA(cudaGetLastError());
+    *q = P.y[0], *k = P.y[1], *v = P.y[2];
+    return ND_ATTN_OK;
+}
 
 // The balanced TMA-staged attend covers 16-bit caches with equal head dims of
 // 64 or 128 (GQA width <= 4 at 128), calls in which no position wraps the
@@ -813,6 +936,7 @@ int nd_attn_open(const nd_attn_config *cfg_in, nd_attn **out) {
     if (cfg.kv_dtype < ND_DT_I8 || cfg.kv_dtype > ND_DT_BF16 || cfg.act_dtype < ND_DT_F32 ||
         cfg.act_dtype > ND_DT_BF16 || cfg.out_dtype < ND_DT_F32 || cfg.out_dtype > ND_DT_BF16)
         return fail(ND_ATTN_ERR_ARG, "bad dtype");
+    if (cfg.qkv_conv_taps > kTapMax) return fail(ND_ATTN_ERR_GEOM, "qkv_conv_taps %u > %u", cfg.qkv_conv_taps, kTapMax);
     if (cfg.block_size) {
         if (cfg.block_size & (cfg.block_size - 1)) return fail(ND_ATTN_ERR_GEOM, "block_size must be a power of two");
         if (cfg.window % cfg.block_size) return fail(ND_ATTN_ERR_GEOM, "window must be a multiple of block_size");
@@ -922,6 +1046,31 @@ int nd_attn_open(const nd_attn_config *cfg_in, nd_attn **out) {
             return bail(fail(ND_ATTN_ERR_NOMEM, "split-KV scratch allocation failed"));
         cudaMemsetAsync(h->counters, 0, h->counter_cap * sizeof(int), h->stream);
     }
+    if (cfg.qkv_conv_taps) {
+        // Identity taps until set (w[0] = 1), zero history; the tap buffer
+        // serves a decode of every sequence without growing.
+        const size_t T = cfg.qkv_conv_taps, qd = (size_t)cfg.n_heads * cfg.qk_head_dim;
+        const size_t D = qd + h->k_dim + h->v_dim;
+        h->hist_seq = (size_t)cfg.n_layers * T * D;
+        std::vector<float> w((size_t)cfg.n_layers * T * D, 0.0f);
+        for (size_t l = 0; l < cfg.n_layers; l++) {
+            float *wl = w.data() + l * T * D;
+            for (size_t i = 0; i < qd; i++) wl[i] = 1.0f;
+            for (size_t i = 0; i < h->k_dim; i++) wl[T * qd + i] = 1.0f;
+            for (size_t i = 0; i < h->v_dim; i++) wl[T * (qd + h->k_dim) + i] = 1.0f;
+        }
+        const size_t es = dt_size(cfg.act_dtype), m = cfg.max_seqs;
+        if (cudaMalloc(&h->d_tapw, w.size() * sizeof(float)) != cudaSuccess ||
+            cudaMalloc(&h->d_hist, m * h->hist_seq * sizeof(float)) != cudaSuccess ||
+            cudaMalloc(&h->d_snaphist, m * h->hist_seq * sizeof(float)) != cudaSuccess ||
+            grow(&h->d_tapio, &h->tapio_cap, (m * qd * es + 255) / 256 * 256 + (m * h->k_dim * es + 255) / 256 * 256 +
+                                                m * h->v_dim * es) != ND_ATTN_OK)
+            return bail(fail(ND_ATTN_ERR_NOMEM, "conv tap state allocation failed"));
+        if (cudaMemcpy(h->d_tapw, w.data(), w.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess)
+            return bail(fail(ND_ATTN_ERR_CUDA, "conv tap upload failed"));
+        cudaMemsetAsync(h->d_hist, 0, m * h->hist_seq * sizeof(float), h->stream);
+        cudaMemsetAsync(h->d_snaphist, 0, m * h->hist_seq * sizeof(float), h->stream);
+    }
     if (cudaStreamSynchronize(h->stream) != cudaSuccess)
         return bail(fail(ND_ATTN_ERR_CUDA, "initialisation failed: %s", cudaGetErrorString(cudaGetLastError())));
     *out = h;
@@ -936,6 +1085,7 @@ void nd_attn_close(nd_attn *h) {
     cudaFree(h->rope); cudaFree(h->norms); cudaFree(h->d_state); cudaFree(h->d_btab);
     cudaFree(h->part_o); cudaFree(h->part_ml); cudaFree(h->counters);
     cudaFree(h->d_tok); cudaFree(h->d_u32); cudaFree(h->d_lean); cudaFree(h->d_vbig); cudaFree(h->dio); cudaFree(h->d_work); cudaFree(h->d_spans);
+    cudaFree(h->d_tapw); cudaFree(h->d_hist); cudaFree(h->d_snaphist); cudaFree(h->d_tapio); cudaFree(h->d_tspans);
     if (h->hstage) cudaFreeHost(h->hstage);
     if (h->err_host) cudaFreeHost(h->err_host);
     if (h->own) cudaStreamDestroy(h->own);
@@ -959,12 +1109,43 @@ int nd_attn_set_head_norm(nd_attn *h, uint32_t layer, const float *q_scale, cons
     return ND_ATTN_OK;
 }
 
+int nd_attn_set_conv_taps(nd_attn *h, uint32_t layer, const float *wq, const float *wk, const float *wv) {
+    if (!h) return fail(ND_ATTN_ERR_ARG, "null handle");
+    if (!h->cfg.qkv_conv_taps) return fail(ND_ATTN_ERR_ARG, "the handle was opened without conv taps");
+    if (layer >= h->cfg.n_layers) return fail(ND_ATTN_ERR_RANGE, "layer %u", layer);
+    if (!wq || !wk || !wv) return fail(ND_ATTN_ERR_ARG, "null tap weights");
+    DeviceGuard dg(h->cfg.device);
+    const size_t T = h->cfg.qkv_conv_taps, qd = (size_t)h->cfg.n_heads * h->cfg.qk_head_dim;
+    float *wl = h->d_tapw + (size_t)layer * T * (qd + h->k_dim + h->v_dim);
+    ND_CUDA(cudaStreamSynchronize(h->stream));
+    ND_CUDA(cudaMemcpy(wl, wq, T * qd * sizeof(float), cudaMemcpyHostToDevice));
+    ND_CUDA(cudaMemcpy(wl + T * qd, wk, T * h->k_dim * sizeof(float), cudaMemcpyHostToDevice));
+    ND_CUDA(cudaMemcpy(wl + T * (qd + h->k_dim), wv, T * h->v_dim * sizeof(float), cudaMemcpyHostToDevice));
+    return ND_ATTN_OK;
+}
+
+// Tap history of a sequence: cleared by reset (nd_model.c:1575-1580), copied
+// by snapshot and rewind (1423-1425, 1451-1453).
+static int hist_reset(nd_attn *h, uint32_t seq) {
+    if (!h->cfg.qkv_conv_taps) return ND_ATTN_OK;
+    ND_CUDA(cudaMemsetAsync(h->d_hist + seq * h->hist_seq, 0, h->hist_seq * sizeof(float), h->stream));
+    return ND_ATTN_OK;
+}
+static int hist_copy(nd_attn *h, uint32_t seq, bool to_snapshot) {
+    if (!h->cfg.qkv_conv_taps) return ND_ATTN_OK;
+    float *live = h->d_hist + seq * h->hist_seq, *snap = h->d_snaphist + seq * h->hist_seq;
+    ND_CUDA(cudaMemcpyAsync(to_snapshot ? snap : live, to_snapshot ? live : snap, h->hist_seq * sizeof(float),
+                            cudaMemcpyDeviceToDevice, h->stream));
+    return ND_ATTN_OK;
+}
+
 int nd_attn_reset(nd_attn *h, uint32_t seq) {
     int rc = check_seq(h, seq);
     if (rc) return rc;
     DeviceGuard dg(h->cfg.device);
     h->seqs[seq] = HostSeq();
-    return push_state(h, seq);
+    rc = hist_reset(h, seq);
+    return rc ? rc : push_state(h, seq);
 }
 
 int nd_attn_set_sink(nd_attn *h, uint32_t seq, uint32_t n) {
@@ -985,7 +1166,8 @@ int nd_attn_snapshot(nd_attn *h, uint32_t seq) {
     s.n_sink = s.pos > cap ? cap : s.pos;
     s.snap_pos = s.pos;
     s.has_snap = 1;
-    return push_state(h, seq);
+    rc = hist_copy(h, seq, true);
+    return rc ? rc : push_state(h, seq);
 }
 
 int nd_attn_rewind(nd_attn *h, uint32_t seq) {
@@ -995,7 +1177,8 @@ int nd_attn_rewind(nd_attn *h, uint32_t seq) {
     if (!s.has_snap) return nd_attn_reset(h, seq);
     DeviceGuard dg(h->cfg.device);
     s.pos = s.snap_pos;
-    return push_state(h, seq);
+    rc = hist_copy(h, seq, false);
+    return rc ? rc : push_state(h, seq);
 }
 
 int nd_attn_advance(nd_attn *h, uint32_t n, const uint32_t *seq_ids, const uint32_t *len) {
@@ -1050,6 +1233,15 @@ int nd_attn_decode(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
     if (rc) return rc;
     if (!q || !k || !v || !out) return fail(ND_ATTN_ERR_ARG, "null tensor");
     DeviceGuard dg(h->cfg.device);
+    if (h->cfg.qkv_conv_taps) {
+        std::vector<nda::SeqSpan> sp;
+        if (seq_ids) {
+            sp.resize(n);
+            for (uint32_t i = 0; i < n; i++) sp[i] = nda::SeqSpan{seq_ids[i], i, 1u};
+        }
+        rc = run_taps(h, layer, n, seq_ids ? sp.data() : nullptr, n, &q, &k, &v);
+        if (rc) return rc;
+    }
     std::vector<uint32_t> vis(n), tseq(n), tpos(n);
     bool no_wrap = true;
     for (uint32_t i = 0; i < n; i++) {
@@ -1092,6 +1284,13 @@ int nd_attn_prefill(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_
     }
     if (total == 0) return ND_ATTN_OK;
     if (total > 0x7fffffffu / h->cfg.n_kv_heads) return fail(ND_ATTN_ERR_RANGE, "too many tokens");
+    if (h->cfg.qkv_conv_taps) {
+        std::vector<nda::SeqSpan> sp;
+        for (uint32_t i = 0; i < n; i++)
+            if (len[i]) sp.push_back(nda::SeqSpan{seq_ids ? seq_ids[i] : i, cu[i], len[i]});
+        rc = run_taps(h, layer, (uint32_t)sp.size(), sp.data(), (uint32_t)total, &q, &k, &v);
+        if (rc) return rc;
+    }
     if (!wraps) {
         // Every new position gets its own slot and nothing a token reads is
         // overwritten: append all tokens, then attend causally.
@@ -1364,6 +1563,10 @@ int nd_attn_decode_noalloc(nd_attn *h, uint32_t layer, uint32_t n, const void *q
     char *base = nullptr;
     int rc = noalloc_scratch(h->cfg.device, &base);
     if (rc) return rc;
+    if (h->cfg.qkv_conv_taps) {   // the tap buffer was sized for max_seqs tokens at open: no allocation
+        rc = run_taps(h, layer, n, nullptr, n, &q, &k, &v);
+        if (rc) return rc;
+    }
     const size_t nq = (size_t)nda::nq_for_rep(h->rep);
     const size_t vd = h->cfg.v_head_dim;
     const size_t ticket_bytes = (size_t)ND_ATTN_NOALLOC_MAX_ITEMS * sizeof(int);
@@ -1402,7 +1605,10 @@ nd_attn_prefix *nd_attn_prefix_save(nd_attn *h, uint32_t seq) {
     const uint32_t live = std::min(s.snap_pos + 1u, c.window);
     const size_t krow = h->k_dim * h->kes, vrow = h->v_dim * h->kes, srow = c.n_kv_heads * sizeof(float);
     const bool sc = c.kv_dtype == ND_DT_I8;
-    const size_t bytes = (size_t)c.n_layers * live * (krow + vrow + (sc ? 2 * srow : 0));
+    // prefix_copy's order (nd_model.c:1493-1529): live K, V (and scale) rows,
+    // then the snapshot's tap histories.
+    const size_t hist_bytes = h->hist_seq * sizeof(float);
+    const size_t bytes = (size_t)c.n_layers * live * (krow + vrow + (sc ? 2 * srow : 0)) + hist_bytes;
     nd_attn_prefix *p = new nd_attn_prefix();
     p->owner = h; p->pos = s.snap_pos; p->sink = s.n_sink; p->live = live; p->bytes = bytes;
     if (cudaMalloc(&p->dev, std::max<size_t>(bytes, 4)) != cudaSuccess) {
@@ -1421,6 +1627,8 @@ nd_attn_prefix *nd_attn_prefix_save(nd_attn *h, uint32_t seq) {
         h->launches++;
         dst += (size_t)c.n_layers * live * parts[i].row;
     }
+    if (hist_bytes)
+        cudaMemcpyAsync(dst, h->d_snaphist + seq * h->hist_seq, hist_bytes, cudaMemcpyDeviceToDevice, h->stream);
     if (cudaStreamSynchronize(h->stream) != cudaSuccess) {
         fail(ND_ATTN_ERR_CUDA, "prefix copy failed: %s", cudaGetErrorString(cudaGetLastError()));
         cudaFree(p->dev);
@@ -1453,10 +1661,14 @@ int nd_attn_prefix_restore(nd_attn *h, uint32_t seq, const nd_attn_prefix *p) {
         h->launches++;
         src += (size_t)c.n_layers * p->live * parts[i].row;
     }
+    if (h->hist_seq)
+        ND_CUDA(cudaMemcpyAsync(h->d_snaphist + seq * h->hist_seq, src, h->hist_seq * sizeof(float),
+                                cudaMemcpyDeviceToDevice, h->stream));
     ND_CUDA(cudaGetLastError());
     s.has_snap = 1;
     s.pos = s.snap_pos;  // nd_model_rewind
-    return push_state(h, seq);
+    rc = hist_copy(h, seq, false);
+    return rc ? rc : push_state(h, seq);
 }
 
 void nd_attn_prefix_free(nd_attn_prefix *p) {
@@ -1600,7 +1812,7 @@ const nd_attn_ops *nd_attn_cuda_ops(void) {
         nd_attn_reset,         nd_attn_set_sink,      nd_attn_snapshot,     nd_attn_rewind,
         nd_attn_advance,       nd_attn_decode,        nd_attn_prefill,      nd_attn_decode_host,
         nd_attn_prefill_host,  nd_attn_prefix_save,   nd_attn_prefix_restore, nd_attn_prefix_free,
-        nd_attn_sync,          nd_attn_last_error,
+        nd_attn_sync,          nd_attn_last_error,    nd_attn_set_conv_taps,
     };
     return &ops;
 }

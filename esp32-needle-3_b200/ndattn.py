@@ -45,7 +45,8 @@ class Config(ctypes.Structure):
                 ("qk_head_dim", c_uint32), ("v_head_dim", c_uint32), ("window", c_uint32),
                 ("max_seqs", c_uint32), ("block_size", c_uint32), ("n_blocks", c_uint32),
                 ("max_pos", c_uint32), ("rope_theta", c_float), ("kv_dtype", c_int32),
-                ("act_dtype", c_int32), ("out_dtype", c_int32), ("device", c_int32)]
+                ("act_dtype", c_int32), ("out_dtype", c_int32), ("device", c_int32),
+                ("qkv_conv_taps", c_uint32)]
 
 
 _lib = None
@@ -71,6 +72,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "nd_attn_open": (c_int, [POINTER(Config), POINTER(vp)]),
         "nd_attn_close": (None, [vp]),
         "nd_attn_set_head_norm": (c_int, [vp, u32, vp, vp]),
+        "nd_attn_set_conv_taps": (c_int, [vp, u32, vp, vp, vp]),
         "nd_attn_reset": (c_int, [vp, u32]),
         "nd_attn_set_sink": (c_int, [vp, u32, u32]),
         "nd_attn_snapshot": (c_int, [vp, u32]),
@@ -170,7 +172,7 @@ class Attn:
 
     def __init__(self, n_layers=1, n_heads=8, n_kv_heads=8, qk_head_dim=64, v_head_dim=64, window=384,
                  max_seqs=1, block_size=0, n_blocks=0, max_pos=0, rope_theta=10000.0, kv_dtype="f32",
-                 act_dtype="f32", out_dtype=None, device=0):
+                 act_dtype="f32", out_dtype=None, device=0, qkv_conv_taps=0):
         lib = load()
         cfg = Config()
         lib.nd_attn_config_init(ctypes.byref(cfg))
@@ -180,7 +182,7 @@ class Attn:
                          n_blocks=n_blocks, max_pos=max_pos or window, rope_theta=rope_theta,
                          kv_dtype=dt(kv_dtype), act_dtype=dt(act_dtype),
                          out_dtype=dt(out_dtype if out_dtype is not None else act_dtype),
-                         device=device).items():
+                         device=device, qkv_conv_taps=qkv_conv_taps).items():
             setattr(cfg, k, v)
         self.cfg = cfg
         h = c_void_p()
@@ -211,6 +213,11 @@ class Attn:
         q = None if q_scale is None else np.ascontiguousarray(q_scale, dtype=np.float32)
         k = None if k_scale is None else np.ascontiguousarray(k_scale, dtype=np.float32)
         _check(load().nd_attn_set_head_norm(self.h, layer, _hptr(q), _hptr(k)))
+
+    def set_conv_taps(self, layer: int, wq, wk, wv) -> None:
+        """Tap weights [taps][dim] of the layer's q, k and v projections."""
+        w = [np.ascontiguousarray(x, dtype=np.float32) for x in (wq, wk, wv)]
+        _check(load().nd_attn_set_conv_taps(self.h, layer, *(_hptr(x) for x in w)))
 
     def reset(self, seq: int = 0) -> None:
         _check(load().nd_attn_reset(self.h, seq))

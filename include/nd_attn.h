@@ -99,6 +99,9 @@ typedef struct {
     int32_t  act_dtype;      /* q/k/v/gate element type: F32, F16 or BF16 */
     int32_t  out_dtype;      /* out element type: F32, F16 or BF16 */
     int32_t  device;         /* CUDA device ordinal */
+    uint32_t qkv_conv_taps;  /* 0, or the short causal convolution over q/k/v
+                              * projections (nd_cact_header.qkv_conv_taps,
+                              * nd_cact.h:55), at most 4 taps */
 } nd_attn_config;
 
 typedef struct nd_attn nd_attn;
@@ -121,6 +124,23 @@ ND_ATTN_API void nd_attn_close(nd_attn *h);
  * (apply_rope, nd_model.c:381-397). */
 ND_ATTN_API int  nd_attn_set_head_norm(nd_attn *h, uint32_t layer,
                            const float *q_scale, const float *k_scale);
+
+/* Per-layer tap weights of the QKV short causal convolution, the layer's
+ * archive tensors 4, 5 and 6 staged as floats (nd_model.c:782-823):
+ * wq [taps][n_heads * qk_head_dim], wk [taps][n_kv_heads * qk_head_dim],
+ * wv [taps][n_kv_heads * v_head_dim], element (j, i) at j * dim + i (host).
+ * With taps configured, the q/k/v every decode and prefill call takes are the
+ * raw projections: each token's column i becomes
+ *   0 + w[0][i]*x(pos)[i] + w[1][i]*x(pos-1)[i] + ...  over min(taps, pos+1)
+ * taps, separately rounded in ascending tap order (tap_projection /
+ * tap_rows, nd_model.c:2361-2379, 1753-1802), before the head norm and RoPE.
+ * The per-sequence history of raw projections is kept on the device; reset
+ * clears it, snapshot / rewind / prefix_save / prefix_restore carry it like
+ * nd_model_snapshot (nd_model.c:1395-1456). Layers start with w[0] = 1 and
+ * the other taps 0. 16-bit activations: the convolved rows are rounded to
+ * act_dtype. */
+ND_ATTN_API int  nd_attn_set_conv_taps(nd_attn *h, uint32_t layer, const float *wq, const float *wk,
+                           const float *wv);
 
 /* ---- session state (per sequence) --------------------------------------- */
 /* nd_model_reset (nd_model.c:1557-1581): pos = 0, n_sink = 0, no snapshot. */
@@ -240,7 +260,7 @@ ND_ATTN_API int  nd_attn_set_block_table(nd_attn *h, uint32_t seq, const int32_t
  * engine/src/nd_quant.c:717). nd_attn_cuda_ops() returns this library's table;
  * its members are the entry points declared above. No reference counterpart
  * for the accessor itself. */
-#define ND_ATTN_OPS_VERSION 1u
+#define ND_ATTN_OPS_VERSION 2u
 typedef struct nd_attn_ops {
     uint32_t version;   /* ND_ATTN_OPS_VERSION */
     int  (*open)(const nd_attn_config *cfg, nd_attn **out);
@@ -265,6 +285,7 @@ typedef struct nd_attn_ops {
     void (*prefix_free)(nd_attn_prefix *p);
     int  (*sync)(nd_attn *h);
     const char *(*last_error)(void);
+    int  (*set_conv_taps)(nd_attn *h, uint32_t layer, const float *wq, const float *wk, const float *wv);
 } nd_attn_ops;
 ND_ATTN_API const nd_attn_ops *nd_attn_cuda_ops(void);
 

@@ -191,6 +191,31 @@ static double ndo_load(const void *base, int32_t dt, size_t idx)
     }
 }
 
+/* QKV short causal convolution, tap_projection / tap_rows (nd_model.c:
+ * 2361-2379, 1753-1802): history slot pos % taps takes the raw row x, then
+ *   out[i] = 0 + w[0][i]*h(pos)[i] + w[1][i]*h(pos-1)[i] + ...
+ * over min(taps, pos+1) taps in ascending order, every product and sum
+ * rounded on its own (no contraction). w and hist are [taps][dim]. */
+int ndo_conv_taps(uint32_t taps, uint32_t pos, uint32_t dim, const float *w, const float *x, float *hist,
+                  float *out)
+{
+    uint32_t i, j, nt;
+
+    if (!taps) return -1;
+    nt = taps < pos + 1u ? taps : pos + 1u;
+    memcpy(hist + (size_t)(pos % taps) * dim, x, (size_t)dim * sizeof(float));
+    for (i = 0; i < dim; i++) {
+        float acc = 0.0f;
+        for (j = 0; j < nt; j++) {
+            const float prod = w[(size_t)j * dim + i] * hist[(size_t)((pos - j) % taps) * dim + i];
+            acc = acc + prod;
+        }
+        out[i] = acc;
+    }
+    return 0;
+}
+
+
 /* Rotate q/k (in place), store k/v at kv_slot(pos), attend. Caches are one
  * (layer, sequence) view: k [window][n_kv*qk_hd], v [window][n_kv*v_hd],
  * scales [window][n_kv] (int8 only). gate NULL = gate of 1. out is double

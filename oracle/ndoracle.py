@@ -60,6 +60,8 @@ def orc() -> ctypes.CDLL:
         lib.ndo_token.argtypes = [POINTER(Geom), c_void_p, c_void_p, c_void_p, c_void_p, c_uint32, c_uint32,
                                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                   c_void_p, c_void_p]
+        lib.ndo_conv_taps.restype = c_int
+        lib.ndo_conv_taps.argtypes = [c_uint32, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p, c_void_p]
         lib.ndo_rope_table.argtypes = [c_float, c_uint32, c_uint32, c_void_p]
         lib.ndo_rope_table.restype = None
         lib.ndo_kv_slot.restype = c_uint32
@@ -99,7 +101,10 @@ def ref() -> ctypes.CDLL:
         lib.ndref_rope_at.argtypes = [c_void_p, c_uint32, c_uint32, c_void_p, c_void_p]
         lib.ndref_prefix_image.restype = c_long
         lib.ndref_prefix_image.argtypes = [POINTER(RefGeom), c_void_p, c_void_p, c_void_p, c_void_p, c_uint32,
-                                           c_void_p, c_size_t, POINTER(c_uint32)]
+                                           c_uint32, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                                           POINTER(c_uint32)]
+        lib.ndref_tap.restype = c_int
+        lib.ndref_tap.argtypes = [c_uint32, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p]
         lib.ndref_prefill_bench.restype = c_double
         lib.ndref_prefill_bench.argtypes = [POINTER(RefGeom), c_uint32, c_uint32, c_uint32, c_float, c_uint32]
         lib.ndref_decode_bench.restype = c_double
@@ -157,7 +162,13 @@ def set_sink_cap(window: int, n: int) -> int:
 
 # ------------------------------------------------------------ sequences
 class _SeqBase:
-    def __init__(self, n_layers, n_heads, n_kv_heads, qk, vd, window, kv_dtype, theta=10000.0, max_pos=None):
+    """One sequence of the reference session. taps > 0 adds the QKV short
+    causal convolution ahead of the path (tap_projection, nd_model.c:2361-2379)
+    with its per-layer history; act_dtype is the activation type its output is
+    rounded to (the GPU path stores convolved rows in that type)."""
+
+    def __init__(self, n_layers, n_heads, n_kv_heads, qk, vd, window, kv_dtype, theta=10000.0, max_pos=None,
+                 taps=0, act_dtype=F32):
         self.L, self.H, self.HKV, self.QK, self.VD, self.W = n_layers, n_heads, n_kv_heads, qk, vd, window
         self.kv_dtype = kv_dtype
         npdt = NP_KV[kv_dtype]
@@ -169,11 +180,38 @@ class _SeqBase:
         self.has_snap = False
         self.tab = rope_table(theta, qk, max_pos or window)
         self.norms: dict[int, tuple[np.ndarray, np.ndarray]] = {}
+        self.T, self.act_dtype = taps, act_dtype
+        dims = (n_heads * qk, n_kv_heads * qk, n_kv_heads * vd)
+        # q_hist / k_hist / v_hist [layers][taps][dim] and the snapshot copies
+        self.hist = [np.zeros((n_layers, taps, d), np.float32) for d in dims]
+        self.snap_hist = [h.copy() for h in self.hist]
+        ident = [np.zeros((taps, d), np.float32) for d in dims]
+        for w in ident:
+            w[:1] = 1.0
+        self.tapw = {layer: ident for layer in range(n_layers)}
+
+    def set_conv_taps(self, layer, wq, wk, wv):
+        self.tapw[layer] = [np.ascontiguousarray(w, dtype=np.float32) for w in (wq, wk, wv)]
+
+    def conv(self, layer, pos, q, k, v):
+        """The convolved q, k, v of the token at `pos` (history updated)."""
+        out = []
+        for x, w, h in zip((q, k, v), self.tapw[layer], self.hist):
+            x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+            hl = np.ascontiguousarray(h[layer])
+            y = np.zeros_like(x)
+            assert orc().ndo_conv_taps(self.T, pos, x.size, w.ctypes.data, x.ctypes.data, hl.ctypes.data,
+                                       y.ctypes.data) == 0
+            h[layer] = hl
+            out.append(round_act(y, self.act_dtype))
+        return out
 
     # reference session rules
     def reset(self):
         self.pos = self.n_sink = 0
         self.has_snap = False
+        for h in self.hist:
+            h[...] = 0.0
 
     def set_sink(self, n):
         self.n_sink = set_sink_cap(self.W, n)
@@ -182,12 +220,14 @@ class _SeqBase:
         self.set_sink(self.pos)
         self.snap_pos = self.pos
         self.has_snap = True
+        self.snap_hist = [h.copy() for h in self.hist]
 
     def rewind(self):
         if not self.has_snap:
             self.reset()
         else:
             self.pos = self.snap_pos
+            self.hist = [h.copy() for h in self.snap_hist]
 
     def advance(self, n=1):
         self.pos += n
@@ -199,6 +239,7 @@ class _SeqBase:
         parts = [self.k[:, :live], self.v[:, :live]]
         if self.kv_dtype == I8:
             parts += [self.ks[:, :live], self.vs[:, :live]]
+        parts += self.snap_hist          # q_hist, k_hist, v_hist of the snapshot (empty without taps)
         return b"".join(np.ascontiguousarray(p).tobytes() for p in parts)
 
     def prefix_save(self):
@@ -206,13 +247,15 @@ class _SeqBase:
             return None
         live = min(self.snap_pos + 1, self.W)
         return dict(pos=self.snap_pos, sink=self.n_sink, live=live, k=self.k[:, :live].copy(),
-                    v=self.v[:, :live].copy(), ks=self.ks[:, :live].copy(), vs=self.vs[:, :live].copy())
+                    v=self.v[:, :live].copy(), ks=self.ks[:, :live].copy(), vs=self.vs[:, :live].copy(),
+                    hist=[h.copy() for h in self.snap_hist])
 
     def prefix_restore(self, p):
         self.snap_pos, self.n_sink = p["pos"], p["sink"]
         live = p["live"]
         self.k[:, :live], self.v[:, :live] = p["k"], p["v"]
         self.ks[:, :live], self.vs[:, :live] = p["ks"], p["vs"]
+        self.snap_hist = [h.copy() for h in p["hist"]]
         self.has_snap = True
         self.rewind()
 
@@ -226,6 +269,8 @@ class OracleSeq(_SeqBase):
 
     def step(self, layer, q, k, v, gate=None, off=0):
         pos = self.pos + off
+        if self.T:
+            q, k, v = self.conv(layer, pos, q, k, v)
         g = Geom(self.H, self.HKV, self.QK, self.VD, self.W, self.kv_dtype)
         q = np.array(q, dtype=np.float32, copy=True).reshape(-1)
         k = np.array(k, dtype=np.float32, copy=True).reshape(-1)
@@ -252,8 +297,21 @@ class RefSeq(_SeqBase):
     def geom(self):
         return RefGeom(self.L, self.H, self.HKV, self.QK, self.VD, self.W)
 
+    def conv(self, layer, pos, q, k, v):
+        """The reference's own tap_projection on q, k, v (history updated)."""
+        out = []
+        for x, w, h in zip((q, k, v), self.tapw[layer], self.hist):
+            y = np.array(x, dtype=np.float32, copy=True).reshape(-1)
+            hl = np.ascontiguousarray(h[layer])
+            assert ref().ndref_tap(self.T, pos, y.size, w.ctypes.data, y.ctypes.data, hl.ctypes.data) == 0
+            h[layer] = hl
+            out.append(y)
+        return out
+
     def step(self, layer, q, k, v, gate=None, off=0):
         pos = self.pos + off
+        if self.T:
+            q, k, v = self.conv(layer, pos, q, k, v)
         g = self.geom()
         q = np.array(q, dtype=np.float32, copy=True).reshape(-1)
         k = np.array(k, dtype=np.float32, copy=True).reshape(-1)
@@ -273,11 +331,14 @@ class RefSeq(_SeqBase):
         """The image the reference's own nd_model_snapshot + prefix_save make at pos."""
         g = self.geom()
         sink = c_uint32()
+        hist = [np.ascontiguousarray(h) for h in self.hist]
+        hp = [h.ctypes.data if self.T else None for h in hist]
         n = ref().ndref_prefix_image(ctypes.byref(g), self.k.ctypes.data, self.v.ctypes.data, self.ks.ctypes.data,
-                                     self.vs.ctypes.data, self.pos, None, 0, ctypes.byref(sink))
+                                     self.vs.ctypes.data, self.pos, self.T, *hp, None, 0, ctypes.byref(sink))
         buf = np.zeros(max(n, 1), dtype=np.uint8)
         ref().ndref_prefix_image(ctypes.byref(g), self.k.ctypes.data, self.v.ctypes.data, self.ks.ctypes.data,
-                                 self.vs.ctypes.data, self.pos, buf.ctypes.data, buf.size, ctypes.byref(sink))
+                                 self.vs.ctypes.data, self.pos, self.T, *hp, buf.ctypes.data, buf.size,
+                                 ctypes.byref(sink))
         return buf[:n].tobytes(), sink.value
 
 

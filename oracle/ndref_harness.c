@@ -14,6 +14,7 @@
  *   kv_store_int8                   nd_model.c:1822-1866
  *   attn_heads                      nd_model.c:2105-2359
  *   nd_model_snapshot / prefix_save nd_model.c:1395-1541
+ *   tap_projection / tap_rows       nd_model.c:2361-2379, 1753-1802  QKV conv taps
  *
  * The only statements restated here are the glue that attention()
  * (nd_model.c:2382-2502) runs inline between those calls: the per-KV-head
@@ -178,13 +179,31 @@ int ndref_attn_token(const ndref_geom *g, int8_t *k_cache, int8_t *v_cache,
     return 0;
 }
 
+/* The reference's tap_projection on one projection row (layer 0): `hist` is
+ * that layer's [taps][dim] history (slot pos % taps takes the row), `w` its
+ * staged [taps][dim] weights; `proj` is replaced by the convolved row. */
+int ndref_tap(uint32_t taps, uint32_t pos, uint32_t dim, const float *w, float *proj, float *hist)
+{
+    nd_model m;
+
+    if (!taps) return -1;
+    memset(&m, 0, sizeof(m));
+    m.c.h.qkv_conv_taps = taps;
+    m.pos = pos;
+    m.fp16_slot[0][4] = (float *)w;
+    tap_projection(&m, 4, proj, hist, 0, dim);
+    return 0;
+}
+
 /* The reference's saved-prefix image for a session whose caches are given:
  * nd_model_snapshot at `pos` (pins the sinks), then nd_model_prefix_save, with
- * no conv-tap, engram or confidence state (zero taps, zero sites). Writes the
+ * no engram or confidence state (zero sites). `taps` > 0 adds the conv-tap
+ * histories q_hist / k_hist / v_hist ([layers][taps][dim] each). Writes the
  * image bytes (prefix_copy order, nd_model.c:1493-1529) to `img` if it is large
  * enough and returns its size; *sink gets the pinned count. */
 long ndref_prefix_image(const ndref_geom *g, int8_t *k_cache, int8_t *v_cache,
-                        float *k_scale, float *v_scale, uint32_t pos,
+                        float *k_scale, float *v_scale, uint32_t pos, uint32_t taps,
+                        float *q_hist, float *k_hist, float *v_hist,
                         unsigned char *img, size_t cap, uint32_t *sink)
 {
     nd_model   m;
@@ -195,6 +214,8 @@ long ndref_prefix_image(const ndref_geom *g, int8_t *k_cache, int8_t *v_cache,
     m.pos = pos;
     m.k_cache = k_cache; m.v_cache = v_cache;
     m.k_scale = k_scale; m.v_scale = v_scale;
+    m.c.h.qkv_conv_taps = taps;
+    m.q_hist = q_hist; m.k_hist = k_hist; m.v_hist = v_hist;
     if (nd_model_snapshot(&m)) return -1;
     p = nd_model_prefix_save(&m);
     if (!p) return -1;

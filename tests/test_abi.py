@@ -103,7 +103,7 @@ def test_hook_table_points_at_the_entry_points(tmp_path):
     name; built as a C program against the header and linked to the library."""
     members = ["open", "close", "set_head_norm", "reset", "set_sink", "snapshot", "rewind", "advance", "decode",
                "prefill", "decode_host", "prefill_host", "prefix_save", "prefix_restore", "prefix_free", "sync",
-               "last_error"]
+               "last_error", "set_conv_taps"]
     checks = "\n".join(f'    bad += (void *)o->{m} != (void *)nd_attn_{m};' for m in members)
     src = tmp_path / "ops.c"
     src.write_text('#include <stdio.h>\n#include "nd_attn.h"\nint main(void){\n'

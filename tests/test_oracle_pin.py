@@ -90,6 +90,74 @@ def test_prefix_image_matches_reference():
     assert img == mine.prefix_image()
 
 
+@pytest.mark.parametrize("taps", [1, 2, 3, 4])
+@pytest.mark.parametrize("dim", [48, 257])
+def test_conv_taps_match_reference(taps, dim):
+    """The QKV short causal convolution: the restatement against the
+    reference's own tap_projection (nd_model.c:2361-2379), outputs and
+    history bit for bit over positions 0.. (the ramp of min(taps, pos+1)
+    taps, then every history slot reused), an odd width (the reference's
+    two-column loop plus its tail) and signed zeros among the weights."""
+    rng = np.random.default_rng(taps * 1000 + dim)
+    w = (rng.standard_normal((taps, dim)) * 0.7).astype(np.float32)
+    w[:, ::11] = 0.0
+    w[:, 5::13] = -0.0
+    h_ref = np.zeros((taps, dim), np.float32)
+    h_mine = np.zeros((taps, dim), np.float32)
+    for pos in range(3 * taps + 4):
+        x = rng.standard_normal(dim).astype(np.float32)
+        x[::7] = -0.0
+        ref_row = x.copy()
+        assert O.ref().ndref_tap(taps, pos, dim, w.ctypes.data, ref_row.ctypes.data, h_ref.ctypes.data) == 0
+        out = np.zeros(dim, np.float32)
+        assert O.orc().ndo_conv_taps(taps, pos, dim, w.ctypes.data, x.ctypes.data, h_mine.ctypes.data,
+                                     out.ctypes.data) == 0
+        assert np.array_equal(ref_row.view(np.uint32), out.view(np.uint32)), pos
+        assert np.array_equal(h_ref.view(np.uint32), h_mine.view(np.uint32)), pos
+
+
+def test_conv_taps_session_and_prefix_image_match_reference():
+    """A session with 3 conv taps through both: the reference's tap_projection
+    + attention and the restatement. Int8 KV bytes bit-exact, outputs within
+    1e-5, and after a snapshot, a rewind and more tokens, the saved-prefix
+    image (KV rows, scales, then q/k/v tap histories) byte for byte."""
+    rng = np.random.default_rng(17)
+    H, HKV, QK, VD, W, L, T = 8, 2, 64, 64, 160, 2, 3
+    ref = O.RefSeq(L, H, HKV, QK, VD, W, O.I8, taps=T)
+    mine = O.OracleSeq(L, H, HKV, QK, VD, W, O.I8, taps=T)
+    for l in range(L):
+        ws = [(rng.standard_normal((T, d)) * 0.6).astype(np.float32) for d in (H * QK, HKV * QK, HKV * VD)]
+        ref.set_conv_taps(l, *ws)
+        mine.set_conv_taps(l, *ws)
+    worst = 0.0
+
+    def tokens(n):
+        nonlocal worst
+        for _ in range(n):
+            for l in range(L):
+                q = (rng.standard_normal(H * QK) * 0.5).astype(np.float32)
+                k = (rng.standard_normal(HKV * QK) * 0.5).astype(np.float32)
+                v = (rng.standard_normal(HKV * VD) * 0.5).astype(np.float32)
+                a, b = ref.step(l, q, k, v), mine.step(l, q, k, v)
+                worst = max(worst, float(np.max(np.abs(a - b) / np.maximum(1.0, np.abs(b)))))
+            ref.advance()
+            mine.advance()
+
+    tokens(40)
+    ref.snapshot()
+    mine.snapshot()
+    tokens(5)
+    ref.rewind()
+    mine.rewind()
+    tokens(3)
+    assert np.array_equal(ref.k, mine.k) and np.array_equal(ref.v, mine.v)
+    assert all(np.array_equal(a.view(np.uint32), b.view(np.uint32)) for a, b in zip(ref.hist, mine.hist))
+    assert worst <= 1e-5, worst
+    img, sink = ref.ref_prefix_image()
+    mine.snapshot()
+    assert sink == mine.n_sink and img == mine.prefix_image()
+
+
 def test_quantiser_edge_rows():
     """Zero rows (scale 1), ties at .5 after division, tiny and huge values."""
     H, HKV, QK, VD, W = 2, 2, 64, 64, 128
