@@ -357,6 +357,78 @@ def run_decode(args, world, rank, local, dist):
 
 
 # ------------------------------------------------------- GPU: head-sharded decode
+def run_decode_taps(args, world, rank, local, dist, plain_value):
+    """Config 2 with the reference model's 3-tap QKV short causal convolution
+    ahead of the path (random tap weights, seed 3000 + rank): same caches,
+    shapes and timing as the decode leg; reports tok/s and its cost against
+    the plain decode."""
+    import numpy as np
+    import torch
+
+    import ndattn
+
+    T = 3
+    K, Wm = args.steps, args.warmup
+    ctx = ctx_lengths(rank)
+    window = (CTX_HI + K + Wm + 2 + 63) // 64 * 64
+    a = ndattn.Attn(n_layers=LAYERS, n_heads=H, n_kv_heads=HKV, qk_head_dim=QK, v_head_dim=VD, window=window,
+                    max_seqs=BATCH, kv_dtype="f16", act_dtype="f16", out_dtype="f16", device=local, qkv_conv_taps=T)
+    wr = np.random.default_rng(3000 + rank)
+    for l in range(LAYERS):
+        a.set_conv_taps(l, *[(wr.standard_normal((T, d)) * 0.6).astype(np.float32)
+                             for d in (H * QK, HKV * QK, HKV * VD)])
+    stream = torch.cuda.ExternalStream(a.stream)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1000 + rank)
+    for l in range(LAYERS):
+        for s in range(BATCH):
+            n = int(ctx[s])
+            kk = (torch.randn((n, HKV * QK), generator=gen, device="cuda") * 0.5).half()
+            vv = (torch.randn((n, HKV * VD), generator=gen, device="cuda") * 0.5).half()
+            torch.cuda.synchronize()
+            a.write_cache(l, s, 0, n, kk, vv)
+    for s in range(BATCH):
+        a.set_state(s, int(ctx[s]), 0)
+    nsteps = K + Wm
+    q = torch.randn((nsteps, LAYERS, BATCH, H * QK), generator=gen, device="cuda").half()
+    k = (torch.randn((nsteps, LAYERS, BATCH, HKV * QK), generator=gen, device="cuda") * 0.5).half()
+    v = (torch.randn((nsteps, LAYERS, BATCH, HKV * VD), generator=gen, device="cuda") * 0.5).half()
+    out = torch.empty((LAYERS, BATCH, H * VD), dtype=torch.float16, device="cuda")
+
+    def step(i):
+        for l in range(LAYERS):
+            a.decode(l, BATCH, q[i, l], k[i, l], v[i, l], out[l])
+        a.advance(BATCH)
+
+    for i in range(Wm):
+        step(i)
+    a.sync()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = a.launches
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(K):
+        step(Wm + i)
+    t1.record(stream)
+    a.sync()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    launches = a.launches - launches0
+    a.close()
+    times = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms = float(times[0])
+    value = BATCH * world * K / (ms / 1e3)
+    return {"value": value, "unit": "tok/s", "ms_per_step": ms / K, "taps": T, "gpu_launches": int(launches),
+            "vs_plain_decode": value / plain_value,
+            "workload": "config 2 decode with 3 QKV conv taps (tap kernel + balanced attend per layer)"}
+
+
 def run_decode_heads(args, world, rank, local, dist):
     """Config 2 head-sharded over the ranks (strong scaling): every rank holds
     all 64 sequences (contexts of seed 1) for its H/world KV heads; per layer it
@@ -716,6 +788,7 @@ def run_ours(args):
                                   data="synthetic")), flush=True)
     else:
         dec = run_decode(args, world, rank, local, dist)
+        taps = run_decode_taps(args, world, rank, local, dist, dec["value"])
         heads = run_decode_heads(args, world, rank, local, dist) if world > 1 and HKV % world == 0 else None
         pre = run_prefill(args, world, rank, local, dist) if args.prefill_steps > 0 else None
         lng = run_long(args, world, rank, local, dist) if args.long_steps > 0 else None
@@ -742,9 +815,10 @@ def run_ours(args):
                                "parallelism": f"batch-sharded x{world} (no collective)"},
                     "roofline": dec["roofline"], "cpu_baseline": cpu, "e2e": dec["e2e"],
                     "gpu_launches": dec["gpu_launches"] + (pre["gpu_launches"] if pre else 0)
-                    + (lng["gpu_launches"] if lng else 0) + (srv["gpu_launches"] if srv else 0),
+                    + (lng["gpu_launches"] if lng else 0) + (srv["gpu_launches"] if srv else 0)
+                    + taps["gpu_launches"],
                     "clocks": dec["clocks"], "prefill": pre, "long_decode": lng, "serving": srv,
-                    "head_sharded": heads}
+                    "head_sharded": heads, "conv_taps": taps}
             print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

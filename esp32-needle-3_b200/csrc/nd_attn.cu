@@ -128,6 +128,10 @@ __global__ void __launch_bounds__(256) ingest_kernel(const IngestParams P) {
 // the call's own raw row for positions inside the span, else the sequence's
 // history. The raw rows of the span's last min(len, taps) positions then go
 // to history slot p % taps. Columns [0, qd) are q, then k, then v.
+// Launched with programmatic stream serialization: it releases its dependent
+// (the attend launch) at once and waits for the kernel before it before it
+// touches memory, so the attend launch of this layer may start under the
+// previous layer's tail, as it does without taps.
 constexpr uint32_t kTapMax = 4;
 struct TapParams {
     const void *x[3];           // raw q, k, v rows of the call
@@ -145,23 +149,26 @@ struct TapParams {
 
 __global__ void __launch_bounds__(128) tap_kernel(const TapParams P) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const uint32_t col = blockIdx.x * blockDim.x + threadIdx.x;
-    if (col >= P.cols) return;
-    const int which = col < P.dim[0] ? 0 : col < P.dim[0] + P.dim[1] ? 1 : 2;
-    const uint32_t D = P.dim[which];
-    const uint32_t c = col - (which > 0 ? P.dim[0] : 0u) - (which > 1 ? P.dim[1] : 0u);
-    const float *w = P.w + (which > 0 ? (size_t)P.taps * P.dim[0] : 0) + (which > 1 ? (size_t)P.taps * P.dim[1] : 0);
-    float wj[kTapMax];
-#pragma unroll
-    for (uint32_t j = 0; j < kTapMax; j++) wj[j] = j < P.taps ? w[(size_t)j * D + c] : 0.0f;
-    for (uint32_t sp = blockIdx.y; sp < P.n_spans; sp += gridDim.y) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // (span, column) pairs, columns fastest: a small grid (its blocks stay
+    // resident beside the attend CTAs while they wait) strides over them.
+    const uint64_t total = (uint64_t)P.n_spans * P.cols;
+    for (uint64_t it = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; it < total;
+         it += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t sp = (uint32_t)(it / P.cols), col = (uint32_t)(it % P.cols);
+        const int which = col < P.dim[0] ? 0 : col < P.dim[0] + P.dim[1] ? 1 : 2;
+        const uint32_t D = P.dim[which];
+        const uint32_t c = col - (which > 0 ? P.dim[0] : 0u) - (which > 1 ? P.dim[1] : 0u);
+        const float *w = P.w + (which > 0 ? (size_t)P.taps * P.dim[0] : 0) + (which > 1 ? (size_t)P.taps * P.dim[1] : 0);
         const nda::SeqSpan s = P.spans ? P.spans[sp] : nda::SeqSpan{sp, sp, 1u};
         const uint32_t p0 = P.state[s.seq].pos;
         float *hist = P.hist + (size_t)s.seq * P.hist_seq + P.hist_off[which];   // [taps][D]
-        float win[kTapMax];   // win[j] = x(p - 1 - j) before token p, x(p - j) after it
+        float wj[kTapMax], win[kTapMax];   // win[j] = x(p - 1 - j) before token p, x(p - j) after it
 #pragma unroll
-        for (uint32_t j = 0; j < kTapMax; j++)
+        for (uint32_t j = 0; j < kTapMax; j++) {
+            wj[j] = j < P.taps ? w[(size_t)j * D + c] : 0.0f;
             win[j] = j + 1 < P.taps && p0 >= j + 1 ? hist[(size_t)((p0 - 1 - j) % P.taps) * D + c] : 0.0f;
+        }
         for (uint32_t t = 0; t < s.len; t++) {
             const uint32_t p = p0 + t;
             const size_t xi = (size_t)(s.tok_base + t) * D + c;
@@ -507,10 +514,20 @@ int run_taps(nd_attn *h, uint32_t layer, uint32_t n_spans, const nda::SeqSpan *s
     P.state = h->d_state;
     P.n_spans = n_spans;
     P.act_dt = c.act_dtype;
-    note_writer(h, kNoLayer);
-    tap_kernel<<<dim3((P.cols + 127) / 128, std::min<uint32_t>(n_spans, 65535u)), 128, 0, h->stream>>>(P);
+    // No note_writer: the tap kernel writes no cache, but the kernel before it
+    // may still be running when the attend launch after it starts.
+    cudaLaunchConfig_t lc = {};
+    const uint64_t pairs = (uint64_t)n_spans * P.cols;
+    lc.gridDim = dim3((uint32_t)std::min<uint64_t>((pairs + 127) / 128, (uint64_t)h->sm_count * 2));
+    lc.blockDim = dim3(128);
+    lc.stream = h->stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    ND_CUDA(cudaLaunchKernelEx(&lc, tap_kernel, P));
     h->launches++;
-    ND_CUDA(cudaGetLastError());
     *q = P.y[0], *k = P.y[1], *v = P.y[2];
     return ND_ATTN_OK;
 }
