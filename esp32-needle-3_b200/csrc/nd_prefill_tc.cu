@@ -441,7 +441,9 @@ __global__ void __launch_bounds__(192, 2)
         // ---------------- softmax / correction / epilogue: thread = query row
         const uint32_t r = tid;
         const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
-        const float c = P.scale_log2;
+        // Softmax scale in log2 units; with f16 queries, times the power of two
+        // this row's Q was scaled down by (set per item in setup).
+        float c = P.scale_log2;
         bool ok = true, store_pending = false;
         uint32_t n_stores = 0;
 
@@ -487,11 +489,28 @@ __global__ void __launch_bounds__(192, 2)
                 const float2 rb = __ffma2_rn(b2, c2, __fmul2_rn(a2, s2));
                 x[i] = ra.x, x[i + 1] = ra.y, x[i + HD / 2] = rb.x, x[i + 1 + HD / 2] = rb.y;
             }
-            uint32_t hi[32], lo[32];
+            uint32_t hi[32];
+            if constexpr (BF16) {
+                uint32_t lo[32];
 #pragma unroll
-            for (int e = 0; e < 32; e++) split2<BF16>(x[2 * e], x[2 * e + 1], hi[e], lo[e]);
-            tmem_st32(lane_addr + COL_QHI, hi);
-            if constexpr (BF16) tmem_st32(lane_addr + COL_QLO, lo);
+                for (int e = 0; e < 32; e++) split2<true>(x[2 * e], x[2 * e + 1], hi[e], lo[e]);
+                tmem_st32(lane_addr + COL_QHI, hi);
+                tmem_st32(lane_addr + COL_QLO, lo);
+            } else {
+                // f16 queries: the row scaled by 2^-e so that its largest |q|
+                // stays below 2^15 (RoPE can push an f16 input past 65504);
+                // exact, a power of two. S comes out 2^-e too small and the
+                // row's scale c takes 2^e.
+                float amax = 0.0f;
+#pragma unroll
+                for (int i = 0; i < HD; i++) amax = fmaxf(amax, fabsf(x[i]));
+                const int e = max(0, (int)((__float_as_uint(amax) >> 23) & 0xffu) - 127 - 14);
+                const float down = __uint_as_float((uint32_t)(127 - min(e, 126)) << 23);
+#pragma unroll
+                for (int i = 0; i < 32; i++) hi[i] = pack2<false>(x[2 * i] * down, x[2 * i + 1] * down);
+                c = P.scale_log2 * __uint_as_float((uint32_t)(127 + min(e, 127)) << 23);
+                tmem_st32(lane_addr + COL_QHI, hi);
+            }
             tmem_wait_st();
             fence_before();
             __syncwarp();

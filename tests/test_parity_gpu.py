@@ -564,11 +564,13 @@ def test_tensor_core_prefill_16bit_out(dt, gate):
     a.close()
 
 
-def test_tensor_core_prefill_bf16_v_beyond_f16():
-    """bf16 V values that f16 cannot represent (2^17 here) take the hi/lo
-    variant: the append that stores one sets the layer's flag on the device,
-    and both that call's prefill and later calls over the cached row stay
-    within the bar (the f16-PV variant would turn the value into Inf)."""
+@pytest.mark.parametrize("which", ["k", "v"])
+def test_tensor_core_prefill_bf16_kv_beyond_f16(which):
+    """bf16 values that f16 cannot represent (2^17 here). In V they take the
+    hi/lo variant: the append that stores one sets the layer's flag on the
+    device (the f16-PV variant would turn the value into Inf). K stays bf16 in
+    both variants. That call's prefill and later calls over the cached row
+    stay within the bar."""
     import torch
     rng = np.random.default_rng(43)
     H, HKV, D, W = 8, 2, 64, 512
@@ -581,7 +583,7 @@ def test_tensor_core_prefill_bf16_v_beyond_f16():
         k = (rng.standard_normal((n, HKV * D)) * 0.5).astype(np.float32)
         v = (rng.standard_normal((n, HKV * D)) * 0.5).astype(np.float32)
         if call == 0:
-            v[57, 1 * D + 3] = 2.0 ** 17
+            (k if which == "k" else v)[57, 1 * D + 3] = 2.0 ** 17
         out = torch.zeros((n, H * D), dtype=torch.float32, device="cuda")
         a.prefill(0, [n], dev(q, O.BF16), dev(k, O.BF16), dev(v, O.BF16), out)
         a.sync()
@@ -592,5 +594,38 @@ def test_tensor_core_prefill_bf16_v_beyond_f16():
             worst = max(worst, rel_err(got[t].reshape(H, D), want))
         a.advance(1, lens=[n])
         seq.advance(n)
+    assert worst <= TOL
+    a.close()
+
+
+@pytest.mark.parametrize("dt", [O.F16, O.BF16])
+def test_tensor_core_prefill_large_queries_stay_finite(dt):
+    """Query rows of very large magnitude (|q| ~ 2^17 in bf16; ~6e4 in f16,
+    whose rotation can exceed 65504, so f16 queries go into TMEM scaled by a
+    power of two per row) give finite outputs. 16-bit queries that large
+    cannot meet the 1e-3 bar in any form, so only the ordinary rows are held
+    to it."""
+    import torch
+    rng = np.random.default_rng(47)
+    H, HKV, D, W, n = 8, 2, 64, 256, 160
+    a = ndattn.Attn(n_layers=1, n_heads=H, n_kv_heads=HKV, qk_head_dim=D, v_head_dim=D, window=W, max_seqs=1,
+                    kv_dtype=dt, act_dtype=dt, out_dtype="f32", max_pos=W)
+    seq = O.OracleSeq(1, H, HKV, D, D, W, dt, max_pos=W)
+    q = (rng.standard_normal((n, H * D)) * 0.5).astype(np.float32)
+    k = (rng.standard_normal((n, HKV * D)) * 0.5).astype(np.float32)
+    v = (rng.standard_normal((n, HKV * D)) * 0.5).astype(np.float32)
+    big_rows = [3, 64, 131]
+    for t in big_rows:
+        q[t] = np.sign(q[t]) * (2.0 ** 17 if dt == O.BF16 else 60000.0)
+    out = torch.zeros((n, H * D), dtype=torch.float32, device="cuda")
+    a.prefill(0, [n], dev(q, dt), dev(k, dt), dev(v, dt), out)
+    a.sync()
+    got = out.cpu().numpy()
+    assert np.all(np.isfinite(got))
+    worst = 0.0
+    for t in range(n):
+        want = seq.step(0, O.round_act(q[t], dt), O.round_act(k[t], dt), O.round_act(v[t], dt), off=t)
+        if t not in big_rows:
+            worst = max(worst, rel_err(got[t].reshape(H, D), want))
     assert worst <= TOL
     a.close()
