@@ -12,7 +12,8 @@ One session per cache type walks every place the tap history matters:
   byte for byte) restored into another sequence;
 - a reset (history cleared), then more tokens.
 int8 runs the general kernels, f16 / bf16 at head dim 64 the tensor-core
-prefill and the balanced decode. Outputs within TOL, caches bit-exact."""
+prefill and the balanced decode, over MHA and query groups of two and four
+rows. Outputs within TOL, caches bit-exact."""
 import numpy as np
 import pytest
 
@@ -25,11 +26,12 @@ pytestmark = pytest.mark.gpu
 NAMES = {O.F32: "f32", O.F16: "f16", O.BF16: "bf16", O.I8: "i8"}
 
 
-@pytest.mark.parametrize("kv_dt,act_dt", [(O.I8, O.F32), (O.F16, O.F16), (O.BF16, O.BF16)])
-def test_conv_taps_session(kv_dt, act_dt):
+@pytest.mark.parametrize("kv_dt,act_dt,H,HKV", [(O.I8, O.F32, 8, 2), (O.F16, O.F16, 8, 2), (O.BF16, O.BF16, 8, 2),
+                                                 (O.F16, O.F16, 4, 4), (O.BF16, O.BF16, 8, 4)])
+def test_conv_taps_session(kv_dt, act_dt, H, HKV):
     import torch
-    rng = np.random.default_rng(23 + kv_dt)
-    L, H, HKV, HD, W, B, T = 2, 8, 2, 64, 256, 3, 3
+    rng = np.random.default_rng(23 + kv_dt + H * HKV)
+    L, HD, W, B, T = 2, 64, 256, 3, 3
     a = ndattn.Attn(n_layers=L, n_heads=H, n_kv_heads=HKV, window=W, max_seqs=B, kv_dtype=NAMES[kv_dt],
                     act_dtype=NAMES[act_dt], out_dtype="f32", qkv_conv_taps=T)
     seqs = [O.OracleSeq(L, H, HKV, HD, HD, W, kv_dt, taps=T, act_dtype=act_dt) for _ in range(B)]
