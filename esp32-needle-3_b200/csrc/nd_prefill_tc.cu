@@ -117,8 +117,8 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
 #define ND_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
 #define ND_W8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), "r"(r[i + 5]), "r"(r[i + 6]), "r"(r[i + 7])
 
-// 32 consecutive 32-bit TMEM columns of this thread's lane; tmem_ld32 waits,
-// tmem_ld32_async leaves the wait to tmem_wait_ld() so loads can overlap.
+// 32 consecutive 32-bit TMEM columns of this thread's lane; the wait is left
+// to tmem_wait_ld() so that several loads can be in flight at once.
 __device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t *r) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -127,10 +127,6 @@ __device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t *r) {
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    tmem_ld32_async(taddr, r);
-    tmem_wait_ld();
-}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -147,6 +143,15 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// 16 consecutive 32-bit TMEM columns of this thread's lane (waits).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    tmem_wait_ld();
+}
 #undef ND_R8
 #undef ND_W8
 
@@ -543,14 +548,18 @@ __global__ void __launch_bounds__(192, 2)
                 fence_after();
                 const int lim = (int)qpos - (int)(j * BN);   // keys [0, lim] of this tile are visible
                 const bool masked = !__all_sync(0xffffffffu, lim >= BN - 1);   // tile crosses the warp's diagonal
-                // Pass 1: the tile's row max (8 independent chains per 32 columns).
+                // Pass 1: the tile's row max (8 independent chains per 32 columns),
+                // both 32-column loads in flight before one wait.
                 float mx[8];
 #pragma unroll
                 for (int kq = 0; kq < 8; kq++) mx[kq] = -INFINITY;
+                uint32_t sv2[BN / 32][32];
+#pragma unroll
+                for (int c2 = 0; c2 < BN / 32; c2++) tmem_ld32_async(sbuf + 32 * c2, sv2[c2]);
+                tmem_wait_ld();
 #pragma unroll
                 for (int c2 = 0; c2 < BN / 32; c2++) {
-                    uint32_t sv[32];
-                    tmem_ld32(sbuf + 32 * c2, sv);
+                    uint32_t(&sv)[32] = sv2[c2];
                     if (masked) {
 #pragma unroll
                         for (int e = 0; e < 32; e++)
@@ -578,28 +587,21 @@ __global__ void __launch_bounds__(192, 2)
                     fence_after();
                     const float alpha = grow ? ex2(m - tmax) : 1.0f;
                     l2 = __fmul2_rn(l2, make_float2(alpha, alpha));
-                    uint32_t ov[32];
+                    // 16 columns at a time: this tile's 64 S values stay live.
+                    uint32_t ov[16];
 #pragma unroll
-                    for (int h2 = 0; h2 < HD / 32; h2++) {
-                        tmem_ld32(lane_addr + COL_O + h2 * 32, ov);
+                    for (int h2 = 0; h2 < HD / 16; h2++) {
+                        tmem_ld16(lane_addr + COL_O + h2 * 16, ov);
 #pragma unroll
-                        for (int e = 0; e < 32; e++) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-                        tmem_st32(lane_addr + COL_O + h2 * 32, ov);
+                        for (int e = 0; e < 16; e++) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+                        tmem_st16(lane_addr + COL_O + h2 * 16, ov);
                     }
                 }
                 if (grow) m = tmax;
-                // Pass 2: P = 2^(S*c - m) over the S columns.
+                // Pass 2: P = 2^(S*c - m) over the S columns, from the values
+                // pass 1 loaded (masked already).
 #pragma unroll
-                for (int c2 = 0; c2 < BN / 32; c2++) {
-                    uint32_t sv[32];
-                    tmem_ld32(sbuf + 32 * c2, sv);
-                    if (masked) {
-#pragma unroll
-                        for (int e = 0; e < 32; e++)
-                            if (c2 * 32 + e > lim) sv[e] = 0xff800000u;
-                    }
-                    write_p_chunk<PSPLIT>(sv, sbuf + 32 * c2, c, m, l2);
-                }
+                for (int c2 = 0; c2 < BN / 32; c2++) write_p_chunk<PSPLIT>(sv2[c2], sbuf + 32 * c2, c, m, l2);
                 if constexpr (BF16 && PVF16) {
                     // V tile of this stage to f16 in place (exact: the layer's
                     // V holds no value f16 cannot represent), a quarter per warp.
