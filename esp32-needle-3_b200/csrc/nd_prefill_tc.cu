@@ -185,30 +185,9 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t 
     lo = pack2<BF16>(a - h.x, b - h.y);
 }
 
-// 2^t for a pair on the FMA pipe, to take load off the MUFU unit (which the
-// softmax warps otherwise saturate): t = n + f with n = RN(t) (the 1.5 * 2^23
-// addition leaves n in the low mantissa bits), 2^f on [-1/2, 1/2] by a cubic
-// fitted to 2^f by least squares on the relative error at Chebyshev nodes
-// (max relative error 7.7e-5 in float32, below f16's own 4.9e-4 rounding of
-// P), then n added to the exponent field. t is clamped at -125 first, so the
-// exponent stays in range (masked scores, t = -inf, give 2^-125 ~ 0).
-__device__ __forceinline__ float2 exp2_poly2(float2 t) {
-    t = make_float2(fmaxf(t.x, -125.0f), fmaxf(t.y, -125.0f));
-    const float2 magic = make_float2(12582912.0f, 12582912.0f);
-    const float2 y = __fadd2_rn(t, magic);
-    const float2 f = __fadd2_rn(t, __fadd2_rn(magic, make_float2(-y.x, -y.y)));
-    float2 p = __ffma2_rn(make_float2(0.05508868396282196f, 0.05508868396282196f), f,
-                          make_float2(0.24260404706001282f, 0.24260404706001282f));
-    p = __ffma2_rn(p, f, make_float2(0.6932762265205383f, 0.6932762265205383f));
-    p = __ffma2_rn(p, f, make_float2(0.9999289512634277f, 0.9999289512634277f));
-    return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(y.x) << 23)),
-                       __int_as_float(__float_as_int(p.y) + (__float_as_int(y.y) << 23)));
-}
-
 // P = 2^(S*c - m) for 32 keys of a row, written over their S columns: with
 // PSPLIT as hi/lo bf16 pairs (16 columns of hi, then 16 of lo), else as single
-// f16 pairs (16 columns; one pair in four through exp2_poly2). The row sum
-// goes into l2.
+// f16 pairs (16 columns). The row sum goes into l2.
 template <bool PSPLIT>
 __device__ __forceinline__ void write_p_chunk(const uint32_t (&sv)[32], uint32_t taddr, float c, float m, float2 &l2) {
     const float2 c2v = make_float2(c, c), nm2 = make_float2(-m, -m), neg1 = make_float2(-1.0f, -1.0f);
@@ -218,13 +197,7 @@ __device__ __forceinline__ void write_p_chunk(const uint32_t (&sv)[32], uint32_t
     for (int e = 0; e < 32; e += 2) {
         const float2 sp = make_float2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
         const float2 t = __ffma2_rn(sp, c2v, nm2);
-        float2 pp;
-        if constexpr (!PSPLIT) {
-            if ((e / 2) % 4 == 3) pp = exp2_poly2(t);
-            else pp = make_float2(ex2(t.x), ex2(t.y));
-        } else {
-            pp = make_float2(ex2(t.x), ex2(t.y));
-        }
+        const float2 pp = make_float2(ex2(t.x), ex2(t.y));
         acc[(e >> 1) & 1] = __fadd2_rn(acc[(e >> 1) & 1], pp);
         if constexpr (PSPLIT) {
             // hi = the upper halves (truncated bf16), lo = RN(p - hi): p - hi is
