@@ -30,7 +30,6 @@ import json
 import os
 import statistics
 import sys
-import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -51,7 +50,7 @@ P_METRIC = "prefill tok/s (config 3: 512 seq x 1024 tok x 8 layers, GQA 16/4, hd
 # here), the prefill launch on 64 sequences scaled by 8 to 512 (traffic grows
 # with the sequences processed).
 DECODE_TRAFFIC = (157.5e6 + 3.9e6)
-PREFILL_TRAFFIC = (311.9e6 + 100.3e6) * 8
+PREFILL_TRAFFIC = (309.5e6 + 100.4e6) * 8
 # config 4 (long-context paged decode)
 L_SEQS, L_CTX, L_H, L_HD, L_BLOCK, L_STEPS = 256, 32768, 8, 128, 64, 64
 L_METRIC = ("decode tok/s (config 4: B=256/GPU x 32768 cached, 8x128 MHA, fp16 KV, 64-slot pages in a "
@@ -73,66 +72,100 @@ def ctx_lengths(rank: int):
     return rng.integers(CTX_LO, CTX_HI + 1, size=BATCH)
 
 
+def _clock_poll(uuid, dev, conn, stop):
+    """Sampler process of Clocks: SM clock and clock-event reasons through NVML
+    about every millisecond until `stop` is set, then the samples go back
+    through `conn`. A process of its own, so that the bench's Python thread,
+    busy enqueuing launches, cannot starve it."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        h = None
+        if uuid:
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                hh = pynvml.nvmlDeviceGetHandleByIndex(i)
+                u = pynvml.nvmlDeviceGetUUID(hh)
+                u = u.decode() if isinstance(u, bytes) else u
+                if u.replace("GPU-", "") == uuid.replace("GPU-", ""):
+                    h = hh
+        h = h or pynvml.nvmlDeviceGetHandleByIndex(dev)
+        get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)   # first queries are slow: before the region
+        get_reasons(h)
+        conn.send(("ready", mx))
+    except Exception as e:
+        conn.send(("fail", str(e)))
+        return
+    rows = []
+    while not stop.is_set():
+        try:
+            rows.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), get_reasons(h)))
+        except Exception:
+            pass
+        time.sleep(0.001)
+    conn.send(("rows", rows))
+
+
 class Clocks:
-    """Samples SM clocks and throttle reasons through NVML every ~2 ms while
-    the timed region runs (nvidia-smi's 100 ms period is longer than a short
-    timed region)."""
+    """Samples SM clocks and clock-event (throttle) reasons through NVML about
+    every millisecond while the timed region runs (nvidia-smi's 100 ms period
+    is longer than a short timed region), from a spawned process (the bench
+    process has CUDA initialised, so it is not forked)."""
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
                "sw_power_cap": 0x4}
 
     def __init__(self, dev: int):
-        self.dev, self.rows, self.stop, self.t = dev, [], False, None
+        self.dev, self.rows, self.p = dev, [], None
 
     def __enter__(self):
         try:
-            import pynvml
-            pynvml.nvmlInit()
+            import multiprocessing as mp
             uuid = None
             try:
                 import torch
                 uuid = str(torch.cuda.get_device_properties(self.dev).uuid)
             except Exception:
                 pass
-            h = None
-            if uuid:
-                for i in range(pynvml.nvmlDeviceGetCount()):
-                    hh = pynvml.nvmlDeviceGetHandleByIndex(i)
-                    u = pynvml.nvmlDeviceGetUUID(hh)
-                    u = u.decode() if isinstance(u, bytes) else u
-                    if u.replace("GPU-", "") == uuid.replace("GPU-", ""):
-                        h = hh
-            self.h = h or pynvml.nvmlDeviceGetHandleByIndex(self.dev)
-            self.nv = pynvml
-            self.max = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
-            self.t = threading.Thread(target=self._poll, daemon=True)
-            self.t.start()
+            ctx = mp.get_context("spawn")
+            self.conn, child = ctx.Pipe()
+            self.stop = ctx.Event()
+            self.p = ctx.Process(target=_clock_poll, args=(uuid, self.dev, child, self.stop), daemon=True)
+            self.p.start()
+            if not self.conn.poll(60):
+                raise RuntimeError("clock sampler did not start")
+            kind, val = self.conn.recv()
+            if kind != "ready":
+                raise RuntimeError(val)
+            self.max = val
         except Exception:
-            self.t = None
+            self._end()
         return self
 
-    def _poll(self):
-        nv = self.nv
-        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-            nv.nvmlDeviceGetCurrentClocksThrottleReasons
-        while not self.stop:
-            try:
-                self.rows.append((nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM), get_reasons(self.h)))
-            except Exception:
-                pass
-            time.sleep(0.002)
+    def _end(self):
+        if self.p is not None:
+            self.p.join(timeout=5)
+            if self.p.is_alive():
+                self.p.kill()
+            self.p = None
 
     def __exit__(self, *exc):
-        self.stop = True
-        if self.t:
-            self.t.join(timeout=2)
+        if self.p is not None:
+            self.stop.set()
+            if self.conn.poll(10):
+                kind, val = self.conn.recv()
+                if kind == "rows":
+                    self.rows = val
+        self._end()
 
     def summary(self):
         sm = [r[0] for r in self.rows]
         reasons = sorted({n for _, m in self.rows for n, bit in self.REASONS.items() if m & bit})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": getattr(self, "max", None), "reasons": reasons, "samples": len(sm),
-                "source": "nvml, ~2 ms period, during the timed region"}
+                "source": "nvml, ~1 ms period, sampler process, during the timed region"}
 
 
 # ------------------------------------------------------------ CPU reference
@@ -827,7 +860,7 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
