@@ -276,6 +276,7 @@ struct nd_attn {
     std::vector<uint32_t> lean_key, lean_key_next;
     uint64_t lean_nt = 0, lean_g = 0, lean_s = 0, lean_ch = 0, lean_nu = 0;
     std::vector<CUtensorMap> lean_kmap, lean_vmap;   // per layer, built on first use
+    std::vector<CUtensorMap> lean_ksmap, lean_vsmap; // int8: the layer's scale maps
     std::vector<uint8_t> lean_map_ok;
     uint32_t lean_parity = 0;          // half of counters / partials the next balanced launch uses
     // Cache rows our most recently launched kernel may write: kNoLayer (none),
@@ -472,6 +473,8 @@ int upload_tok(nd_attn *h, const std::vector<TokMeta> &tok) {
 
 int make_map(CUtensorMap *m, bool bf16, const void *base, uint64_t inner, uint64_t rows, uint64_t stride_bytes,
              uint32_t box_rows, uint32_t box_inner, bool swizzle);
+int make_map_dt(CUtensorMap *m, int dt, const void *base, uint64_t inner, uint64_t rows, uint64_t stride_bytes,
+                uint32_t box_rows, uint32_t box_inner, bool swizzle);
 
 // History block offsets of `layer` inside a sequence's [q | k | v] history.
 void tap_offsets(const nd_attn *h, uint32_t layer, size_t off[3]) {
@@ -532,13 +535,18 @@ int run_taps(nd_attn *h, uint32_t layer, uint32_t n_spans, const nda::SeqSpan *s
     return ND_ATTN_OK;
 }
 
-// The balanced TMA-staged attend covers 16-bit caches with equal head dims of
-// 64 or 128 (GQA width <= 4 at 128), calls in which no position wraps the
-// ring, and pages (if any) holding whole 64-row boxes.
+// The balanced TMA-staged attend covers 16-bit caches, and int8 caches whose
+// scale rows ([n_kv] floats) are a multiple of 16 bytes (n_kv % 4 == 0: the
+// scales come in as TMA boxes too) with query groups of at most two rows,
+// with equal head dims of 64 or 128 (GQA
+// width <= 4 at 128), calls in which no position wraps the ring, and pages
+// (if any) holding whole 64-row boxes.
 bool lean_ok(const nd_attn *h, bool no_wrap) {
     const nd_attn_config &cf = h->cfg;
     const int nq = nda::nq_for_rep(h->rep);
-    return no_wrap && (cf.kv_dtype == ND_DT_F16 || cf.kv_dtype == ND_DT_BF16) && cf.qk_head_dim == cf.v_head_dim &&
+    const bool dt_ok = cf.kv_dtype == ND_DT_F16 || cf.kv_dtype == ND_DT_BF16 ||
+                       (cf.kv_dtype == ND_DT_I8 && cf.n_kv_heads % 4 == 0 && nq <= 2);
+    return no_wrap && dt_ok && cf.qk_head_dim == cf.v_head_dim &&
            (cf.qk_head_dim == 64 || (cf.qk_head_dim == 128 && nq <= 4)) &&
            (cf.block_size == 0 || cf.block_size % (uint32_t)nda::kTmaRows == 0) && h->rows_per_layer < 0x7fffffffu;
 }
@@ -615,16 +623,18 @@ int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, co
     const nd_attn_config &cf = h->cfg;
     const uint32_t hd = cf.qk_head_dim;
     const int nq = nda::nq_for_rep(h->rep);
-    const bool bf16 = cf.kv_dtype == ND_DT_BF16;
-    auto launch = [&](const void *km, const void *vm, const nda::AttnParams &P, int *occ) {
-        return bf16 ? nda::attend_lean_launch_bf16((int)hd, nq, km, vm, P, occ, h->stream)
-                    : nda::attend_lean_launch_f16((int)hd, nq, km, vm, P, occ, h->stream);
+    const bool bf16 = cf.kv_dtype == ND_DT_BF16, i8 = cf.kv_dtype == ND_DT_I8;
+    auto launch = [&](const void *km, const void *vm, const void *ksm, const void *vsm, const nda::AttnParams &P,
+                      int *occ) {
+        return i8     ? nda::attend_lean_launch_i8((int)hd, nq, km, vm, ksm, vsm, P, occ, h->stream)
+               : bf16 ? nda::attend_lean_launch_bf16((int)hd, nq, km, vm, ksm, vsm, P, occ, h->stream)
+                      : nda::attend_lean_launch_f16((int)hd, nq, km, vm, ksm, vsm, P, occ, h->stream);
     };
     int &occ = h->lean_occ[(bf16 ? 4 : 0) + (nq == 1 ? 0 : nq == 2 ? 1 : nq == 4 ? 2 : 3)];
     AttnParams P = base_params(h, layer);
     if (occ <= 0) {
         int b = 0;
-        ND_CUDA(launch(nullptr, nullptr, P, &b));
+        ND_CUDA(launch(nullptr, nullptr, nullptr, nullptr, P, &b));
         if (b <= 0) return fail(ND_ATTN_ERR_CUDA, "balanced attend kernel does not fit on an SM");
         occ = b;
     }
@@ -671,18 +681,29 @@ int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, co
     if (h->lean_map_ok.size() != cf.n_layers) {
         h->lean_kmap.resize(cf.n_layers);
         h->lean_vmap.resize(cf.n_layers);
+        h->lean_ksmap.resize(cf.n_layers);
+        h->lean_vsmap.resize(cf.n_layers);
         h->lean_map_ok.assign(cf.n_layers, 0);
     }
     if (!h->lean_map_ok[layer]) {   // the layer's cache never moves: encode its maps once
-        int rc = make_map(&h->lean_kmap[layer], bf16, P.c.k, h->k_dim, h->rows_per_layer, (uint64_t)h->k_dim * 2,
-                          nda::kTmaRows, hd, false);
-        if (!rc) rc = make_map(&h->lean_vmap[layer], bf16, P.c.v, h->v_dim, h->rows_per_layer,
-                               (uint64_t)h->v_dim * 2, nda::kTmaRows, hd, false);
+        // Rows of [n_kv][hd] elements, box {hd, 64} at x = g * hd; int8 scales
+        // [n_kv] f32 per row, box {4, 64} at x = g rounded down to 4 (16 bytes).
+        const size_t es = h->kes;
+        int rc = make_map_dt(&h->lean_kmap[layer], cf.kv_dtype, P.c.k, h->k_dim, h->rows_per_layer,
+                             (uint64_t)h->k_dim * es, nda::kTmaRows, hd, false);
+        if (!rc) rc = make_map_dt(&h->lean_vmap[layer], cf.kv_dtype, P.c.v, h->v_dim, h->rows_per_layer,
+                                  (uint64_t)h->v_dim * es, nda::kTmaRows, hd, false);
+        if (!rc && i8) rc = make_map_dt(&h->lean_ksmap[layer], ND_DT_F32, P.c.ks, cf.n_kv_heads, h->rows_per_layer,
+                                        (uint64_t)cf.n_kv_heads * 4, nda::kTmaRows, 4, false);
+        if (!rc && i8) rc = make_map_dt(&h->lean_vsmap[layer], ND_DT_F32, P.c.vs, cf.n_kv_heads, h->rows_per_layer,
+                                        (uint64_t)cf.n_kv_heads * 4, nda::kTmaRows, 4, false);
         if (rc) return rc;
+        if (!i8) h->lean_ksmap[layer] = h->lean_kmap[layer], h->lean_vsmap[layer] = h->lean_vmap[layer];  // unused
         h->lean_map_ok[layer] = 1;
     }
     note_writer(h, fuse_append ? (int)layer : kNoLayer);
-    ND_CUDA(launch(&h->lean_kmap[layer], &h->lean_vmap[layer], P, nullptr));
+    ND_CUDA(launch(&h->lean_kmap[layer], &h->lean_vmap[layer], &h->lean_ksmap[layer], &h->lean_vsmap[layer], P,
+                   nullptr));
     h->launches++;
     return ND_ATTN_OK;
 }
@@ -794,6 +815,7 @@ int make_map_dt(CUtensorMap *m, int dt, const void *base, uint64_t inner, uint64
     const cuuint32_t estr[2] = {1, 1};
     const CUtensorMapDataType t = dt == ND_DT_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                   : dt == ND_DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                  : dt == ND_DT_I8  ? CU_TENSOR_MAP_DATA_TYPE_UINT8
                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     const CUresult r = fn(m, t, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                           swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,

@@ -59,12 +59,19 @@ constexpr int kTmaRows = 64;   // rows per TMA box / tile
 constexpr int kLeanAheadMax = 4;
 
 template <int HD, typename KVT, int NQ> struct LeanCfg {
+    static constexpr bool I8 = KvT<KVT>::dt == DT_I8;
     static constexpr int NW = 4;                                     // consumer warps
-    static constexpr int STAGES = HD == 64 ? ND_LEAN_STAGES64 : (NQ >= 4 ? 2 : 3);  // tile ring depth
+    // Tile ring depth: int8 tiles are half the bytes, so more of them.
+    static constexpr int STAGES = I8 ? (HD == 64 ? 6 : 4) : HD == 64 ? ND_LEAN_STAGES64 : (NQ >= 4 ? 2 : 3);
     static constexpr int SQ = NQ * HD >= 256 ? 2 : 4;                // segment slot ring depth
     static constexpr uint32_t TILE = kTmaRows * HD * sizeof(KVT);
+    // int8: per stage the K and V scales of the tile's rows for four KV heads
+    // (a {4, 64} f32 box: TMA moves at least 16 bytes per row).
+    static constexpr uint32_t SC = I8 ? kTmaRows * 16 : 0;
     static constexpr uint32_t OFF_V = STAGES * TILE;
-    static constexpr uint32_t OFF_Q = 2 * STAGES * TILE;                        // [SQ][NQ][HD] f32
+    static constexpr uint32_t OFF_KS = 2 * STAGES * TILE;                       // [STAGES][64][4] f32
+    static constexpr uint32_t OFF_VS = OFF_KS + STAGES * SC;
+    static constexpr uint32_t OFF_Q = OFF_KS + 2 * STAGES * SC;                 // [SQ][NQ][HD] f32
     static constexpr uint32_t OFF_MO = OFF_Q + SQ * NQ * HD * 4;                // [SQ][NW][NQ][HD] f32
     static constexpr uint32_t OFF_ML = OFF_MO + SQ * NW * NQ * HD * 4;          // [SQ][NW][NQ][2] f32
     static constexpr uint32_t SMEM = OFF_ML + SQ * NW * NQ * 2 * 4;
@@ -188,6 +195,8 @@ struct LeanInfo {   // the same segment, completed by the prep warp
 template <int HD, typename KVT, int NQ>
 __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant__ CUtensorMap kmap,
                                                           const __grid_constant__ CUtensorMap vmap,
+                                                          const __grid_constant__ CUtensorMap ksmap,
+                                                          const __grid_constant__ CUtensorMap vsmap,
                                                           const AttnParams P) {
     using C = LeanCfg<HD, KVT, NQ>;
     using S = AttendShape<HD, HD, KVT, NQ>;
@@ -195,7 +204,7 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
     constexpr int PRODUCER = NW, PREP = NW + 1, FINISH = NW + 2;
     constexpr int LPR = S::LPR, RPW = S::RPW, EK = S::EK, EV = S::EV, WK = S::WK, WV = S::WV, ES = S::ES;
     constexpr int RW = TR / NW;              // rows per warp per tile
-    constexpr int UB = 4;                    // row groups per consume call
+    constexpr int UB = RW / RPW < 4 ? RW / RPW : 4;   // row groups per consume call
     constexpr int NCALL = RW / (RPW * UB);   // consume calls per tile
     static_assert(RW % (RPW * UB) == 0, "tile rows split evenly");
     constexpr uint32_t TILE_BYTES = C::TILE;
@@ -287,9 +296,13 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                         const uint32_t s2 = tc % STAGES;
                         if (tc == STAGES && !grabbed) ND_LEAN_GRAB_AHEAD();
                         if (tc >= STAGES && !mbar_wait(&empty[s2], ((tc / STAGES) - 1) & 1, abort_flag)) break;
-                        mbar_expect_tx(&full[s2], 2 * TILE_BYTES);
+                        mbar_expect_tx(&full[s2], 2 * TILE_BYTES + 2 * C::SC);
                         tma_load_2d(smem + s2 * TILE_BYTES, &kmap, (int)(w.g * HD), y, &full[s2]);
                         tma_load_2d(smem + C::OFF_V + s2 * TILE_BYTES, &vmap, (int)(w.g * HD), y, &full[s2]);
+                        if constexpr (C::I8) {   // x = the KV head rounded down to a multiple of 4 (16 bytes)
+                            tma_load_2d(smem + C::OFF_KS + s2 * C::SC, &ksmap, (int)(w.g & ~3u), y, &full[s2]);
+                            tma_load_2d(smem + C::OFF_VS + s2 * C::SC, &vsmap, (int)(w.g & ~3u), y, &full[s2]);
+                        }
                     }
                     x += nt;
                     w.advance(P, nt);
@@ -498,7 +511,9 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
 
     // ---------------- consumers (warps 0..NW-1)
     const int sub = lane % LPR, rl = lane / LPR;
-    const float zero_sc[UB] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float zero_sc[UB];
+#pragma unroll
+    for (int u = 0; u < UB; u++) zero_sc[u] = 0.0f;
     uint32_t tc = 0;
     for (uint32_t seg = 0;; seg++) {
         const uint32_t i = seg % SQ, par = (seg / SQ) & 1;
@@ -544,7 +559,23 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
 #pragma unroll
                     for (int k3 = 0; k3 < WV; k3++) vw[u][k3] = valid[u] ? vp[k3] : 0u;   // 0 * (Inf|NaN) guard
                 }
-                consume<HD, HD, KVT, NQ, UB>(qr, kw, vw, zero_sc, zero_sc, valid, m, l, acc);
+                if constexpr (C::I8) {
+                    // The rows' scales (column g & 3 of the stage's {4, 64} box);
+                    // a row past the item's end gets scale 0, so stale or NaN
+                    // scale bits contribute nothing.
+                    const float *ks = reinterpret_cast<const float *>(smem + C::OFF_KS + s2 * C::SC);
+                    const float *vs = reinterpret_cast<const float *>(smem + C::OFF_VS + s2 * C::SC);
+                    float ksc[UB], vsc[UB];
+#pragma unroll
+                    for (int u = 0; u < UB; u++) {
+                        const int r = warp * RW + (cI * UB + u) * RPW + rl;
+                        ksc[u] = valid[u] ? ks[r * 4 + (d.g & 3u)] : 0.0f;
+                        vsc[u] = valid[u] ? vs[r * 4 + (d.g & 3u)] : 0.0f;
+                    }
+                    consume<HD, HD, KVT, NQ, UB>(qr, kw, vw, ksc, vsc, valid, m, l, acc);
+                } else {
+                    consume<HD, HD, KVT, NQ, UB>(qr, kw, vw, zero_sc, zero_sc, valid, m, l, acc);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s2]);
@@ -557,11 +588,15 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
             const char *vb = static_cast<const char *>(P.c.v) + ((size_t)d.g * HD + (size_t)sub * EV) * ES;
             const size_t row = phys_row(P.c, si.seq, si.pos);
             uint32_t kw[1][WK], vw[1][WV];
-            const float sc1[1] = {0.0f};
+            float ksc1[1] = {0.0f}, vsc1[1] = {0.0f};
+            if constexpr (C::I8) {   // its scales, written by the same launch: coherent loads too
+                ksc1[0] = *reinterpret_cast<const volatile float *>(P.c.ks + row * P.c.n_kv + d.g);
+                vsc1[0] = *reinterpret_cast<const volatile float *>(P.c.vs + row * P.c.n_kv + d.g);
+            }
             const bool valid[1] = {rl == 0};
             load_words<WK, false>(kb + row * (size_t)P.c.k_dim * ES, kw[0]);
             load_words<WV, false>(vb + row * (size_t)P.c.v_dim * ES, vw[0]);
-            consume<HD, HD, KVT, NQ, 1>(qr, kw, vw, sc1, sc1, valid, m, l, acc);
+            consume<HD, HD, KVT, NQ, 1>(qr, kw, vw, ksc1, vsc1, valid, m, l, acc);
         }
         // Reduce across the row lanes; hand (m, l, acc) of this warp over.
 #pragma unroll

@@ -58,11 +58,12 @@ cudaError_t append_launch_t(int qk, int vd, const AttnParams &P, cudaStream_t s)
 // kernel itself waits where it depends on it). With blocks_per_sm set, only
 // raises the kernel's dynamic shared memory limit and reports how many CTAs of
 // the instantiation one SM holds (no launch); the host asks once per handle
-// and instantiation before the first launch.
+// and instantiation before the first launch. ksmap / vsmap: the int8 scale
+// maps (16-bit instantiations take any valid map and ignore it).
 template <typename KVT>
-cudaError_t attend_lean_launch_t(int hd, int nq, const void *kmap, const void *vmap, const AttnParams &P,
-                                 int *blocks_per_sm, cudaStream_t s) {
-    if constexpr (KvT<KVT>::dt == DT_F16 || KvT<KVT>::dt == DT_BF16) {
+cudaError_t attend_lean_launch_t(int hd, int nq, const void *kmap, const void *vmap, const void *ksmap,
+                                 const void *vsmap, const AttnParams &P, int *blocks_per_sm, cudaStream_t s) {
+    if constexpr (KvT<KVT>::dt == DT_F16 || KvT<KVT>::dt == DT_BF16 || KvT<KVT>::dt == DT_I8) {
 #define ND_CASE(H, N)                                                                                   \
         if (hd == H && nq == N) {                                                                       \
             constexpr uint32_t smem = attend_lean_smem_bytes<H, KVT, N>();                              \
@@ -85,10 +86,18 @@ cudaError_t attend_lean_launch_t(int hd, int nq, const void *kmap, const void *v
             cfg.numAttrs = 1;                                                                           \
             return cudaLaunchKernelEx(&cfg, attend_lean_kernel<H, KVT, N>,                              \
                                       *static_cast<const CUtensorMap *>(kmap),                          \
-                                      *static_cast<const CUtensorMap *>(vmap), P);                      \
+                                      *static_cast<const CUtensorMap *>(vmap),                          \
+                                      *static_cast<const CUtensorMap *>(ksmap),                         \
+                                      *static_cast<const CUtensorMap *>(vsmap), P);                     \
         }
-        ND_CASE(64, 1) ND_CASE(64, 2) ND_CASE(64, 4) ND_CASE(64, 8)
-        ND_CASE(128, 1) ND_CASE(128, 2) ND_CASE(128, 4)
+        if constexpr (KvT<KVT>::dt == DT_I8) {
+            // int8: query groups of one or two rows (wider groups would cost
+            // registers, hence occupancy; they take the exact-grid kernel).
+            ND_CASE(64, 1) ND_CASE(64, 2) ND_CASE(128, 1) ND_CASE(128, 2)
+        } else {
+            ND_CASE(64, 1) ND_CASE(64, 2) ND_CASE(64, 4) ND_CASE(64, 8)
+            ND_CASE(128, 1) ND_CASE(128, 2) ND_CASE(128, 4)
+        }
 #undef ND_CASE
     }
     return cudaErrorInvalidValue;
@@ -106,7 +115,8 @@ cudaError_t attend_lean_launch_t(int hd, int nq, const void *kmap, const void *v
         return append_launch_t<KVT>(qk, vd, P, s);                                              \
     }                                                                                           \
     cudaError_t attend_lean_launch_##SUF(int hd, int nq, const void *kmap, const void *vmap,    \
-                                         const AttnParams &P, int *blocks_per_sm, cudaStream_t s) { \
-        return attend_lean_launch_t<KVT>(hd, nq, kmap, vmap, P, blocks_per_sm, s);              \
+                                         const void *ksmap, const void *vsmap, const AttnParams &P, \
+                                         int *blocks_per_sm, cudaStream_t s) {                  \
+        return attend_lean_launch_t<KVT>(hd, nq, kmap, vmap, ksmap, vsmap, P, blocks_per_sm, s); \
     }                                                                                           \
     }

@@ -182,3 +182,72 @@ def test_config4_geometry_long_context_paged():
         assert np.array_equal(cache_bits(gk), cache_bits(ok[CTX:CTX + 2]))
         assert np.array_equal(cache_bits(gv), cache_bits(ov[CTX:CTX + 2]))
     a.close()
+
+
+@pytest.mark.parametrize("hd,rep,block_size", [(64, 1, 0), (64, 2, 0), (64, 1, 256), (128, 1, 64), (128, 2, 0)])
+def test_int8_balanced_decode(hd, rep, block_size):
+    """int8 caches (the reference's own format, f32 activations) through the
+    balanced kernel: KV-head counts whose scale rows are 16-byte multiples,
+    so the scales arrive as TMA boxes beside the int8 rows. Every slot is
+    first poisoned with arbitrary int8 bytes and NaN scales; ragged contexts
+    are then filled by prefill (K1 append + the balanced attend, outputs
+    checked too) and decoded for two steps. Outputs within TOL of the oracle,
+    KV bytes and scales bit-exact: rows past each item's end, read by the last
+    box, must contribute nothing."""
+    import torch
+    rng = np.random.default_rng(101 + hd + rep + block_size)
+    HKV = 8 if hd == 64 else 4
+    H, L, W, B = HKV * rep, 2, 1536, 4
+    ctx = [1, 63, 700, 1283]
+    a = ndattn.Attn(n_layers=L, n_heads=H, n_kv_heads=HKV, qk_head_dim=hd, v_head_dim=hd, window=W, max_seqs=B,
+                    kv_dtype="i8", act_dtype="f32", out_dtype="f32", block_size=block_size, max_pos=W)
+    seqs = [O.OracleSeq(L, H, HKV, hd, hd, W, O.I8, max_pos=W) for _ in range(B)]
+    if block_size:
+        nb = W // block_size
+        pages = rng.permutation(B * nb)
+        for s in range(B):
+            a.set_block_table(s, pages[s * nb:(s + 1) * nb])
+    junk_k = torch.from_numpy(rng.integers(-128, 128, size=(W, HKV * hd), dtype=np.int8)).cuda()
+    junk_v = torch.from_numpy(rng.integers(-128, 128, size=(W, HKV * hd), dtype=np.int8)).cuda()
+    nan_sc = torch.full((W, HKV), float("nan"), dtype=torch.float32, device="cuda")
+    for s in range(B):
+        for l in range(L):
+            a.write_cache(l, s, 0, W, junk_k, junk_v, nan_sc, nan_sc)
+    worst = 0.0
+    for s, n in enumerate(ctx):
+        for l in range(L):
+            q = rng.standard_normal((n, H * hd)).astype(np.float32)
+            k = (rng.standard_normal((n, HKV * hd)) * 0.5).astype(np.float32)
+            v = (rng.standard_normal((n, HKV * hd)) * 0.5).astype(np.float32)
+            out = torch.zeros((n, H * hd), dtype=torch.float32, device="cuda")
+            a.prefill(l, [n], dev(q, O.F32), dev(k, O.F32), dev(v, O.F32), out, seq_ids=[s])
+            a.sync()
+            got = out.cpu().numpy()
+            for t in range(n):
+                want = seqs[s].step(l, q[t], k[t], v[t], off=t)
+                worst = max(worst, rel_err(got[t].reshape(H, hd), want))
+        a.advance(1, seq_ids=[s], lens=[n])
+        seqs[s].advance(n)
+    for _ in range(2):
+        q = rng.standard_normal((B, H * hd)).astype(np.float32)
+        k = (rng.standard_normal((B, HKV * hd)) * 0.5).astype(np.float32)
+        v = (rng.standard_normal((B, HKV * hd)) * 0.5).astype(np.float32)
+        for l in range(L):
+            out = torch.zeros((B, H * hd), dtype=torch.float32, device="cuda")
+            a.decode(l, B, dev(q, O.F32), dev(k, O.F32), dev(v, O.F32), out)
+            a.sync()
+            got = out.cpu().numpy()
+            for s in range(B):
+                worst = max(worst, rel_err(got[s].reshape(H, hd), seqs[s].step(l, q[s], k[s], v[s])))
+        a.advance(B)
+        for s in seqs:
+            s.advance()
+    assert worst <= TOL, worst
+    for s, seq in enumerate(seqs):
+        n = seq.pos
+        for l in range(L):
+            gk, gv, gks, gvs = a.read_cache(l, s, 0, n)
+            assert np.array_equal(gk, seq.k[l][:n]) and np.array_equal(gv, seq.v[l][:n]), (s, l)
+            assert np.array_equal(gks.view(np.uint32), seq.ks[l][:n].view(np.uint32)), (s, l)
+            assert np.array_equal(gvs.view(np.uint32), seq.vs[l][:n].view(np.uint32)), (s, l)
+    a.close()
