@@ -572,7 +572,7 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                         ksc[u] = valid[u] ? ks[r * 4 + (d.g & 3u)] : 0.0f;
                         vsc[u] = valid[u] ? vs[r * 4 + (d.g & 3u)] : 0.0f;
                     }
-                    consume<HD, HD, KVT, NQ, UB>(qr, kw, vw, ksc, vsc, valid, m, l, acc);
+                    consume<HD, HD, KVT, NQ, UB, true>(qr, kw, vw, ksc, vsc, valid, m, l, acc);
                 } else {
                     consume<HD, HD, KVT, NQ, UB>(qr, kw, vw, zero_sc, zero_sc, valid, m, l, acc);
                 }
@@ -596,7 +596,7 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
             const bool valid[1] = {rl == 0};
             load_words<WK, false>(kb + row * (size_t)P.c.k_dim * ES, kw[0]);
             load_words<WV, false>(vb + row * (size_t)P.c.v_dim * ES, vw[0]);
-            consume<HD, HD, KVT, NQ, 1>(qr, kw, vw, ksc1, vsc1, valid, m, l, acc);
+            consume<HD, HD, KVT, NQ, 1, true>(qr, kw, vw, ksc1, vsc1, valid, m, l, acc);
         }
         // Reduce across the row lanes; hand (m, l, acc) of this warp over.
 #pragma unroll

@@ -504,11 +504,21 @@ __device__ __forceinline__ void load_words(const void *p, uint32_t (&w)[W]) {
     }
 }
 
-template <typename KVT, int W>
+// I8_PERM: int8 through the ALU instead of the conversion unit. XOR with 0x80
+// turns each signed byte b into b + 128; a byte permute places it in the low
+// mantissa bits of 2^23 (bits 0x4B0000xx), and subtracting 2^23 + 128 leaves
+// b exactly. The balanced kernel is conversion-bound on int8 rows and takes
+// it; the exact-grid kernel measured slower with it and keeps the conversion.
+template <typename KVT, int W, bool I8_PERM = false>
 __device__ __forceinline__ void unpack(const uint32_t (&w)[W], float *f) {
 #pragma unroll
     for (int i = 0; i < W; i++) {
-        if constexpr (KvT<KVT>::dt == DT_I8) {
+        if constexpr (KvT<KVT>::dt == DT_I8 && I8_PERM) {
+            const uint32_t x = w[i] ^ 0x80808080u;
+#pragma unroll
+            for (int b = 0; b < 4; b++)
+                f[4 * i + b] = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7540u + b)) - 8388736.0f;
+        } else if constexpr (KvT<KVT>::dt == DT_I8) {
             f[4 * i + 0] = (float)(int8_t)(w[i] & 0xffu);
             f[4 * i + 1] = (float)(int8_t)((w[i] >> 8) & 0xffu);
             f[4 * i + 2] = (float)(int8_t)((w[i] >> 16) & 0xffu);
@@ -542,8 +552,9 @@ struct AttendShape {
     static_assert(QK % LPR == 0 && (EK * ES) % 4 == 0, "K chunk");
 };
 
-// Online-softmax update of one warp with UU row groups of loaded K/V words.
-template <int QK, int VD, typename KVT, int NQ, int UU>
+// Online-softmax update of one warp with UU row groups of loaded K/V words
+// (I8_PERM: the int8 unpack above).
+template <int QK, int VD, typename KVT, int NQ, int UU, bool I8_PERM = false>
 __device__ __forceinline__ void consume(const float (&qr)[NQ][AttendShape<QK, VD, KVT, NQ>::EK],
                                         const uint32_t (&kw)[UU][AttendShape<QK, VD, KVT, NQ>::WK],
                                         const uint32_t (&vw)[UU][AttendShape<QK, VD, KVT, NQ>::WV],
@@ -556,7 +567,7 @@ __device__ __forceinline__ void consume(const float (&qr)[NQ][AttendShape<QK, VD
 #pragma unroll
     for (int u = 0; u < UU; u++) {
         float kf[S::EK];
-        unpack<KVT, S::WK>(kw[u], kf);
+        unpack<KVT, S::WK, I8_PERM>(kw[u], kf);
 #pragma unroll
         for (int qi = 0; qi < NQ; qi++) {
             float a = 0.0f;
@@ -603,7 +614,7 @@ __device__ __forceinline__ void consume(const float (&qr)[NQ][AttendShape<QK, VD
 #pragma unroll
     for (int u = 0; u < UU; u++) {
         float vf[S::EV];
-        unpack<KVT, S::WV>(vw[u], vf);
+        unpack<KVT, S::WV, I8_PERM>(vw[u], vf);
 #pragma unroll
         for (int qi = 0; qi < NQ; qi++) {
             const float pv = SCALED ? p[u][qi] * vsc[u] : p[u][qi];
