@@ -49,7 +49,7 @@ P_METRIC = "prefill tok/s (config 3: 512 seq x 1024 tok x 8 layers, GQA 16/4, hd
 # the decode launch on the one-layer case (per-launch work equals a launch
 # here), the prefill launch on 64 sequences scaled by 8 to 512 (traffic grows
 # with the sequences processed).
-DECODE_TRAFFIC = (157.5e6 + 3.9e6)
+DECODE_TRAFFIC = (153.7e6 + 1.8e6)
 PREFILL_TRAFFIC = (309.5e6 + 100.4e6) * 8
 # config 4 (long-context paged decode)
 L_SEQS, L_CTX, L_H, L_HD, L_BLOCK, L_STEPS = 256, 32768, 8, 128, 64, 64
@@ -387,6 +387,89 @@ def run_decode(args, world, rank, local, dist):
                 "d2h_bytes_per_step": int(LAYERS * BATCH * H * VD * 2)},
         "gpu_launches": int(launches), "clocks": clk.summary(),
     }
+
+
+def run_decode_int8(args, world, rank, local, dist):
+    """Config 2's decode in the reference's own cache format: int8 K/V with one
+    f32 scale per (slot, KV head), f32 activations. The cached rows are the
+    config's N(0,1)*0.5 values quantised per (row, head) to amax/127 scales
+    (seed 2000 + rank); same contexts, layers and step count as the fp16 line."""
+    import torch
+
+    import ndattn
+
+    K, Wm = args.steps, args.warmup
+    ctx = ctx_lengths(rank)
+    window = (CTX_HI + K + Wm + 2 + 63) // 64 * 64
+    a = ndattn.Attn(n_layers=LAYERS, n_heads=H, n_kv_heads=HKV, qk_head_dim=QK, v_head_dim=VD, window=window,
+                    max_seqs=BATCH, kv_dtype="i8", act_dtype="f32", out_dtype="f32", device=local)
+    stream = torch.cuda.ExternalStream(a.stream)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(2000 + rank)
+
+    def quant(x, d):
+        x = x.view(x.shape[0], HKV, d)
+        sc = (x.abs().amax(dim=2) / 127.0).clamp_min(1e-30)
+        q8 = torch.round(x / sc[..., None]).clamp(-127, 127).to(torch.int8)
+        return q8.view(x.shape[0], HKV * d).contiguous(), sc.contiguous()
+
+    for l in range(LAYERS):
+        for s in range(BATCH):
+            n = int(ctx[s])
+            kq, ks = quant(torch.randn((n, HKV * QK), generator=gen, device="cuda") * 0.5, QK)
+            vq, vs = quant(torch.randn((n, HKV * VD), generator=gen, device="cuda") * 0.5, VD)
+            torch.cuda.synchronize()
+            a.write_cache(l, s, 0, n, kq, vq, ks, vs)
+    for s in range(BATCH):
+        a.set_state(s, int(ctx[s]), 0)
+    nsteps = K + Wm
+    q = torch.randn((nsteps, LAYERS, BATCH, H * QK), generator=gen, device="cuda")
+    k = torch.randn((nsteps, LAYERS, BATCH, HKV * QK), generator=gen, device="cuda") * 0.5
+    v = torch.randn((nsteps, LAYERS, BATCH, HKV * VD), generator=gen, device="cuda") * 0.5
+    out = torch.empty((LAYERS, BATCH, H * VD), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+
+    def step(i):
+        for l in range(LAYERS):
+            a.decode(l, BATCH, q[i, l], k[i, l], v[i, l], out[l])
+        a.advance(BATCH)
+
+    for i in range(Wm):
+        step(i)
+    a.sync()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = a.launches
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(K):
+        step(Wm + i)
+    t1.record(stream)
+    a.sync()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches = a.launches - launches0
+    a.close()
+    t = torch.tensor([t0.elapsed_time(t1)], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    # Algorithmic bytes of a launch: visited K and V rows (1 B per element)
+    # and their two f32 scales per KV head, plus f32 q/k/v in and out.
+    pos0 = ctx + Wm
+    rows = sum(float((pos0 + i + 1).sum()) for i in range(K)) / K
+    bytes_per_launch = rows * HKV * (QK + VD + 8) + BATCH * (H * QK + HKV * QK + HKV * VD + H * VD) * 4
+    avg_s = ms / 1e3 / (K * LAYERS)
+    pk, peak_kind = peaks()
+    achieved = bytes_per_launch / avg_s / 1e9
+    return {"value": BATCH * world * K / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms / K, "steps": K,
+            "kv_dtype": "int8 + f32 scale per (slot, KV head)", "act_dtype": "f32",
+            "kernel": "attend_lean_kernel<64,int8,1>", "avg_launch_us": avg_s * 1e6,
+            "bytes_per_launch": bytes_per_launch, "achieved_gbs": achieved,
+            "frac": achieved / pk["hbm_gbs"], "peak_kind": f"{peak_kind} copy bandwidth",
+            "gpu_launches": int(launches)}
 
 
 # ------------------------------------------------------- GPU: head-sharded decode
@@ -822,6 +905,7 @@ def run_ours(args):
     else:
         dec = run_decode(args, world, rank, local, dist)
         taps = run_decode_taps(args, world, rank, local, dist, dec["value"])
+        i8 = run_decode_int8(args, world, rank, local, dist)
         heads = run_decode_heads(args, world, rank, local, dist) if world > 1 and HKV % world == 0 else None
         pre = run_prefill(args, world, rank, local, dist) if args.prefill_steps > 0 else None
         lng = run_long(args, world, rank, local, dist) if args.long_steps > 0 else None
@@ -849,9 +933,9 @@ def run_ours(args):
                     "roofline": dec["roofline"], "cpu_baseline": cpu, "e2e": dec["e2e"],
                     "gpu_launches": dec["gpu_launches"] + (pre["gpu_launches"] if pre else 0)
                     + (lng["gpu_launches"] if lng else 0) + (srv["gpu_launches"] if srv else 0)
-                    + taps["gpu_launches"],
+                    + taps["gpu_launches"] + i8["gpu_launches"],
                     "clocks": dec["clocks"], "prefill": pre, "long_decode": lng, "serving": srv,
-                    "head_sharded": heads, "conv_taps": taps}
+                    "head_sharded": heads, "conv_taps": taps, "decode_int8": i8}
             print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -277,6 +277,7 @@ struct nd_attn {
     uint64_t lean_nt = 0, lean_g = 0, lean_s = 0, lean_ch = 0, lean_nu = 0;
     std::vector<CUtensorMap> lean_kmap, lean_vmap;   // per layer, built on first use
     std::vector<CUtensorMap> lean_ksmap, lean_vsmap; // int8: the layer's scale maps
+    std::vector<CUtensorMap> lean_ktmap, lean_vtmap; // K / V rows in 16-row boxes (item tails)
     std::vector<uint8_t> lean_map_ok;
     uint32_t lean_parity = 0;          // half of counters / partials the next balanced launch uses
     // Cache rows our most recently launched kernel may write: kNoLayer (none),
@@ -624,17 +625,17 @@ int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, co
     const uint32_t hd = cf.qk_head_dim;
     const int nq = nda::nq_for_rep(h->rep);
     const bool bf16 = cf.kv_dtype == ND_DT_BF16, i8 = cf.kv_dtype == ND_DT_I8;
-    auto launch = [&](const void *km, const void *vm, const void *ksm, const void *vsm, const nda::AttnParams &P,
-                      int *occ) {
-        return i8     ? nda::attend_lean_launch_i8((int)hd, nq, km, vm, ksm, vsm, P, occ, h->stream)
-               : bf16 ? nda::attend_lean_launch_bf16((int)hd, nq, km, vm, ksm, vsm, P, occ, h->stream)
-                      : nda::attend_lean_launch_f16((int)hd, nq, km, vm, ksm, vsm, P, occ, h->stream);
+    auto launch = [&](const void *km, const void *vm, const void *ksm, const void *vsm, const void *ktm,
+                      const void *vtm, const nda::AttnParams &P, int *occ) {
+        return i8     ? nda::attend_lean_launch_i8((int)hd, nq, km, vm, ksm, vsm, ktm, vtm, P, occ, h->stream)
+               : bf16 ? nda::attend_lean_launch_bf16((int)hd, nq, km, vm, ksm, vsm, ktm, vtm, P, occ, h->stream)
+                      : nda::attend_lean_launch_f16((int)hd, nq, km, vm, ksm, vsm, ktm, vtm, P, occ, h->stream);
     };
     int &occ = h->lean_occ[(bf16 ? 4 : 0) + (nq == 1 ? 0 : nq == 2 ? 1 : nq == 4 ? 2 : 3)];
     AttnParams P = base_params(h, layer);
     if (occ <= 0) {
         int b = 0;
-        ND_CUDA(launch(nullptr, nullptr, nullptr, nullptr, P, &b));
+        ND_CUDA(launch(nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, P, &b));
         if (b <= 0) return fail(ND_ATTN_ERR_CUDA, "balanced attend kernel does not fit on an SM");
         occ = b;
     }
@@ -683,16 +684,22 @@ int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, co
         h->lean_vmap.resize(cf.n_layers);
         h->lean_ksmap.resize(cf.n_layers);
         h->lean_vsmap.resize(cf.n_layers);
+        h->lean_ktmap.resize(cf.n_layers);
+        h->lean_vtmap.resize(cf.n_layers);
         h->lean_map_ok.assign(cf.n_layers, 0);
     }
     if (!h->lean_map_ok[layer]) {   // the layer's cache never moves: encode its maps once
-        // Rows of [n_kv][hd] elements, box {hd, 64} at x = g * hd; int8 scales
+        // Rows of [n_kv][hd] elements, box {hd, 64} (item tails: {hd, 16}) at x = g * hd; int8 scales
         // [n_kv] f32 per row, box {4, 64} at x = g rounded down to 4 (16 bytes).
         const size_t es = h->kes;
         int rc = make_map_dt(&h->lean_kmap[layer], cf.kv_dtype, P.c.k, h->k_dim, h->rows_per_layer,
                              (uint64_t)h->k_dim * es, nda::kTmaRows, hd, false);
         if (!rc) rc = make_map_dt(&h->lean_vmap[layer], cf.kv_dtype, P.c.v, h->v_dim, h->rows_per_layer,
                                   (uint64_t)h->v_dim * es, nda::kTmaRows, hd, false);
+        if (!rc) rc = make_map_dt(&h->lean_ktmap[layer], cf.kv_dtype, P.c.k, h->k_dim, h->rows_per_layer,
+                                  (uint64_t)h->k_dim * es, 16, hd, false);
+        if (!rc) rc = make_map_dt(&h->lean_vtmap[layer], cf.kv_dtype, P.c.v, h->v_dim, h->rows_per_layer,
+                                  (uint64_t)h->v_dim * es, 16, hd, false);
         if (!rc && i8) rc = make_map_dt(&h->lean_ksmap[layer], ND_DT_F32, P.c.ks, cf.n_kv_heads, h->rows_per_layer,
                                         (uint64_t)cf.n_kv_heads * 4, nda::kTmaRows, 4, false);
         if (!rc && i8) rc = make_map_dt(&h->lean_vsmap[layer], ND_DT_F32, P.c.vs, cf.n_kv_heads, h->rows_per_layer,
@@ -702,8 +709,8 @@ int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, co
         h->lean_map_ok[layer] = 1;
     }
     note_writer(h, fuse_append ? (int)layer : kNoLayer);
-    ND_CUDA(launch(&h->lean_kmap[layer], &h->lean_vmap[layer], &h->lean_ksmap[layer], &h->lean_vsmap[layer], P,
-                   nullptr));
+    ND_CUDA(launch(&h->lean_kmap[layer], &h->lean_vmap[layer], &h->lean_ksmap[layer], &h->lean_vsmap[layer],
+                   &h->lean_ktmap[layer], &h->lean_vtmap[layer], P, nullptr));
     h->launches++;
     return ND_ATTN_OK;
 }

@@ -65,6 +65,9 @@ template <int HD, typename KVT, int NQ> struct LeanCfg {
     static constexpr int STAGES = I8 ? (HD == 64 ? 6 : 4) : HD == 64 ? ND_LEAN_STAGES64 : (NQ >= 4 ? 2 : 3);
     static constexpr int SQ = NQ * HD >= 256 ? 2 : 4;                // segment slot ring depth
     static constexpr uint32_t TILE = kTmaRows * HD * sizeof(KVT);
+    // An item's last tile loads only the 16-row sub-boxes that hold its rows.
+    static constexpr int SUBR = 16;
+    static constexpr uint32_t SUB = SUBR * HD * sizeof(KVT);
     // int8: per stage the K and V scales of the tile's rows for four KV heads
     // (a {4, 64} f32 box: TMA moves at least 16 bytes per row).
     static constexpr uint32_t SC = I8 ? kTmaRows * 16 : 0;
@@ -197,6 +200,8 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                                                           const __grid_constant__ CUtensorMap vmap,
                                                           const __grid_constant__ CUtensorMap ksmap,
                                                           const __grid_constant__ CUtensorMap vsmap,
+                                                          const __grid_constant__ CUtensorMap ktmap,
+                                                          const __grid_constant__ CUtensorMap vtmap,
                                                           const AttnParams P) {
     using C = LeanCfg<HD, KVT, NQ>;
     using S = AttendShape<HD, HD, KVT, NQ>;
@@ -296,9 +301,26 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                         const uint32_t s2 = tc % STAGES;
                         if (tc == STAGES && !grabbed) ND_LEAN_GRAB_AHEAD();
                         if (tc >= STAGES && !mbar_wait(&empty[s2], ((tc / STAGES) - 1) & 1, abort_flag)) break;
-                        mbar_expect_tx(&full[s2], 2 * TILE_BYTES + 2 * C::SC);
-                        tma_load_2d(smem + s2 * TILE_BYTES, &kmap, (int)(w.g * HD), y, &full[s2]);
-                        tma_load_2d(smem + C::OFF_V + s2 * TILE_BYTES, &vmap, (int)(w.g * HD), y, &full[s2]);
+                        // Rows of this tile the item reads: [row0, jw). A tile that
+                        // ends 16 or more rows past them takes 16-row sub-boxes (the
+                        // rest of the stage keeps stale rows, which the consumers mask).
+                        const uint32_t row0 = (w.kt + k2) * TR, jw = w.pos + 1u - (P.fuse_append ? 1u : 0u);
+                        const uint32_t nsub = jw >= row0 + (uint32_t)(TR - C::SUBR) + 1u
+                                                  ? 0u
+                                                  : jw > row0 ? (jw - row0 + C::SUBR - 1) / C::SUBR : 1u;
+                        mbar_expect_tx(&full[s2], (nsub ? 2 * nsub * C::SUB : 2 * TILE_BYTES) + 2 * C::SC);
+                        if (nsub == 0) {
+                            tma_load_2d(smem + s2 * TILE_BYTES, &kmap, (int)(w.g * HD), y, &full[s2]);
+                            tma_load_2d(smem + C::OFF_V + s2 * TILE_BYTES, &vmap, (int)(w.g * HD), y, &full[s2]);
+                        } else {
+                            for (uint32_t j = 0; j < nsub; j++) {
+                                const int yj = y + (int)j * C::SUBR;
+                                tma_load_2d(smem + s2 * TILE_BYTES + j * C::SUB, &ktmap, (int)(w.g * HD), yj,
+                                            &full[s2]);
+                                tma_load_2d(smem + C::OFF_V + s2 * TILE_BYTES + j * C::SUB, &vtmap,
+                                            (int)(w.g * HD), yj, &full[s2]);
+                            }
+                        }
                         if constexpr (C::I8) {   // x = the KV head rounded down to a multiple of 4 (16 bytes)
                             tma_load_2d(smem + C::OFF_KS + s2 * C::SC, &ksmap, (int)(w.g & ~3u), y, &full[s2]);
                             tma_load_2d(smem + C::OFF_VS + s2 * C::SC, &vsmap, (int)(w.g & ~3u), y, &full[s2]);

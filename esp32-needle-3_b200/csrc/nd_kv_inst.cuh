@@ -59,10 +59,12 @@ cudaError_t append_launch_t(int qk, int vd, const AttnParams &P, cudaStream_t s)
 // raises the kernel's dynamic shared memory limit and reports how many CTAs of
 // the instantiation one SM holds (no launch); the host asks once per handle
 // and instantiation before the first launch. ksmap / vsmap: the int8 scale
-// maps (16-bit instantiations take any valid map and ignore it).
+// maps (16-bit instantiations take any valid map and ignore it); ktmap /
+// vtmap: the same rows as kmap / vmap in 16-row boxes (item tails).
 template <typename KVT>
 cudaError_t attend_lean_launch_t(int hd, int nq, const void *kmap, const void *vmap, const void *ksmap,
-                                 const void *vsmap, const AttnParams &P, int *blocks_per_sm, cudaStream_t s) {
+                                 const void *vsmap, const void *ktmap, const void *vtmap, const AttnParams &P,
+                                 int *blocks_per_sm, cudaStream_t s) {
     if constexpr (KvT<KVT>::dt == DT_F16 || KvT<KVT>::dt == DT_BF16 || KvT<KVT>::dt == DT_I8) {
 #define ND_CASE(H, N)                                                                                   \
         if (hd == H && nq == N) {                                                                       \
@@ -88,7 +90,9 @@ cudaError_t attend_lean_launch_t(int hd, int nq, const void *kmap, const void *v
                                       *static_cast<const CUtensorMap *>(kmap),                          \
                                       *static_cast<const CUtensorMap *>(vmap),                          \
                                       *static_cast<const CUtensorMap *>(ksmap),                         \
-                                      *static_cast<const CUtensorMap *>(vsmap), P);                     \
+                                      *static_cast<const CUtensorMap *>(vsmap),                         \
+                                      *static_cast<const CUtensorMap *>(ktmap),                         \
+                                      *static_cast<const CUtensorMap *>(vtmap), P);                     \
         }
         if constexpr (KvT<KVT>::dt == DT_I8) {
             // int8: query groups of one or two rows (wider groups would cost
@@ -115,8 +119,9 @@ cudaError_t attend_lean_launch_t(int hd, int nq, const void *kmap, const void *v
         return append_launch_t<KVT>(qk, vd, P, s);                                              \
     }                                                                                           \
     cudaError_t attend_lean_launch_##SUF(int hd, int nq, const void *kmap, const void *vmap,    \
-                                         const void *ksmap, const void *vsmap, const AttnParams &P, \
-                                         int *blocks_per_sm, cudaStream_t s) {                  \
-        return attend_lean_launch_t<KVT>(hd, nq, kmap, vmap, ksmap, vsmap, P, blocks_per_sm, s); \
+                                         const void *ksmap, const void *vsmap, const void *ktmap,  \
+                                         const void *vtmap, const AttnParams &P, int *blocks_per_sm, \
+                                         cudaStream_t s) {                                      \
+        return attend_lean_launch_t<KVT>(hd, nq, kmap, vmap, ksmap, vsmap, ktmap, vtmap, P, blocks_per_sm, s); \
     }                                                                                           \
     }
