@@ -76,8 +76,16 @@ __global__ void set_state_kernel(SeqState *st, uint32_t seq, uint32_t pos, uint3
     st[seq].n_sink = n_sink;
 }
 
+// Launched as a programmatic dependent: the launch after it may start at once
+// (every kernel that reads positions does so after its own grid-dependency
+// wait, which returns once this grid has completed), while this grid waits for
+// the kernels before it, which may still read the positions, before changing
+// them. So the attend launch that follows a step's advance starts under the
+// previous attend launch's tail, as consecutive attend launches do.
 __global__ void advance_kernel(SeqState *st, uint32_t n, const uint32_t *ids, const uint32_t *len,
                                uint32_t step) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     st[ids ? ids[i] : i].pos += len ? len[i] : step;
@@ -1248,8 +1256,18 @@ int nd_attn_advance(nd_attn *h, uint32_t n, const uint32_t *seq_ids, const uint3
         }
     }
     for (uint32_t i = 0; i < n; i++) h->seqs[seq_ids ? seq_ids[i] : i].pos += len ? len[i] : 1;
-    note_writer(h, kNoLayer);
-    advance_kernel<<<(n + 127) / 128, 128, 0, h->stream>>>(h->d_state, n, d_ids, d_len, 1);
+    // No note_writer: the advance writes no cache, but the kernel before it may
+    // still be running when the attend launch after it starts.
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((n + 127) / 128);
+    lc.blockDim = dim3(128);
+    lc.stream = h->stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    ND_CUDA(cudaLaunchKernelEx(&lc, advance_kernel, h->d_state, n, d_ids, d_len, 1u));
     h->launches++;
     ND_CUDA(cudaGetLastError());
     return ND_ATTN_OK;
