@@ -286,6 +286,7 @@ struct nd_attn {
     std::vector<CUtensorMap> lean_kmap, lean_vmap;   // per layer, built on first use
     std::vector<CUtensorMap> lean_ksmap, lean_vsmap; // int8: the layer's scale maps
     std::vector<CUtensorMap> lean_ktmap, lean_vtmap; // K / V rows in 16-row boxes (item tails)
+    nda::LeanTok lean_tok;             // a small call's tokens, passed as launch parameters
     std::vector<uint8_t> lean_map_ok;
     uint32_t lean_parity = 0;          // half of counters / partials the next balanced launch uses
     // Cache rows our most recently launched kernel may write: kNoLayer (none),
@@ -570,6 +571,21 @@ constexpr uint32_t kLeanAhead = 2;
 // unit the walk state at its first tile. Uploads it when it differs from what
 // the device holds and records its shape (tiles, static units and their
 // size, dynamic unit size, units).
+// Unit geometry of a balanced launch of nt tiles. Launches alternate between
+// two halves of the tickets and of the partial scratch (two consecutive
+// launches may overlap). Unit budget per half: tickets [0, NU) plus the two
+// queue counters, 2 NU partial slots.
+void lean_geometry(nd_attn *h, uint64_t nt, int occ) {
+    const size_t cnt_half = h->counter_cap / 2, slot_half = h->part_slots / 2;
+    const uint64_t budget = std::min<uint64_t>(cnt_half - 2, slot_half / 2);
+    const uint64_t G = std::min<uint64_t>({nt, (uint64_t)h->sm_count * (uint64_t)occ, budget});
+    const uint64_t S = std::max<uint64_t>(1, nt * kLeanStaticPct / (100 * G));
+    const uint64_t dyn = nt - G * S;
+    uint64_t CH = std::max<uint64_t>(kLeanUnitMin, (dyn + 4 * G - 1) / (4 * G));
+    while (G + (dyn + CH - 1) / CH > budget) CH *= 2;
+    h->lean_nt = nt, h->lean_g = G, h->lean_s = S, h->lean_ch = CH, h->lean_nu = G + (dyn + CH - 1) / CH;
+}
+
 int build_lean_plan(nd_attn *h, uint32_t ntok, const std::vector<uint32_t> &vis, const std::vector<uint32_t> &tok_seq,
                     const std::vector<uint32_t> &tok_pos, int fuse_append, int occ) {
     const uint32_t n_kv = h->cfg.n_kv_heads;
@@ -587,17 +603,8 @@ int build_lean_plan(nd_attn *h, uint32_t ntok, const std::vector<uint32_t> &vis,
         if (nt > 0x7fffffffu) return fail(ND_ATTN_ERR_RANGE, "launch too large");
     }
     up[4 * ntok] = (uint32_t)nt;
-    // Launches alternate between two halves of the tickets and of the partial
-    // scratch (two consecutive launches may overlap). Unit budget per half:
-    // tickets [0, NU) plus the two queue counters, 2 NU partial slots.
-    const size_t cnt_half = h->counter_cap / 2, slot_half = h->part_slots / 2;
-    const uint64_t budget = std::min<uint64_t>(cnt_half - 2, slot_half / 2);
-    const uint64_t G = std::min<uint64_t>({nt, (uint64_t)h->sm_count * (uint64_t)occ, budget});
-    const uint64_t S = std::max<uint64_t>(1, nt * kLeanStaticPct / (100 * G));
-    const uint64_t dyn = nt - G * S;
-    uint64_t CH = std::max<uint64_t>(kLeanUnitMin, (dyn + 4 * G - 1) / (4 * G));
-    while (G + (dyn + CH - 1) / CH > budget) CH *= 2;
-    const uint64_t NU = G + (dyn + CH - 1) / CH;
+    lean_geometry(h, nt, occ);
+    const uint64_t G = h->lean_g, S = h->lean_s, CH = h->lean_ch, NU = h->lean_nu;
     const size_t ub = up.size();
     up.resize(ub + NU * 8, 0u);
     for (uint64_t u = 0, t = 0; u < NU; u++) {
@@ -615,7 +622,6 @@ int build_lean_plan(nd_attn *h, uint32_t ntok, const std::vector<uint32_t> &vis,
                                 h->stream));
         h->lean_last = up;
     }
-    h->lean_nt = nt, h->lean_g = G, h->lean_s = S, h->lean_ch = CH, h->lean_nu = NU;
     return ND_ATTN_OK;
 }
 
@@ -635,9 +641,10 @@ int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, co
     const bool bf16 = cf.kv_dtype == ND_DT_BF16, i8 = cf.kv_dtype == ND_DT_I8;
     auto launch = [&](const void *km, const void *vm, const void *ksm, const void *vsm, const void *ktm,
                       const void *vtm, const nda::AttnParams &P, int *occ) {
-        return i8     ? nda::attend_lean_launch_i8((int)hd, nq, km, vm, ksm, vsm, ktm, vtm, P, occ, h->stream)
-               : bf16 ? nda::attend_lean_launch_bf16((int)hd, nq, km, vm, ksm, vsm, ktm, vtm, P, occ, h->stream)
-                      : nda::attend_lean_launch_f16((int)hd, nq, km, vm, ksm, vsm, ktm, vtm, P, occ, h->stream);
+        const nda::LeanTok *tk = &h->lean_tok;
+        return i8     ? nda::attend_lean_launch_i8((int)hd, nq, km, vm, ksm, vsm, ktm, vtm, tk, P, occ, h->stream)
+               : bf16 ? nda::attend_lean_launch_bf16((int)hd, nq, km, vm, ksm, vsm, ktm, vtm, tk, P, occ, h->stream)
+                      : nda::attend_lean_launch_f16((int)hd, nq, km, vm, ksm, vsm, ktm, vtm, tk, P, occ, h->stream);
     };
     int &occ = h->lean_occ[(bf16 ? 4 : 0) + (nq == 1 ? 0 : nq == 2 ? 1 : nq == 4 ? 2 : 3)];
     AttnParams P = base_params(h, layer);
@@ -647,22 +654,42 @@ int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, co
         if (b <= 0) return fail(ND_ATTN_ERR_CUDA, "balanced attend kernel does not fit on an SM");
         occ = b;
     }
-    // Plan: per token {first tile, tiles per item, sequence, position} (and a
-    // sentinel), then per unit the walk state at its first tile. Rebuilt only
-    // when its inputs differ from the last plan's.
-    std::vector<uint32_t> &key = h->lean_key_next;
-    key.resize((size_t)ntok * 3 + 2);
-    key[0] = (uint32_t)fuse_append;
-    key[1] = (uint32_t)occ;
-    for (uint32_t t = 0; t < ntok; t++) {
-        key[2 + 3 * t] = vis[t];
-        key[3 + 3 * t] = tok_seq[t];
-        key[4 + 3 * t] = tok_pos[t];
-    }
-    if (key != h->lean_key) {
-        int rc = build_lean_plan(h, ntok, vis, tok_seq, tok_pos, fuse_append, occ);
-        if (rc) return rc;
-        h->lean_key.swap(key);
+    nda::LeanTok &tk = h->lean_tok;
+    if (ntok <= (uint32_t)nda::kLeanParamTok) {
+        // A small call's token table travels as a launch parameter (the same
+        // entries as build_lean_plan's): no copy between this launch and the
+        // one before, which it overlaps.
+        uint64_t nt = 0;
+        for (uint32_t t = 0; t < ntok; t++) {
+            const uint32_t rows = vis[t] - (fuse_append ? 1u : 0u);
+            const uint32_t T = std::max<uint32_t>(1u, (rows + nda::kTmaRows - 1) / nda::kTmaRows);
+            tk.tok[t] = make_uint4((uint32_t)nt, T, tok_seq[t], tok_pos[t]);
+            nt += (uint64_t)cf.n_kv_heads * T;
+            if (nt > 0x7fffffffu) return fail(ND_ATTN_ERR_RANGE, "launch too large");
+        }
+        tk.tok[ntok] = make_uint4((uint32_t)nt, 0u, 0u, 0u);
+        tk.n = ntok;
+        lean_geometry(h, nt, occ);
+        h->lean_key.clear();   // the next large call rebuilds its plan and geometry
+    } else {
+        // Plan: per token {first tile, tiles per item, sequence, position} (and
+        // a sentinel), then per unit the walk state at its first tile. Rebuilt
+        // only when its inputs differ from the last plan's.
+        tk.n = 0;
+        std::vector<uint32_t> &key = h->lean_key_next;
+        key.resize((size_t)ntok * 3 + 2);
+        key[0] = (uint32_t)fuse_append;
+        key[1] = (uint32_t)occ;
+        for (uint32_t t = 0; t < ntok; t++) {
+            key[2 + 3 * t] = vis[t];
+            key[3 + 3 * t] = tok_seq[t];
+            key[4 + 3 * t] = tok_pos[t];
+        }
+        if (key != h->lean_key) {
+            int rc = build_lean_plan(h, ntok, vis, tok_seq, tok_pos, fuse_append, occ);
+            if (rc) return rc;
+            h->lean_key.swap(key);
+        }
     }
     const uint64_t nt = h->lean_nt, G = h->lean_g, S = h->lean_s, CH = h->lean_ch, NU = h->lean_nu;
     const size_t cnt_half = h->counter_cap / 2, slot_half = h->part_slots / 2;

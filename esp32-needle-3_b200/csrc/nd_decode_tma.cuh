@@ -100,20 +100,42 @@ struct LeanUnits {
 
 // Position in the item list: token t (q row t), KV head g, tile kt of the
 // item; T tiles per item of the token, base = first tile of the token, and
-// the token's sequence and position. The host plans the call and uploads, per
-// token, {base, T, seq, pos} (P.split_cu, uint4) and, per unit, the walk
-// state at its first tile (P.cta_tok, two uint4): one load starts a unit,
-// where a chain of dependent lookups would cost several round trips.
+// the token's sequence and position. Per token {base, T, seq, pos} (uint4)
+// comes from a table the host builds: for calls of at most kLeanParamTok
+// tokens it is a kernel parameter (LeanTok) and a unit's walk state is found by
+// binary search over it; for larger calls the host uploads it (P.split_cu)
+// with, per unit, the walk state at its first tile (P.cta_tok, two uint4): one
+// global load starts a unit, where a chain of dependent lookups would cost
+// several round trips.
 struct LeanWalk {
     uint32_t t, g, kt, T, base, seq, pos;
-    __device__ __forceinline__ void load_token(const AttnParams &P) {
-        const uint4 v = reinterpret_cast<const uint4 *>(P.split_cu)[t];
+    const uint4 *tab;
+    __device__ __forceinline__ void load_token() {
+        const uint4 v = tab[t];
         base = v.x, T = v.y, seq = v.z, pos = v.w;
     }
     __device__ __forceinline__ void init(const AttnParams &P, uint32_t u) {
+        tab = reinterpret_cast<const uint4 *>(P.split_cu);
         const uint4 a = reinterpret_cast<const uint4 *>(P.cta_tok)[2 * u];
         const uint4 b = reinterpret_cast<const uint4 *>(P.cta_tok)[2 * u + 1];
         t = a.x, g = a.y, kt = a.z, T = a.w, base = b.x, seq = b.y, pos = b.z;
+    }
+    // Walk state at tile x0 (below the call's total) of a table of ntok
+    // tokens: the last token whose first tile is <= x0 (every token holds at
+    // least one tile per KV head, so first tiles strictly increase).
+    __device__ __forceinline__ void init_at(const uint4 *tab_, uint32_t ntok, uint32_t x0) {
+        tab = tab_;
+        uint32_t lo = 0, hi = ntok;
+        while (hi - lo > 1) {
+            const uint32_t mid = (lo + hi) / 2;
+            if (tab[mid].x <= x0) lo = mid;
+            else hi = mid;
+        }
+        t = lo;
+        load_token();
+        const uint32_t r = x0 - base;
+        g = r / T;
+        kt = r - g * T;
     }
     __device__ __forceinline__ uint32_t item_start() const { return base + g * T; }
     // Advances past nt tiles of the current item (nt <= T - kt).
@@ -123,7 +145,7 @@ struct LeanWalk {
         kt = 0;
         if (++g < P.c.n_kv) return;
         g = 0;
-        if (++t < P.n_tok) load_token(P);
+        if (++t < P.n_tok) load_token();
     }
 };
 
@@ -202,6 +224,7 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                                                           const __grid_constant__ CUtensorMap vsmap,
                                                           const __grid_constant__ CUtensorMap ktmap,
                                                           const __grid_constant__ CUtensorMap vtmap,
+                                                          const __grid_constant__ LeanTok tk,
                                                           const AttnParams P) {
     using C = LeanCfg<HD, KVT, NQ>;
     using S = AttendShape<HD, HD, KVT, NQ>;
@@ -286,7 +309,8 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                 uint32_t x = U.start(u);
                 const uint32_t xe = U.start(u + 1);
                 LeanWalk w;
-                w.init(P, u);
+                if (tk.n) w.init_at(tk.tok, tk.n, x);
+                else w.init(P, u);
                 while (x < xe && !*abort_flag) {
                     const uint32_t nt = min(xe - x, w.T - w.kt), i = seg % SQ;
                     if (seg >= SQ && !mbar_wait(&slot_free[i], ((seg / SQ) - 1) & 1, abort_flag)) break;

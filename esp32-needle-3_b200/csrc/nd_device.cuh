@@ -101,6 +101,17 @@ struct AttnParams {
     int *err;                    // status word in mapped pinned host memory (0 = ok)
 };
 
+// Balanced decode of a call of at most kLeanParamTok tokens: the plan's token
+// table travels as a kernel parameter, so no host-to-device copy sits between
+// consecutive launches.
+constexpr int kLeanParamTok = 128;
+struct LeanTok {
+    uint32_t n;                       // tokens in tok; 0: the plan is in global memory
+    uint32_t pad[3];
+    uint4 tok[kLeanParamTok + 1];     // per token {first tile, tiles per item, sequence, position};
+                                      //   entry n: {tiles of the call, 0, 0, 0}
+};
+
 // ---------------------------------------------------------------- helpers
 // The status word is host memory mapped into the device's address space, so
 // the host reads it after a stream sync with no copy. A plain store: any

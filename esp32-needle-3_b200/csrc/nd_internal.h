@@ -29,8 +29,8 @@ int attend_rows_per_iter(int kv_dt, int vd, int nq);
     cudaError_t append_launch_##SUF(int qk, int vd, const AttnParams &P, cudaStream_t s);                \
     cudaError_t attend_lean_launch_##SUF(int hd, int nq, const void *kmap, const void *vmap,            \
                                          const void *ksmap, const void *vsmap, const void *ktmap,        \
-                                         const void *vtmap, const AttnParams &P, int *blocks_per_sm,     \
-                                         cudaStream_t s);
+                                         const void *vtmap, const LeanTok *tk, const AttnParams &P,      \
+                                         int *blocks_per_sm, cudaStream_t s);
 ND_DECLARE_KV(i8)
 ND_DECLARE_KV(f32)
 ND_DECLARE_KV(f16)

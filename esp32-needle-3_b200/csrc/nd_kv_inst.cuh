@@ -60,11 +60,14 @@ cudaError_t append_launch_t(int qk, int vd, const AttnParams &P, cudaStream_t s)
 // the instantiation one SM holds (no launch); the host asks once per handle
 // and instantiation before the first launch. ksmap / vsmap: the int8 scale
 // maps (16-bit instantiations take any valid map and ignore it); ktmap /
-// vtmap: the same rows as kmap / vmap in 16-row boxes (item tails).
+// vtmap: the same rows as kmap / vmap in 16-row boxes (item tails); tk: the
+// call's tokens when they travel as parameters (LeanTok::n = 0 otherwise).
+static_assert(6 * sizeof(CUtensorMap) + sizeof(LeanTok) + sizeof(AttnParams) <= 4096,
+              "balanced kernel parameters fit the 4 KB parameter space");
 template <typename KVT>
 cudaError_t attend_lean_launch_t(int hd, int nq, const void *kmap, const void *vmap, const void *ksmap,
-                                 const void *vsmap, const void *ktmap, const void *vtmap, const AttnParams &P,
-                                 int *blocks_per_sm, cudaStream_t s) {
+                                 const void *vsmap, const void *ktmap, const void *vtmap, const LeanTok *tk,
+                                 const AttnParams &P, int *blocks_per_sm, cudaStream_t s) {
     if constexpr (KvT<KVT>::dt == DT_F16 || KvT<KVT>::dt == DT_BF16 || KvT<KVT>::dt == DT_I8) {
 #define ND_CASE(H, N)                                                                                   \
         if (hd == H && nq == N) {                                                                       \
@@ -92,7 +95,7 @@ cudaError_t attend_lean_launch_t(int hd, int nq, const void *kmap, const void *v
                                       *static_cast<const CUtensorMap *>(ksmap),                         \
                                       *static_cast<const CUtensorMap *>(vsmap),                         \
                                       *static_cast<const CUtensorMap *>(ktmap),                         \
-                                      *static_cast<const CUtensorMap *>(vtmap), P);                     \
+                                      *static_cast<const CUtensorMap *>(vtmap), *tk, P);                \
         }
         if constexpr (KvT<KVT>::dt == DT_I8) {
             // int8: query groups of one or two rows (wider groups would cost
@@ -120,8 +123,8 @@ cudaError_t attend_lean_launch_t(int hd, int nq, const void *kmap, const void *v
     }                                                                                           \
     cudaError_t attend_lean_launch_##SUF(int hd, int nq, const void *kmap, const void *vmap,    \
                                          const void *ksmap, const void *vsmap, const void *ktmap,  \
-                                         const void *vtmap, const AttnParams &P, int *blocks_per_sm, \
-                                         cudaStream_t s) {                                      \
-        return attend_lean_launch_t<KVT>(hd, nq, kmap, vmap, ksmap, vsmap, ktmap, vtmap, P, blocks_per_sm, s); \
+                                         const void *vtmap, const LeanTok *tk, const AttnParams &P, \
+                                         int *blocks_per_sm, cudaStream_t s) {                  \
+        return attend_lean_launch_t<KVT>(hd, nq, kmap, vmap, ksmap, vsmap, ktmap, vtmap, tk, P, blocks_per_sm, s); \
     }                                                                                           \
     }
