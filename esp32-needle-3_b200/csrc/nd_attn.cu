@@ -561,9 +561,11 @@ bool lean_ok(const nd_attn *h, bool no_wrap) {
            (cf.block_size == 0 || cf.block_size % (uint32_t)nda::kTmaRows == 0) && h->rows_per_layer < 0x7fffffffu;
 }
 
-// Balanced-launch tuning: share of the tiles in static units (percent), least
-// tiles per dynamic unit, dynamic units a producer holds ahead.
-constexpr uint64_t kLeanStaticPct = 75, kLeanUnitMin = 2;
+// Balanced-launch tuning: share of the tiles in static units (percent; 16-bit
+// and int8 caches), least tiles per dynamic unit, dynamic units a producer
+// holds ahead. Config-2 decode swept over 50-90 %: 16-bit caches run fastest
+// at 60-65 % (245k tok/s against 240k at 75 %), int8 caches at 75 %.
+constexpr uint64_t kLeanStaticPct16 = 65, kLeanStaticPctI8 = 75, kLeanUnitMin = 2;
 constexpr uint32_t kLeanAhead = 2;
 
 // Builds the balanced-launch plan of a call into h->lean_up: per token
@@ -579,7 +581,8 @@ void lean_geometry(nd_attn *h, uint64_t nt, int occ) {
     const size_t cnt_half = h->counter_cap / 2, slot_half = h->part_slots / 2;
     const uint64_t budget = std::min<uint64_t>(cnt_half - 2, slot_half / 2);
     const uint64_t G = std::min<uint64_t>({nt, (uint64_t)h->sm_count * (uint64_t)occ, budget});
-    const uint64_t S = std::max<uint64_t>(1, nt * kLeanStaticPct / (100 * G));
+    const uint64_t pct = h->cfg.kv_dtype == ND_DT_I8 ? kLeanStaticPctI8 : kLeanStaticPct16;
+    const uint64_t S = std::max<uint64_t>(1, nt * pct / (100 * G));
     const uint64_t dyn = nt - G * S;
     uint64_t CH = std::max<uint64_t>(kLeanUnitMin, (dyn + 4 * G - 1) / (4 * G));
     while (G + (dyn + CH - 1) / CH > budget) CH *= 2;
@@ -628,7 +631,7 @@ int build_lean_plan(nd_attn *h, uint32_t ntok, const std::vector<uint32_t> &vis,
 // Balanced launch: item (t, g) holds T_t = max(1, ceil((vis[t] - fuse_append)
 // / 64)) tiles (the newest row of a fused append is not in the TMA stream).
 // G = the CTAs the GPU holds at once; the NT tiles of the call become G
-// static units of S ~ 3/4 NT / G tiles, then dynamic units of CH tiles (at
+// static units of S ~ 0.65 NT / G tiles (0.75 for int8 caches), then dynamic units of CH tiles (at
 // most ~4 per CTA) that CTAs take as they run dry. Each unit needs two
 // partial slots and one ticket; two more counters drive the unit queue.
 int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, const nda::SeqSpan *d_spans,
