@@ -211,11 +211,15 @@ ND_ATTN_API int  nd_attn_prefill_host(nd_attn *h, uint32_t layer, uint32_t n, co
  * and nothing is launched; when the partial results of the chosen split would
  * not fit, fewer splits are used (never more memory).
  * The first call on a device looks up the array's device address (with that
- * device current); make that first call before any stream capture.
+ * device current); make that first call before any stream capture. The
+ * address is kept for the life of the process: after cudaDeviceReset (or any
+ * other teardown of the device's primary context) this entry point must not be
+ * called on that device again.
  * Every call on a device shares the one array: calls that can run at the same
  * time on the GPU (two handles on different streams) race and must be
  * serialised by the caller. The array keeps the previous call's contents; the
- * tickets are cleared on the handle's stream at the start of every call. */
+ * merge tickets are cleared on the handle's stream at the start of every call
+ * that splits (a call without splits does not use them). */
 #define ND_ATTN_NOALLOC_SCRATCH_BYTES (8u << 20)
 #define ND_ATTN_NOALLOC_MAX_ITEMS     16384u
 ND_ATTN_API int  nd_attn_decode_noalloc(nd_attn *h, uint32_t layer, uint32_t n, const void *q,

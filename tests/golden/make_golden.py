@@ -5,7 +5,7 @@ Run from the repository root where the reference sources are present:
     python tests/golden/make_golden.py
 
 Fixtures (inputs are regenerated from the seeds, so only outputs are stored):
-  config1_int8.npz  BASELINE config 1: one sequence, 213-token prefix pinned as
+  config1_int8.npz  config 1 of the benchmark set: one sequence, 213-token prefix pinned as
                     sinks (nd_model_set_sink), 40-token suffix, 32 decode steps;
                     8 q / 8 kv heads x 64, theta 1e4, q/k/v ~ N(0,1)*0.5 seed 0,
                     no gate. The reference's only KV format is int8.
