@@ -306,8 +306,10 @@ def run_decode(args, world, rank, local, dist):
     with Clocks(local) as clk:
         torch.cuda.nvtx.range_push("timed")
         t0.record(stream)
+        h0 = time.perf_counter()
         for i in range(K):
             step(Wm + i)
+        host_s = time.perf_counter() - h0
         t1.record(stream)
         torch.cuda.nvtx.range_pop()
         a.sync()
@@ -394,6 +396,7 @@ def run_decode(args, world, rank, local, dist):
                 "h2d_bytes_per_step": int(LAYERS * BATCH * (H * QK + HKV * QK + HKV * VD) * 2),
                 "d2h_bytes_per_step": int(LAYERS * BATCH * H * VD * 2)},
         "gpu_launches": int(launches), "clocks": clk.summary(),
+        "host_enqueue_us_per_layer": host_s * 1e6 / (K * LAYERS),
     }
 
 
@@ -555,9 +558,11 @@ def run_decode_taps(args, world, rank, local, dist, plain_value):
 
 def run_decode_heads(args, world, rank, local, dist):
     """Config 2 head-sharded over the ranks (strong scaling): every rank holds
-    all 64 sequences (contexts of seed 1) for its H/world KV heads; per layer it
-    decodes its heads, then one NCCL all-gather (on the handle's stream) puts
-    out[64, 8, 64] together on every rank."""
+    all 64 sequences (contexts of seed 1) for its H/world KV heads; per layer
+    the gathered decode (nd_attn_decode_gather) computes the rank's heads and
+    its attention kernel stores each output row into every rank's gather
+    buffer over NVLink, so out[64, 8, 64] is complete on every rank after a
+    short wait-and-copy kernel (no collective library call, no permute)."""
     import torch
 
     import ndshard
@@ -586,7 +591,7 @@ def run_decode_heads(args, world, rank, local, dist):
     q = torch.randn((nsteps, LAYERS, BATCH, hq * QK), generator=gen, device="cuda").half()
     k = (torch.randn((nsteps, LAYERS, BATCH, hkv * QK), generator=gen, device="cuda") * 0.5).half()
     v = (torch.randn((nsteps, LAYERS, BATCH, hkv * VD), generator=gen, device="cuda") * 0.5).half()
-    out = torch.empty((LAYERS, BATCH, hq * VD), dtype=torch.float16, device="cuda")
+    out = torch.empty((LAYERS, BATCH, H * VD), dtype=torch.float16, device="cuda")
 
     def step(i):
         for l in range(LAYERS):
@@ -596,24 +601,34 @@ def run_decode_heads(args, world, rank, local, dist):
     for i in range(Wm):
         step(i)
     a.sync()
-    dist.barrier()
+    if world > 1:
+        dist.barrier()
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
+    h0 = time.perf_counter()
     for i in range(K):
         step(Wm + i)
+    host_s = time.perf_counter() - h0
     t1.record(stream)
     a.sync()
-    dist.barrier()
+    if world > 1:
+        dist.barrier()
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1)
+    launches = a.launches
     sh.close()
     times = torch.tensor([ms], device="cuda", dtype=torch.float64)
-    dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
     ms = float(times[0])
     return {"value": BATCH * K / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms / K, "scaling": "strong",
-            "parallelism": f"head-sharded x{world}: {hkv} KV heads per GPU, NCCL all-gather of out per layer",
-            "allgather_bytes_per_layer": BATCH * H * VD * 2}
+            "parallelism": f"head-sharded x{world}: {hkv} KV heads per GPU; each rank's attention kernel stores "
+                           f"its output rows into every rank's gather buffer over NVLink (peer stores), then a "
+                           f"wait-and-copy kernel per layer",
+            "gathered_bytes_per_layer": BATCH * H * VD * 2, "gpu_launches_total": int(launches),
+            "host_enqueue_us_per_layer": host_s * 1e6 / (K * LAYERS),
+            "note": "N=1 is the same gathered path with one rank (all heads, gather to itself)"}
 
 
 # ------------------------------------------------------------ GPU: shared-prefix serving
@@ -920,7 +935,7 @@ def run_ours(args):
         dec = run_decode(args, world, rank, local, dist)
         taps = run_decode_taps(args, world, rank, local, dist, dec["value"])
         i8 = run_decode_int8(args, world, rank, local, dist)
-        heads = run_decode_heads(args, world, rank, local, dist) if world > 1 and HKV % world == 0 else None
+        heads = run_decode_heads(args, world, rank, local, dist) if HKV % world == 0 else None
         pre = run_prefill(args, world, rank, local, dist) if args.prefill_steps > 0 else None
         lng = run_long(args, world, rank, local, dist) if args.long_steps > 0 else None
         srv = run_serve(args, world, rank, local, dist) if args.serve else None

@@ -320,6 +320,17 @@ struct nd_attn {
     size_t work_cap = 0;
     std::vector<uint32_t> work_key;
     uint32_t n_work = 0;
+    // Head-sharded decode over g_world ranks (nd_attn_gather_init / _attach).
+    // g_buf = this rank's gather buffer, two slots of 8-byte {data, epoch}
+    // words that gathered calls alternate between; g_peer[p] = rank p's
+    // buffer as mapped here (own included); g_words = words per gathered row.
+    uint32_t g_world = 0, g_rank = 0, g_words = 0;
+    char *g_buf = nullptr;
+    size_t g_slot_bytes = 0;
+    char *g_peer[nda::kMaxGather] = {};
+    bool g_ready = false;
+    uint32_t g_epoch = 0;
+    nda::GatherView gth_call{};   // in force for the attend launch of a gathered call (G = 0 otherwise)
 };
 
 namespace {
@@ -402,6 +413,7 @@ AttnParams base_params(nd_attn *h, uint32_t layer) {
     P.part_ml = h->part_ml;
     P.counters = h->counters;
     P.err = h->d_err;
+    P.gth = h->gth_call;
     return P;
 }
 
@@ -1173,6 +1185,9 @@ void nd_attn_close(nd_attn *h) {
     if (h->hstage) cudaFreeHost(h->hstage);
     if (h->err_host) cudaFreeHost(h->err_host);
     if (h->own) cudaStreamDestroy(h->own);
+    for (uint32_t p = 0; p < h->g_world; p++)
+        if (h->g_peer[p] && h->g_peer[p] != h->g_buf) cudaIpcCloseMemHandle(h->g_peer[p]);
+    cudaFree(h->g_buf);
     delete h;
 }
 
@@ -1896,6 +1911,212 @@ const char *nd_attn_version(void) {
     static char buf[64];
     if (!buf[0]) snprintf(buf, sizeof(buf), "nd_attn 0.1 sm_100a cudart %d", CUDART_VERSION);
     return buf;
+}
+
+}  // extern "C"
+
+// ============================================================ head-sharded decode
+namespace {
+
+constexpr uint32_t kGatherMagic = 0x4147444eu;   // "NDGA"
+constexpr uint32_t kGatherVersion = 2;
+
+// The record one rank hands to every other rank (ND_ATTN_GATHER_BLOB_BYTES).
+struct GatherBlob {
+    uint32_t magic, version, rank, world;
+    uint32_t max_tokens, row_words;   // gathered row: 8-byte words of {4 data bytes, epoch}
+    uint64_t slot_bytes;
+    uint32_t out_dtype, pad0;
+    uint8_t uuid[16];   // the rank's GPU (cudaDeviceProp::uuid)
+    uint8_t ipc[64];    // cudaIpcMemHandle_t of the rank's gather buffer
+    uint8_t pad1[8];
+};
+static_assert(sizeof(GatherBlob) == ND_ATTN_GATHER_BLOB_BYTES, "gather blob layout");
+static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+
+// Ends a gathered call on this rank: copies the data half of every word of
+// this rank's slot to `out` once the word carries the call's epoch (each
+// word is one 64-bit store of some rank's attend kernel, so a word with the
+// epoch is complete), polling with a bounded wait (~2 s; on expiry status 3,
+// ND_ATTN_ERR_TIMEOUT). Launched as a programmatic dependent of the attend
+// launch, it lets the next launch start at once and copies rows as they
+// arrive, while the attend launch still runs; it waits for that launch to
+// complete only at its end, so its own completion implies that launch's.
+// n_words is even and `out` 8-byte aligned.
+__global__ void gather_wait_kernel(const unsigned long long *slot, uint2 *out, size_t n_words, uint32_t epoch,
+                                   int *err) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const long long t0 = clock64();
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_words / 2; i += stride) {
+        unsigned long long a, b;
+        for (;;) {
+            asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(slot + 2 * i) : "memory");
+            if ((uint32_t)(a >> 32) == epoch && (uint32_t)(b >> 32) == epoch) break;
+            if (clock64() - t0 > nda::kTimeoutCycles) {
+                nda::set_err(err, 3);
+                i = n_words;   // stop this thread
+                break;
+            }
+            __nanosleep(64);
+        }
+        if (i < n_words / 2) out[i] = make_uint2((uint32_t)a, (uint32_t)b);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+int gather_check(const GatherBlob *b, uint32_t world, uint32_t rank) {
+    if (world < 1 || world > (uint32_t)nda::kMaxGather)
+        return fail(ND_ATTN_ERR_ARG, "world %u outside [1, %d]", world, nda::kMaxGather);
+    if (rank >= world) return fail(ND_ATTN_ERR_ARG, "rank %u >= world %u", rank, world);
+    static const uint8_t zero[16] = {0};
+    for (uint32_t i = 0; i < world; i++) {
+        if (b[i].magic != kGatherMagic || b[i].version != kGatherVersion)
+            return fail(ND_ATTN_ERR_ARG, "record %u is not a gather record of this library version", i);
+        if (b[i].rank != i || b[i].world != world)
+            return fail(ND_ATTN_ERR_ARG, "record %u comes from rank %u of %u (records must be in rank order)", i,
+                        b[i].rank, b[i].world);
+        if (b[i].max_tokens != b[0].max_tokens || b[i].row_words != b[0].row_words ||
+            b[i].slot_bytes != b[0].slot_bytes || b[i].out_dtype != b[0].out_dtype)
+            return fail(ND_ATTN_ERR_ARG, "rank %u's handle has another geometry than rank 0's", i);
+        for (uint32_t j = 0; j < i; j++)
+            if (memcmp(b[i].uuid, zero, 16) && !memcmp(b[i].uuid, b[j].uuid, 16))
+                return fail(ND_ATTN_ERR_ARG, "ranks %u and %u share one GPU (one rank per GPU is required: the "
+                            "ranks' kernels wait for one another)", j, i);
+    }
+    return ND_ATTN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int nd_attn_gather_check(const void *blobs, uint32_t world, uint32_t rank) {
+    if (!blobs) return fail(ND_ATTN_ERR_ARG, "null records");
+    return gather_check(static_cast<const GatherBlob *>(blobs), world, rank);
+}
+
+int nd_attn_gather_init(nd_attn *h, uint32_t rank, uint32_t world, void *blob) {
+    if (!h || !blob) return fail(ND_ATTN_ERR_ARG, "null argument");
+    if (h->g_world) return fail(ND_ATTN_ERR_ARG, "the handle is already set up for a gather");
+    if (world < 1 || world > (uint32_t)nda::kMaxGather || rank >= world)
+        return fail(ND_ATTN_ERR_ARG, "rank %u of world %u (world at most %d)", rank, world, nda::kMaxGather);
+    const nd_attn_config &c = h->cfg;
+    DeviceGuard dg(c.device);
+    // A word carries one f32 or two 16-bit output elements.
+    const size_t elems = (size_t)world * c.n_heads * c.v_head_dim;
+    const size_t words = c.out_dtype == ND_DT_F32 ? elems : elems / 2;
+    const size_t slot_bytes = ((size_t)c.max_seqs * words * 8 + 255) / 256 * 256;
+    if (words > 0x7fffffffu) return fail(ND_ATTN_ERR_RANGE, "gathered row too large");
+    if (cudaMalloc(&h->g_buf, 2 * slot_bytes) != cudaSuccess) {
+        cudaGetLastError();
+        h->g_buf = nullptr;
+        return fail(ND_ATTN_ERR_NOMEM, "gather buffer of %zu bytes", 2 * slot_bytes);
+    }
+    ND_CUDA(cudaMemset(h->g_buf, 0, 2 * slot_bytes));   // epoch 0 is never used
+    GatherBlob b;
+    memset(&b, 0, sizeof(b));
+    b.magic = kGatherMagic;
+    b.version = kGatherVersion;
+    b.rank = rank;
+    b.world = world;
+    b.max_tokens = c.max_seqs;
+    b.row_words = (uint32_t)words;
+    b.slot_bytes = slot_bytes;
+    b.out_dtype = (uint32_t)c.out_dtype;
+    cudaDeviceProp prop;
+    ND_CUDA(cudaGetDeviceProperties(&prop, c.device));
+    memcpy(b.uuid, &prop.uuid, 16);
+    cudaIpcMemHandle_t ipc;
+    ND_CUDA(cudaIpcGetMemHandle(&ipc, h->g_buf));
+    memcpy(b.ipc, &ipc, 64);
+    memcpy(blob, &b, sizeof(b));
+    h->g_world = world;
+    h->g_rank = rank;
+    h->g_words = (uint32_t)words;
+    h->g_slot_bytes = slot_bytes;
+    return ND_ATTN_OK;
+}
+
+int nd_attn_gather_attach(nd_attn *h, const void *blobs) {
+    if (!h || !blobs) return fail(ND_ATTN_ERR_ARG, "null argument");
+    if (!h->g_world) return fail(ND_ATTN_ERR_ARG, "nd_attn_gather_init has not run on this handle");
+    if (h->g_ready) return fail(ND_ATTN_ERR_ARG, "the handle is already attached");
+    const GatherBlob *b = static_cast<const GatherBlob *>(blobs);
+    int rc = gather_check(b, h->g_world, h->g_rank);
+    if (rc) return rc;
+    if (b[0].row_words != h->g_words || b[0].slot_bytes != h->g_slot_bytes ||
+        b[0].out_dtype != (uint32_t)h->cfg.out_dtype)
+        return fail(ND_ATTN_ERR_ARG, "the records' geometry differs from this handle's");
+    DeviceGuard dg(h->cfg.device);
+    for (uint32_t p = 0; p < h->g_world; p++) {
+        if (p == h->g_rank) {
+            h->g_peer[p] = h->g_buf;
+            continue;
+        }
+        cudaIpcMemHandle_t ipc;
+        memcpy(&ipc, b[p].ipc, 64);
+        void *ptr = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&ptr, ipc, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (uint32_t q = 0; q < p; q++)
+                if (q != h->g_rank && h->g_peer[q]) cudaIpcCloseMemHandle(h->g_peer[q]);
+            memset(h->g_peer, 0, sizeof(h->g_peer));
+            return fail(ND_ATTN_ERR_CUDA, "cudaIpcOpenMemHandle of rank %u's buffer: %s", p, cudaGetErrorString(e));
+        }
+        h->g_peer[p] = static_cast<char *>(ptr);
+    }
+    h->g_ready = true;
+    return ND_ATTN_OK;
+}
+
+int nd_attn_decode_gather(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const void *q,
+                          const void *k, const void *v, const void *gate, void *out) {
+    if (!h) return fail(ND_ATTN_ERR_ARG, "null handle");
+    if (!h->g_ready) return fail(ND_ATTN_ERR_ARG, "nd_attn_gather_attach has not run on this handle");
+    if (!out) return fail(ND_ATTN_ERR_ARG, "null tensor");
+    if (reinterpret_cast<uintptr_t>(out) & 7u) return fail(ND_ATTN_ERR_ARG, "out must be 8-byte aligned");
+    if (n > h->cfg.max_seqs) return fail(ND_ATTN_ERR_RANGE, "%u sequences (max %u)", n, h->cfg.max_seqs);
+    DeviceGuard dg(h->cfg.device);
+    // Every rank numbers its gathered calls alike: 1, 2, ... (0 skipped at the
+    // wrap; the slots alternate by the number's parity).
+    const uint32_t prev = h->g_epoch;
+    h->g_epoch = prev + 1 ? prev + 1 : 1;
+    const uint32_t epoch = h->g_epoch, slot = epoch & 1u;
+    nda::GatherView g{};
+    g.G = h->g_world;
+    g.col0 = h->g_rank * h->cfg.n_heads * h->cfg.v_head_dim;
+    g.row_elems = h->g_world * h->cfg.n_heads * h->cfg.v_head_dim;
+    g.epoch = epoch;
+    for (uint32_t p = 0; p < h->g_world; p++)
+        g.slot[p] = reinterpret_cast<unsigned long long *>(h->g_peer[p] + slot * h->g_slot_bytes);
+    h->gth_call = g;
+    int rc = nd_attn_decode(h, layer, n, seq_ids, q, k, v, gate, out);
+    h->gth_call = nda::GatherView{};
+    if (rc) {
+        h->g_epoch = prev;   // refused before its attend launch: the ranks' call numbers stay equal
+        return rc;
+    }
+    // The wait-and-copy kernel, a programmatic dependent of the attend launch
+    // (which may still be writing this layer's cache, so the writer record is
+    // left as it is).
+    const size_t n_words = (size_t)n * h->g_words;
+    const unsigned threads = 256;
+    const unsigned blocks = (unsigned)std::max<size_t>(
+        1, std::min<size_t>((n_words / 2 + threads - 1) / threads, (size_t)h->sm_count));
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(blocks);
+    lc.blockDim = dim3(threads);
+    lc.stream = h->stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    const unsigned long long *own = reinterpret_cast<const unsigned long long *>(h->g_buf + slot * h->g_slot_bytes);
+    ND_CUDA(cudaLaunchKernelEx(&lc, gather_wait_kernel, own, static_cast<uint2 *>(out), n_words, epoch, h->d_err));
+    h->launches++;
+    return ND_ATTN_OK;
 }
 
 }  // extern "C"

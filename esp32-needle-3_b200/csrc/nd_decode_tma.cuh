@@ -196,13 +196,14 @@ __device__ __forceinline__ void lean_merge_row(const AttnParams &P, const LeanUn
         }
         M = Mn;
     }
-    const size_t ob = ((size_t)row * P.n_heads + g * P.rep + qi) * HD + lane;
+    const uint32_t col = (g * P.rep + qi) * HD + lane;
+    const size_t ob = (size_t)row * P.n_heads * HD + col;
     const float inv = 1.0f / L;
 #pragma unroll
     for (int c = 0; c < EPL; c++) {
         float val = o[c] * inv;
         if (P.gate) val *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, ob + 32 * c) * 1.4426950408889634f));
-        act_store(P.out, P.out_dt, ob + 32 * c, val);
+        out_store<HD>(P, row, col + 32 * c, val);
     }
 }
 
@@ -523,7 +524,7 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                     if (P.gate)
                         val *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, (out_base + h) * HD + e) *
                                                   1.4426950408889634f));
-                    act_store(P.out, P.out_dt, (out_base + h) * HD + e, val);
+                    out_store<HD>(P, row, h * HD + e, val);
                 } else {
                     P.part_o[((size_t)slot * NQ + qi) * HD + e] = o;
                     if (e == 0) {

@@ -71,9 +71,24 @@ __device__ __forceinline__ bool bf16x2_big(uint32_t w) {
     return (w & 0x7f80u) >= 0x4780u || (w & 0x7f800000u) >= 0x47800000u;
 }
 
+// Head-sharded decode (G ranks, one GPU each, every rank holding the same
+// sequences for its own KV heads): the attend kernels store each output row
+// straight into this call's gather slot on every rank (peer memory over
+// NVLink, the own rank included), rows of row_elems elements with this rank's
+// heads at column col0. The slot holds 8-byte words {4 bytes of output (one
+// f32 or two 16-bit elements), the call's epoch}, each written by one 64-bit
+// store, so a reader knows a word has arrived when it carries the epoch: no
+// fence and no flag are needed. G = 0: plain output to out.
+constexpr int kMaxGather = 8;
+struct GatherView {
+    unsigned long long *slot[kMaxGather];    // this call's slot in rank p's gather buffer
+    uint32_t G, col0, row_elems, epoch;
+};
+
 struct AttnParams {
     const void *q, *k, *v, *gate;
     void *out;
+    GatherView gth;
     int act_dt, out_dt;
     CacheView c;
     const float2 *rope;          // [max_pos][qk_hd/2] (cos, sin)
@@ -134,6 +149,43 @@ __device__ __forceinline__ void act_store(void *p, int dt, size_t i, float x) {
     if (dt == DT_F32) static_cast<float *>(p)[i] = x;
     else if (dt == DT_F16) static_cast<__half *>(p)[i] = __float2half_rn(x);
     else static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(x);
+}
+
+// Output element (row, col) of a call, col = head * VD + d over this
+// launch's heads: into out, or (head-sharded) into every rank's gather slot
+// at the rank's column offset. Head-sharded with 16-bit outputs, the whole
+// warp calls this together with consecutive cols in consecutive lanes (col
+// parity = lane parity): the even lane stores the pair. Static indices over
+// the rank list keep the parameter array out of local memory.
+template <int VD>
+__device__ __forceinline__ void out_store(const AttnParams &P, size_t row, uint32_t col, float x) {
+    if (P.gth.G == 0) {
+        act_store(P.out, P.out_dt, row * P.n_heads * VD + col, x);
+        return;
+    }
+    const size_t e = row * P.gth.row_elems + P.gth.col0 + col;   // element of the gathered rows
+    uint32_t data;
+    size_t wi;
+    if (P.out_dt == DT_F32) {
+        data = __float_as_uint(x);
+        wi = e;
+    } else {
+        const float y = __shfl_xor_sync(0xffffffffu, x, 1);
+        if (col & 1u) return;
+        if (P.out_dt == DT_F16) {
+            const __half2 t = __floats2half2_rn(x, y);
+            data = *reinterpret_cast<const uint32_t *>(&t);
+        } else {
+            const __nv_bfloat162 t = __floats2bfloat162_rn(x, y);
+            data = *reinterpret_cast<const uint32_t *>(&t);
+        }
+        wi = e >> 1;
+    }
+    const unsigned long long w = ((unsigned long long)P.gth.epoch << 32) | data;
+#pragma unroll
+    for (int p = 0; p < kMaxGather; p++)
+        if ((uint32_t)p < P.gth.G)
+            asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(P.gth.slot[p] + wi), "l"(w) : "memory");
 }
 
 __device__ __forceinline__ TokMeta token_meta(const AttnParams &P, uint32_t tok) {
@@ -696,7 +748,7 @@ __device__ __forceinline__ void attend_finish(const AttnParams &P, float (&m)[NQ
             float val = o / L;
             if (P.gate) val *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, (out_base + h) * VD + d) *
                                                  1.4426950408889634f));
-            act_store(P.out, P.out_dt, (out_base + h) * VD + d, val);
+            out_store<VD>(P, out_row, h * VD + d, val);
         } else {
             P.part_o[(part_base + qi) * VD + d] = o;
             if (d == 0) {
@@ -731,7 +783,7 @@ __device__ __forceinline__ void attend_finish(const AttnParams &P, float (&m)[NQ
         float val = o / L;
         if (P.gate) val *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, (out_base + h) * VD + d) *
                                              1.4426950408889634f));
-        act_store(P.out, P.out_dt, (out_base + h) * VD + d, val);
+        out_store<VD>(P, out_row, h * VD + d, val);
     }
     if (tid == 0) P.counters[item] = 0;
 }

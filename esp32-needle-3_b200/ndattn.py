@@ -32,6 +32,7 @@ DT_NAMES = {"i8": DT_I8, "int8": DT_I8, "f32": DT_F32, "float32": DT_F32, "f16":
             "float16": DT_F16, "bf16": DT_BF16, "bfloat16": DT_BF16}
 ERR_ARG, ERR_GEOM, ERR_NOMEM, ERR_CUDA, ERR_RANGE, ERR_TIMEOUT, ERR_NOGPU = -1, -10, -12, -14, -15, -16, -17
 NOALLOC_MAX_ITEMS = 16384            # ND_ATTN_NOALLOC_MAX_ITEMS
+GATHER_BLOB_BYTES = 128              # ND_ATTN_GATHER_BLOB_BYTES
 
 
 class NdAttnError(RuntimeError):
@@ -84,6 +85,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "nd_attn_prefill": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp, vp, vp]),
         "nd_attn_decode_host": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp, vp]),
         "nd_attn_decode_noalloc": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp]),
+        "nd_attn_gather_check": (c_int, [vp, u32, u32]),
+        "nd_attn_gather_init": (c_int, [vp, u32, u32, vp]),
+        "nd_attn_gather_attach": (c_int, [vp, vp]),
+        "nd_attn_decode_gather": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp, vp]),
         "nd_attn_prefill_host": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp, vp, vp]),
         "nd_attn_prefix_save": (vp, [vp, u32]),
         "nd_attn_prefix_restore": (c_int, [vp, u32, vp]),
@@ -106,6 +111,15 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         fn.argtypes = args
     _lib = lib
     return lib
+
+
+def gather_check(records: bytes, world: int, rank: int) -> None:
+    """Validates the rank-ordered gather records of `world` ranks on the host
+    alone (nd_attn_gather_check); raises NdAttnError when they do not fit."""
+    buf = np.frombuffer(records, dtype=np.uint8).copy()
+    if buf.size != world * GATHER_BLOB_BYTES:
+        raise NdAttnError(ERR_ARG, f"{buf.size} bytes of records for {world} ranks")
+    _check(load().nd_attn_gather_check(buf.ctypes.data, world, rank))
 
 
 def _check(rc: int) -> int:
@@ -258,6 +272,27 @@ class Attn:
         """nd_attn_decode for sequences 0..n-1 with its scratch in the library's
         fixed device array (no device allocation by the call)."""
         _check(load().nd_attn_decode_noalloc(self.h, layer, n, _ptr(q), _ptr(k), _ptr(v), _ptr(gate), _ptr(out)))
+
+    # ---- head-sharded decode (one rank per GPU)
+    def gather_init(self, rank: int, world: int) -> bytes:
+        """Allocates this rank's gather buffer; returns the record the other
+        ranks need (nd_attn_gather_init)."""
+        rec = np.zeros(GATHER_BLOB_BYTES, dtype=np.uint8)
+        _check(load().nd_attn_gather_init(self.h, rank, world, rec.ctypes.data))
+        return rec.tobytes()
+
+    def gather_attach(self, records: bytes) -> None:
+        """Maps the other ranks' buffers from the records of all ranks, in rank
+        order (nd_attn_gather_attach)."""
+        buf = np.frombuffer(records, dtype=np.uint8).copy()
+        _check(load().nd_attn_gather_attach(self.h, buf.ctypes.data))
+
+    def decode_gather(self, layer, n, q, k, v, out, gate=None, seq_ids=None) -> None:
+        """nd_attn_decode over this rank's heads, with every rank's heads
+        gathered into out [n, world * n_heads * v_head_dim]."""
+        ids = _u32(seq_ids)
+        _check(load().nd_attn_decode_gather(self.h, layer, n, _hptr(ids), _ptr(q), _ptr(k), _ptr(v), _ptr(gate),
+                                            _ptr(out)))
 
     # ---- hot path (host arrays)
     def decode_host(self, layer, n, q, k, v, out, gate=None, seq_ids=None) -> None:

@@ -7,14 +7,21 @@ needs no collective at all.
 
 Head sharding (the variant): every GPU holds all sequences but only a
 contiguous range of n_kv / G KV heads, with the query heads of those groups
-(GQA keeps a group on one GPU). Each GPU computes out[B, Hq/G, hd] for its
-heads; one all-gather per layer (NCCL over NVLink on GPUs, gloo on CPU) puts
-out[B, Hq, hd] together on every rank. The q/k/v a rank passes in are its own
-head slices, as a column-parallel projection produces them.
+(GQA keeps a group on one GPU). The library's gathered decode
+(nd_attn_decode_gather) computes the rank's heads and stores each output row
+straight into every rank's gather buffer from inside the attention kernel
+(peer stores over NVLink), so out[B, Hq, hd] is complete on every rank with no
+collective library call and no permute. The process group only carries the
+one-time exchange of the ranks' buffer records. The q/k/v a rank passes in are
+its own head slices, as a column-parallel projection produces them.
+gather_heads is the same gather written as a process-group all-gather: the
+layout reference for the CPU tests.
 
-A rank that fails before a collective makes the others' collective fail with
-the process group's timeout (an exception, not a hang); callers open the group
-with a short timeout for that reason.
+A rank that fails before a gathered call makes the others' call end with
+ND_ATTN_ERR_TIMEOUT (a bounded device wait), and a rank that fails before a
+process-group collective makes the others' collective fail with the group's
+timeout (an exception, not a hang); callers open the group with a short
+timeout for that reason.
 """
 from __future__ import annotations
 
@@ -64,25 +71,49 @@ def gather_heads(local_out, group=None):
     return buf.view(world, b, cols).permute(1, 0, 2).reshape(b, world * cols)
 
 
+def exchange_records(record: bytes, group=None) -> bytes:
+    """Every rank's gather record, concatenated in rank order: one all-gather
+    over the process group (a uint8 tensor; on the GPU for NCCL groups)."""
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" \
+        else torch.device("cpu")
+    mine = torch.tensor(list(record), dtype=torch.uint8, device=dev)
+    allr = torch.empty(world * len(record), dtype=torch.uint8, device=dev)
+    dist.all_gather_into_tensor(allr, mine, group=group)
+    return bytes(allr.cpu().numpy().tobytes())
+
+
 class HeadShardedAttn:
-    """An ndattn.Attn over this rank's KV heads, with decode/prefill whose output
-    is gathered over all ranks. Geometry arguments are those of the whole
-    model; q/k/v/gate passed in are this rank's head slices."""
+    """An ndattn.Attn over this rank's KV heads whose decode gathers every
+    rank's heads inside the library (nd_attn_decode_gather). Geometry arguments
+    are those of the whole model; q/k/v/gate passed in are this rank's head
+    slices. Construction and close() are collective over the group."""
 
     def __init__(self, rank: int, world: int, n_heads: int, n_kv_heads: int, group=None, **kw):
+        import torch.distributed as dist
+
         self.kv0, self.kv1, self.q0, self.q1 = head_range(n_heads, n_kv_heads, world, rank)
-        self.group = group
+        self.group, self.rank, self.world = group, rank, world
         self.attn = ndattn.Attn(n_heads=self.q1 - self.q0, n_kv_heads=self.kv1 - self.kv0, **kw)
+        rec = self.attn.gather_init(rank, world)
+        recs = exchange_records(rec, group) if world > 1 else rec
+        ndattn.gather_check(recs, world, rank)
+        self.attn.gather_attach(recs)
+        if world > 1:
+            dist.barrier(group)         # every rank mapped every buffer before the first call
 
-    def decode(self, layer, n, q, k, v, out_local, gate=None, seq_ids=None):
-        """Local decode into out_local [n, Hloc * vd]; returns the gathered
-        [n, Hq * vd]. The all-gather runs on the handle's stream, after the
-        kernel."""
-        import torch
-
-        self.attn.decode(layer, n, q, k, v, out_local, gate=gate, seq_ids=seq_ids)
-        with torch.cuda.stream(torch.cuda.ExternalStream(self.attn.stream)):
-            return gather_heads(out_local, self.group)
+    def decode(self, layer, n, q, k, v, out, gate=None, seq_ids=None):
+        """Decode of this rank's heads; out [n, Hq * vd] receives every rank's
+        heads (rank r's at columns [r * Hloc * vd, (r + 1) * Hloc * vd))."""
+        self.attn.decode_gather(layer, n, q, k, v, out, gate=gate, seq_ids=seq_ids)
 
     def close(self):
+        import torch.distributed as dist
+
+        self.attn.sync()
+        if self.world > 1:
+            dist.barrier(self.group)    # no rank still writes into another's buffer
         self.attn.close()

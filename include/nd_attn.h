@@ -225,6 +225,50 @@ ND_ATTN_API int  nd_attn_prefill_host(nd_attn *h, uint32_t layer, uint32_t n, co
 ND_ATTN_API int  nd_attn_decode_noalloc(nd_attn *h, uint32_t layer, uint32_t n, const void *q,
                                         const void *k, const void *v, const void *gate, void *out);
 
+/* ---- head-sharded decode over several GPUs ---------------------------------- */
+/* The reference splits attention by KV group across its two cores
+ * (attn_heads' head split, engine/src/nd_model.c:2125-2131); this is the same
+ * split across the GPUs of one box, one process (rank) per GPU. Every rank
+ * opens its handle with the geometry of ITS heads (n_heads / world query heads,
+ * n_kv_heads / world KV heads; rank r owns KV heads [r*n_kv/world,
+ * (r+1)*n_kv/world) and their query heads) and holds the same sequences at the
+ * same positions. A gathered decode computes the rank's heads and writes each
+ * output row straight into every rank's gather buffer (peer stores over
+ * NVLink, inside the attention kernel); every rank's `out` then holds all
+ * heads, [n][world * n_heads * v_head_dim] of out_dtype, rank r's heads at
+ * columns [r * n_heads * v_head_dim, (r + 1) * n_heads * v_head_dim).
+ *
+ * Set-up, collective over the ranks:
+ *  1. nd_attn_gather_init on every rank: allocates the rank's gather buffer
+ *     and fills its ND_ATTN_GATHER_BLOB_BYTES record (IPC handle, GPU id,
+ *     geometry);
+ *  2. the caller exchanges the records by any transport (MPI, a TCP store,
+ *     torch.distributed) into an array in rank order;
+ *  3. nd_attn_gather_attach on every rank with that array (maps the peers'
+ *     buffers), then a barrier across the ranks before the first gathered
+ *     decode.
+ * nd_attn_gather_check validates such an array on the host alone (no GPU):
+ * rank order, equal geometry, one GPU per rank.
+ *
+ * nd_attn_decode_gather: the arguments of nd_attn_decode (q/k/v/gate of the
+ * rank's heads, DEVICE pointers), `out` as above (8-byte aligned). Collective:
+ * every rank makes the same sequence of gathered calls with the same n.
+ * Returns after enqueueing, like nd_attn_decode. Each 8-byte word a kernel
+ * stores into a peer's buffer carries 4 bytes of output and the call's number,
+ * so no fence or flag is needed; a bounded device wait (~2 s) for the other
+ * ranks' words ends the call, and when it expires nd_attn_sync reports
+ * ND_ATTN_ERR_TIMEOUT (a rank that stopped or never made the call). One rank
+ * per GPU: the ranks' kernels wait for one another, so two ranks on one GPU
+ * are refused. Peers' buffers are released by nd_attn_close, which the ranks
+ * call after a final barrier. No counterpart in the reference engine. */
+#define ND_ATTN_GATHER_BLOB_BYTES 128u
+ND_ATTN_API int  nd_attn_gather_check(const void *records, uint32_t world, uint32_t rank);
+ND_ATTN_API int  nd_attn_gather_init(nd_attn *h, uint32_t rank, uint32_t world, void *record);
+ND_ATTN_API int  nd_attn_gather_attach(nd_attn *h, const void *records);
+ND_ATTN_API int  nd_attn_decode_gather(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids,
+                                       const void *q, const void *k, const void *v, const void *gate,
+                                       void *out);
+
 /* ---- schema-prefix KV ------------------------------------------------------ */
 /* nd_model_prefix_save (nd_model.c:1531-1541): requires a snapshot at the
  * current position; copies the live slots [0, min(snap_pos+1, window)) of

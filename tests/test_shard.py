@@ -138,3 +138,69 @@ def test_rank_failure_surfaces_as_error():
         msg = f.read()
     os.remove(path)
     assert msg.startswith("error"), msg
+
+
+# ------------------------------------------------ gathered decode: record exchange
+GATHER_MAGIC, GATHER_VERSION = 0x4147444E, 2
+
+
+def _record(rank, world, gpu_id, row_words=256, max_tokens=64, out_dtype=2):
+    """A gather record in the library's layout (the GatherBlob struct of
+    nd_attn.cu: 6 u32, u64 slot bytes, 2 u32, GPU uuid, IPC handle, padding)
+    with a fake IPC handle: what nd_attn_gather_init fills, for host-only
+    checks of the exchange and of nd_attn_gather_check."""
+    import struct
+    slot = (max_tokens * row_words * 8 + 255) // 256 * 256
+    head = struct.pack("<6IQ2I", GATHER_MAGIC, GATHER_VERSION, rank, world, max_tokens, row_words, slot, out_dtype,
+                       0)
+    return head + bytes([gpu_id] * 16) + bytes(64) + bytes(8)
+
+
+def _records_worker(rank, world, port, result_path):
+    sys.path[:0] = [HERE, os.path.join(HERE, "..", "esp32-needle-3_b200")]
+    import torch.distributed as dist
+
+    import ndattn
+    import ndshard as S
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    recs = S.exchange_records(_record(rank, world, 0x10 + rank))
+    try:
+        ndattn.gather_check(recs, world, rank)
+        msg = "ok"
+    except ndattn.NdAttnError as e:
+        msg = f"error {e.code}"
+    if recs[rank * ndattn.GATHER_BLOB_BYTES:(rank + 1) * ndattn.GATHER_BLOB_BYTES] != _record(rank, world, 0x10 + rank):
+        msg = "own record not at its rank's place"
+    with open(f"{result_path}.{rank}", "w") as f:
+        f.write(msg)
+    dist.destroy_process_group()
+
+
+def test_gather_records_exchange_and_check():
+    """The set-up of nd_attn_decode_gather on two gloo ranks: every rank's
+    record ends up at its rank's place in every rank's array, and the
+    library's host-side check accepts it; then the check refuses records out
+    of rank order, two ranks on one GPU, unequal geometry and a world size
+    that differs from the records'."""
+    import torch.multiprocessing as mp
+
+    import ndattn
+    path = os.path.join(os.environ.get("TMPDIR", "/tmp"), f"ndshard_rec_{os.getpid()}")
+    mp.start_processes(_records_worker, args=(2, _port(), path), nprocs=2, start_method="spawn")
+    for r in range(2):
+        with open(f"{path}.{r}") as f:
+            assert f.read() == "ok"
+        os.remove(f"{path}.{r}")
+    ndattn.gather_check(_record(0, 2, 1) + _record(1, 2, 2), 2, 1)
+    ndattn.gather_check(_record(0, 1, 1), 1, 0)
+    bad = [_record(1, 2, 2) + _record(0, 2, 1),                     # out of rank order
+           _record(0, 2, 1) + _record(1, 2, 1),                     # two ranks on one GPU
+           _record(0, 2, 1) + _record(1, 2, 2, row_words=512),      # another geometry
+           _record(0, 3, 1) + _record(1, 3, 2)]                     # records of a world of 3
+    for b in bad:
+        with pytest.raises(ndattn.NdAttnError) as e:
+            ndattn.gather_check(b, 2, 0)
+        assert e.value.code == ndattn.ERR_ARG
+    with pytest.raises(ndattn.NdAttnError):
+        ndattn.gather_check(_record(0, 2, 1) + _record(1, 2, 2), 2, 2)   # rank outside the world
