@@ -32,6 +32,19 @@ __device__ __forceinline__ bool mbar_test(uint64_t *b, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Non-blocking test of the same (test_wait never suspends the thread, where
+// try_wait may, up to a hardware time limit): for event loops that poll
+// several barriers.
+__device__ __forceinline__ bool mbar_ready(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 // Bounded wait for the phase of parity `parity`. False when the CTA is
 // aborting (another role timed out) or this wait timed out (then it raises
 // the abort itself).

@@ -215,7 +215,7 @@ __global__ void wait_expiry_kernel(int *err, long long limit) {
 // Copies whole cache rows between a (layer-strided) cache and a dense buffer:
 // dense row (l, r) <-> cache row phys_row(seq, slot0 + r) of layer l.
 // `to_cache` selects the direction. Row sizes are multiples of 4 bytes.
-// vbig: when copying into a bf16 V cache, the flag of the first layer copied
+// vbig: when copying into a bf16 K or V cache, the flag of the first layer copied
 // (layer blockIdx.y's flag is vbig[blockIdx.y]); nullptr otherwise.
 __global__ void rows_copy_kernel(char *cache, size_t layer_stride, char *dense, size_t dense_layer_stride,
                                  uint32_t row_words, uint32_t n_rows, CacheView c, uint32_t seq,
@@ -310,7 +310,7 @@ struct nd_attn {
     char *hstage = nullptr;       // host-buffer calls: pinned staging, mapped for the kernels
     char *hstage_dev = nullptr;   // its device address
     size_t hstage_cap = 0;
-    int *d_vbig = nullptr;    // per layer: a bf16 V value f16 cannot represent was stored (sticky)
+    int *d_vbig = nullptr;    // per layer: a bf16 K or V value f16 cannot represent was stored (sticky)
     void *dio = nullptr;
     size_t dio_cap = 0;
     uint64_t launches = 0;
@@ -1372,6 +1372,121 @@ int nd_attn_decode(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
                       no_wrap ? &tpos : nullptr);
 }
 
+}  // extern "C"
+
+namespace {
+
+// Head norm + RoPE of query rows (zcrms_heads / apply_rope on m->q,
+// nd_model.c:2419-2421, 326-397), one warp per (token, query head), in the
+// reference's statement order (warp_norm_rope), from src to dst (the same
+// buffer when no conv taps ran). Tokens map through P.spans / P.tok as in the
+// append kernels.
+template <int QK>
+__global__ void __launch_bounds__(128) rope_q_kernel(const void *src, void *dst, const AttnParams P) {
+    const int lane = (int)(threadIdx.x & 31u);
+    const size_t item = (size_t)blockIdx.x * 4u + (threadIdx.x >> 5);
+    if (item >= (size_t)P.n_tok * P.n_heads) return;
+    const uint32_t tok = (uint32_t)(item / P.n_heads), hq = (uint32_t)(item % P.n_heads);
+    const TokMeta tm = nda::token_meta(P, tok);
+    const uint32_t pos = P.state[tm.seq].pos + tm.off;
+    if (pos >= P.max_pos) {
+        if (lane == 0) nda::set_err(P.err, 2);
+        return;
+    }
+    const size_t base = ((size_t)tm.row * P.n_heads + hq) * QK;
+    nda::RopePairs<QK> x;
+    nda::warp_load_pairs<QK>(x, src, P.act_dt, base, lane);
+    nda::warp_norm_rope<QK>(x, P.rope + (size_t)pos * (QK / 2), P.qnorm, lane);
+#pragma unroll
+    for (int c = 0; c < nda::RopePairs<QK>::PPL; c++) {
+        const int i = lane + 32 * c;
+        if (i < QK / 2) {
+            nda::act_store(dst, P.act_dt, base + i, x.a[c]);
+            nda::act_store(dst, P.act_dt, base + i + QK / 2, x.b[c]);
+        }
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int nd_attn_rope_append(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const uint32_t *len,
+                        void *q, const void *k, const void *v) {
+    int rc = check_call(h, layer, n, seq_ids, len);
+    if (rc) return rc;
+    if (!k || !v) return fail(ND_ATTN_ERR_ARG, "null tensor");
+    DeviceGuard dg(h->cfg.device);
+    const nd_attn_config &c = h->cfg;
+    const uint32_t W = c.window;
+    std::vector<uint32_t> cu(n);
+    std::vector<nda::SeqSpan> spans;
+    size_t total = 0;
+    uint32_t maxlen = 0;
+    bool wraps = false;
+    for (uint32_t i = 0; i < n; i++) {
+        const uint32_t s = seq_ids ? seq_ids[i] : i, l = len ? len[i] : 1u;
+        cu[i] = (uint32_t)total;
+        total += l;
+        maxlen = std::max(maxlen, l);
+        // Two tokens of the call on one slot: the later must win, as in the
+        // reference's token-at-a-time order.
+        if ((uint64_t)h->seqs[s].pos + l > W && l > W - h->seqs[s].n_sink) wraps = true;
+        if (l) spans.push_back(nda::SeqSpan{s, cu[i], l});
+    }
+    if (total == 0) return ND_ATTN_OK;
+    if (total > 0x7fffffffu / std::max(c.n_heads, c.n_kv_heads)) return fail(ND_ATTN_ERR_RANGE, "too many tokens");
+    const void *qs = q;
+    if (c.qkv_conv_taps) {
+        rc = run_taps(h, layer, (uint32_t)spans.size(), spans.data(), (uint32_t)total, &qs, &k, &v);
+        if (rc) return rc;
+    }
+    rc = grow(&h->d_spans, &h->spans_cap, spans.size());
+    if (rc) return rc;
+    ND_CUDA(cudaMemcpyAsync(h->d_spans, spans.data(), spans.size() * sizeof(nda::SeqSpan), cudaMemcpyHostToDevice,
+                            h->stream));
+    AttnParams P = base_params(h, layer);
+    P.k = k;
+    P.v = v;
+    note_writer(h, (int)layer);
+    if (!wraps) {
+        P.spans = h->d_spans;
+        P.n_spans = (uint32_t)spans.size();
+        P.n_tok = (uint32_t)total;
+        ND_CUDA(append_launch(h, P));
+        h->launches++;
+    } else {
+        // Token by token (offset t of every sequence that has it), in order.
+        for (uint32_t t = 0; t < maxlen; t++) {
+            std::vector<TokMeta> tok;
+            for (uint32_t i = 0; i < n; i++)
+                if (t < (len ? len[i] : 1u)) tok.push_back(TokMeta{seq_ids ? seq_ids[i] : i, t, cu[i] + t});
+            rc = upload_tok(h, tok);
+            if (rc) return rc;
+            AttnParams Pt = P;
+            Pt.tok = h->d_tok;
+            Pt.n_tok = (uint32_t)tok.size();
+            ND_CUDA(append_launch(h, Pt));
+            h->launches++;
+        }
+    }
+    if (q) {
+        AttnParams Pq = base_params(h, layer);
+        Pq.spans = h->d_spans;
+        Pq.n_spans = (uint32_t)spans.size();
+        Pq.n_tok = (uint32_t)total;
+        const unsigned blocks = (unsigned)((total * c.n_heads + 3) / 4);
+        switch (c.qk_head_dim) {
+        case 48: rope_q_kernel<48><<<blocks, 128, 0, h->stream>>>(qs, q, Pq); break;
+        case 64: rope_q_kernel<64><<<blocks, 128, 0, h->stream>>>(qs, q, Pq); break;
+        default: rope_q_kernel<128><<<blocks, 128, 0, h->stream>>>(qs, q, Pq); break;
+        }
+        ND_CUDA(cudaGetLastError());
+        h->launches++;
+    }
+    return ND_ATTN_OK;
+}
+
 int nd_attn_prefill(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, const uint32_t *len,
                     const void *q, const void *k, const void *v, const void *gate, void *out) {
     if (!len) return fail(ND_ATTN_ERR_ARG, "null len");
@@ -1766,7 +1881,7 @@ int nd_attn_prefix_restore(nd_attn *h, uint32_t seq, const nd_attn_prefix *p) {
         rows_copy_kernel<<<dim3(std::min<uint32_t>(p->live, 1024u), c.n_layers), 128, 0, h->stream>>>(
             static_cast<char *>(parts[i].base), h->rows_per_layer * parts[i].row, src, p->live * parts[i].row,
             (uint32_t)(parts[i].row / 4), p->live, cv, seq, 0, 1,
-            i == 1 && c.kv_dtype == ND_DT_BF16 ? h->d_vbig : nullptr);
+            i <= 1 && c.kv_dtype == ND_DT_BF16 ? h->d_vbig : nullptr);
         h->launches++;
         src += (size_t)c.n_layers * p->live * parts[i].row;
     }
@@ -1831,7 +1946,7 @@ static int cache_io(nd_attn *h, uint32_t layer, uint32_t seq, uint32_t slot0, ui
         note_writer(h, kAllLayers);
         rows_copy_kernel<<<dim3(std::min<uint32_t>(n_slots, 4096u), 1), 128, 0, h->stream>>>(
             static_cast<char *>(parts[i].cache), 0, dense, 0, (uint32_t)(parts[i].row / 4), n_slots, cv, seq,
-            slot0, to_cache, to_cache && i == 1 ? cv.vbig : nullptr);
+            slot0, to_cache, to_cache && i <= 1 ? cv.vbig : nullptr);
         h->launches++;
         ND_CUDA(cudaGetLastError());
         if (!to_cache) ND_CUDA(cudaMemcpyAsync(parts[i].user, d + off, nb, cudaMemcpyDeviceToHost, h->stream));

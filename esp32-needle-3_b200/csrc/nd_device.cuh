@@ -60,13 +60,13 @@ struct CacheView {
     uint32_t k_dim, v_dim, n_kv, window;
     const int32_t *btab;         // nullptr = contiguous
     uint32_t blocks_per_seq, block_shift;
-    int *vbig;                   // bf16 caches: the layer's flag "V holds a value f16 cannot represent"
+    int *vbig;                   // bf16 caches: the layer's flag "K or V holds a value f16 cannot represent"
 };
 
 // A bf16 pair word holding a value with |x| >= 2^16, Inf or NaN (exponent
-// field >= 143): values f16 cannot represent exactly. Writers of a bf16 V cache
-// set the layer's flag when they store one (the tensor-core prefill converts V
-// tiles to f16 only while the flag is clear).
+// field >= 143): values f16 cannot represent. Writers of a bf16 cache set the
+// layer's flag when they store one in K or V (the tensor-core prefill converts
+// K and V tiles to f16 only while the flag is clear).
 __device__ __forceinline__ bool bf16x2_big(uint32_t w) {
     return (w & 0x7f80u) >= 0x4780u || (w & 0x7f800000u) >= 0x47800000u;
 }
@@ -435,15 +435,22 @@ __device__ __forceinline__ void warp_append(const CacheView &c, size_t row, uint
     } else {
         KVT *kd = static_cast<KVT *>(c.k) + kbase;
         KVT *vd = static_cast<KVT *>(c.v) + vbase;
+        bool big = false;
 #pragma unroll
         for (int cI = 0; cI < RopePairs<QK>::PPL; cI++) {
             const int i = lane + 32 * cI;
             if (i < HALF) {
-                kd[i] = kv_from_float<KVT>(kx.a[cI]);
-                kd[i + HALF] = kv_from_float<KVT>(kx.b[cI]);
+                const KVT a = kv_from_float<KVT>(kx.a[cI]), b = kv_from_float<KVT>(kx.b[cI]);
+                kd[i] = a;
+                kd[i + HALF] = b;
+                if constexpr (KvT<KVT>::dt == DT_BF16) {
+                    uint16_t ua, ub;
+                    memcpy(&ua, &a, 2);
+                    memcpy(&ub, &b, 2);
+                    big |= bf16x2_big(ua) || bf16x2_big(ub);
+                }
             }
         }
-        bool big = false;
 #pragma unroll
         for (int cI = 0; cI < VPL; cI++) {
             const int i = lane + 32 * cI;
@@ -531,7 +538,8 @@ __global__ void __launch_bounds__(256) append_vec_kernel(const AttnParams P) {
     *reinterpret_cast<uint2 *>(kd + HALF + 4 * t) = ob;
     *reinterpret_cast<uint4 *>(vd + 8 * t) = vv;
     if constexpr (KvT<KVT>::dt == DT_BF16) {
-        if (P.c.vbig && (bf16x2_big(vv.x) || bf16x2_big(vv.y) || bf16x2_big(vv.z) || bf16x2_big(vv.w)))
+        if (P.c.vbig && (bf16x2_big(vv.x) || bf16x2_big(vv.y) || bf16x2_big(vv.z) || bf16x2_big(vv.w) ||
+                         bf16x2_big(oa.x) || bf16x2_big(oa.y) || bf16x2_big(ob.x) || bf16x2_big(ob.y)))
             atomicOr(P.c.vbig, 1);
     }
 }

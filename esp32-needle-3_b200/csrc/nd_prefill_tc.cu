@@ -46,6 +46,7 @@
 
 #include "nd_async.cuh"
 #include "nd_internal.h"
+#include "nd_tc.cuh"
 
 namespace nda {
 namespace {
@@ -86,105 +87,6 @@ struct Bars {
 };
 constexpr uint32_t SMEM_BYTES = OFF_BAR + sizeof(Bars);
 
-// Shared-memory matrix descriptor, 128-byte swizzle, sm100 version bits.
-__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
-    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
-    d |= (uint64_t)1 << 46;   // descriptor version 1
-    d |= (uint64_t)2 << 61;   // SWIZZLE_128B
-    return d;
-}
-
-// Instruction descriptor of kind::f16: fp32 accumulate, A/B format (0 f16, 1 bf16).
-__host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_fmt, uint32_t m, uint32_t n, uint32_t b_mn_major) {
-    return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (b_mn_major << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
-}
-
-// D (+)= A * B with A from TMEM and B from shared memory.
-__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
-        "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
-}
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
-                 : "memory");
-}
-
-#define ND_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
-#define ND_W8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), "r"(r[i + 5]), "r"(r[i + 6]), "r"(r[i + 7])
-
-// 32 consecutive 32-bit TMEM columns of this thread's lane; the wait is left
-// to tmem_wait_ld() so that several loads can be in flight at once.
-__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t *r) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : ND_R8(0), ND_R8(8), ND_R8(16), ND_R8(24)
-        : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-        ND_W8(0), ND_W8(8), ND_W8(16), ND_W8(24)
-        : "memory");
-}
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-            taddr),
-        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-        : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-// 16 consecutive 32-bit TMEM columns of this thread's lane (waits).
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *r) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    tmem_wait_ld();
-}
-#undef ND_R8
-#undef ND_W8
-
-template <bool BF16>
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-    uint32_t u;
-    if constexpr (BF16) {
-        __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
-        memcpy(&u, &t, 4);
-    } else {
-        __half2 t = __floats2half2_rn(lo, hi);
-        memcpy(&u, &t, 4);
-    }
-    return u;
-}
-template <bool BF16>
-__device__ __forceinline__ float2 unpack2(uint32_t u) {
-    if constexpr (BF16) {
-        return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
-    } else {
-        __half2 t;
-        memcpy(&t, &u, 4);
-        return __half22float2(t);
-    }
-}
-// hi/lo split of a pair: hi = RN16(a,b), lo = RN16(a - hi, b - hi).
-template <bool BF16>
-__device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t &lo) {
-    hi = pack2<BF16>(a, b);
-    const float2 h = unpack2<BF16>(hi);
-    lo = pack2<BF16>(a - h.x, b - h.y);
-}
-
 // P = 2^(S*c - m) for 32 keys of a row, written over their S columns: with
 // PSPLIT as hi/lo bf16 pairs (16 columns of hi, then 16 of lo), else as single
 // f16 pairs (16 columns). The row sum goes into l2.
@@ -214,36 +116,6 @@ __device__ __forceinline__ void write_p_chunk(const uint32_t (&sv)[32], uint32_t
     if constexpr (PSPLIT) tmem_st32(taddr, pk);
     else tmem_st16(taddr, pk);
     l2 = __fadd2_rn(l2, __fadd2_rn(acc[0], acc[1]));
-}
-
-// Three-input maximum (one instruction on sm_100).
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-    float r;
-    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-    return r;
-}
-
-// Offset of 16-byte chunk `c` of row `r` in a 128-byte-swizzled tile.
-__device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) { return r * 128u + ((c ^ (r & 7u)) << 4); }
-// Offset of 16-byte chunk `c` (0..15) of RoPE row `r` in the 32 KB block, as
-// the 3D map [pos][2 halves][32 floats] with the 128-byte swizzle lays it out:
-// 128-byte line 2r + half, chunk XOR (line & 7).
-__device__ __forceinline__ uint32_t cs_off(uint32_t r, uint32_t c) {
-    const uint32_t line = 2 * r + (c >> 3);
-    return line * 128u + (((c & 7u) ^ (line & 7u)) << 4);
-}
-
-__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
-            su32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(z), "r"(su32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
-                 "r"(su32(src)), "r"(x), "r"(y)
-                 : "memory");
 }
 
 // BF16 = 16-bit type of the cache and activations. PVF16 (bf16 only): P and
@@ -365,7 +237,7 @@ __global__ void __launch_bounds__(192, 2)
                 long long idle_since = clock64();
                 while (ok && gp < gend) {
                     bool progressed = false;
-                    if (gp < gs && mbar_test(&B.p_full[gp % NB], (gp / NB) & 1)) {
+                    if (gp < gs && mbar_ready(&B.p_full[gp % NB], (gp / NB) & 1)) {
                         // O += P V (P in S buffer gp % NB, V in stage gp % STAGES).
                         const uint32_t b = gp % NB, st = gp % STAGES;
                         fence_after();
@@ -382,8 +254,8 @@ __global__ void __launch_bounds__(192, 2)
                         gp++;
                         progressed = true;
                     }
-                    if (gs < gend && (gs < NB || (gp > gs - NB && mbar_test(&B.pv_done[gs % NB], (gs / NB - 1) & 1))) &&
-                        mbar_test(&B.kv_full[gs % STAGES], (gs / STAGES) & 1)) {
+                    if (gs < gend && (gs < NB || (gp > gs - NB && mbar_ready(&B.pv_done[gs % NB], (gs / NB - 1) & 1))) &&
+                        mbar_ready(&B.kv_full[gs % STAGES], (gs / STAGES) & 1)) {
                         // S = Q K^T into buffer gs % NB (its previous P was read).
                         const uint32_t b = gs % NB, st = gs % STAGES;
                         fence_after();

@@ -83,6 +83,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "nd_attn_set_state": (c_int, [vp, u32, u32, u32]),
         "nd_attn_decode": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp, vp]),
         "nd_attn_prefill": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp, vp, vp]),
+        "nd_attn_rope_append": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp]),
         "nd_attn_decode_host": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp, vp]),
         "nd_attn_decode_noalloc": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp]),
         "nd_attn_gather_check": (c_int, [vp, u32, u32]),
@@ -267,6 +268,12 @@ class Attn:
         ln, ids = _u32(lens), _u32(seq_ids)
         _check(load().nd_attn_prefill(self.h, layer, len(ln), _hptr(ids), _hptr(ln), _ptr(q), _ptr(k), _ptr(v),
                                       _ptr(gate), _ptr(out)))
+
+    def rope_append(self, layer, lens, q, k, v, seq_ids=None) -> None:
+        """K1 alone (nd_attn_rope_append): norm + RoPE + KV store of k/v at the
+        sequences' current positions; q (or None) rotated in place."""
+        ln, ids = _u32(lens), _u32(seq_ids)
+        _check(load().nd_attn_rope_append(self.h, layer, len(ln), _hptr(ids), _hptr(ln), _ptr(q), _ptr(k), _ptr(v)))
 
     def decode_noalloc(self, layer, n, q, k, v, out, gate=None) -> None:
         """nd_attn_decode for sequences 0..n-1 with its scratch in the library's

@@ -177,6 +177,21 @@ ND_ATTN_API int  nd_attn_decode(nd_attn *h, uint32_t layer, uint32_t n, const ui
 ND_ATTN_API int  nd_attn_prefill(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids,
                      const uint32_t *len, const void *q, const void *k, const void *v,
                      const void *gate, void *out);
+/* K1 alone: the head norm + RoPE and the KV store of attention()
+ * (nd_model.c:2419-2449) without the attention. For len[i] tokens of each
+ * listed sequence at positions [pos, pos + len[i]) (its current position; NULL
+ * len = one token each; not advanced), k is normed with the layer's k_norm,
+ * rotated and stored with v at kv_slot(position), in the handle's cache format
+ * (int8: the bytes and scales of kv_store_int8, nd_model.c:1822-1866). q,
+ * when not NULL, is normed with q_norm and rotated IN PLACE, as zcrms_heads /
+ * apply_rope do to m->q (nd_model.c:326-397), in the reference's statement
+ * order: with f32 activations the bits equal the reference's. Tokens of one
+ * sequence that land on the same ring slot are stored in position order (the
+ * last one stays). With conv taps, q/k/v are the raw projections (convolved
+ * first; q receives the convolved, rotated rows). DEVICE pointers; len is a
+ * HOST array. */
+ND_ATTN_API int  nd_attn_rope_append(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids,
+                                     const uint32_t *len, void *q, const void *k, const void *v);
 /* Same as nd_attn_decode / nd_attn_prefill with q/k/v/gate/out in HOST memory;
  * both return after the work has completed. This is the form the reference
  * engine's attention() seam calls (its buffers m->q, m->kbuf, m->vbuf,

@@ -103,6 +103,8 @@ def ref() -> ctypes.CDLL:
         lib.ndref_prefix_image.argtypes = [POINTER(RefGeom), c_void_p, c_void_p, c_void_p, c_void_p, c_uint32,
                                            c_uint32, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
                                            POINTER(c_uint32)]
+        lib.ndref_norm_rope.restype = c_int
+        lib.ndref_norm_rope.argtypes = [POINTER(RefGeom), c_void_p, c_uint32, c_void_p, c_void_p, c_void_p]
         lib.ndref_tap.restype = c_int
         lib.ndref_tap.argtypes = [c_uint32, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p]
         lib.ndref_prefill_bench.restype = c_double
@@ -340,6 +342,17 @@ class RefSeq(_SeqBase):
                                  self.vs.ctypes.data, self.pos, self.T, *hp, buf.ctypes.data, buf.size,
                                  ctypes.byref(sink))
         return buf[:n].tobytes(), sink.value
+
+
+def ref_norm_rope(x, n_heads, qk, theta, pos, norm=None):
+    """Rows x [n_heads * qk] after the reference's own zcrms_heads (with
+    `norm`) or apply_rope (without) at `pos`."""
+    y = np.array(x, dtype=np.float32, copy=True).reshape(-1)
+    cs, sn = ref_rope(theta, qk, pos)
+    g = RefGeom(1, n_heads, n_heads, qk, qk, max(pos + 1, 2))
+    nm = None if norm is None else np.ascontiguousarray(norm, dtype=np.float32)
+    assert ref().ndref_norm_rope(ctypes.byref(g), y.ctypes.data, n_heads, _p(nm), cs.ctypes.data, sn.ctypes.data) == 0
+    return y
 
 
 def ref_rope(theta, qk, pos):

@@ -179,6 +179,19 @@ int ndref_attn_token(const ndref_geom *g, int8_t *k_cache, int8_t *v_cache,
     return 0;
 }
 
+/* The reference's own norm + RoPE of `nheads` rows in place (zcrms_heads with
+ * a norm, apply_rope without; nd_model.c:326-397), at the cos/sin given. */
+int ndref_norm_rope(const ndref_geom *g, float *x, uint32_t nheads, const float *norm, const float *rope_cos,
+                    const float *rope_sin)
+{
+    nd_model m;
+    ndref_model_view(&m, g);
+    m.rope_cos = (float *)rope_cos; m.rope_sin = (float *)rope_sin;
+    if (norm) zcrms_heads(&m, norm, rope_cos, rope_sin, x, nheads, m.qk_head_dim);
+    else      apply_rope(&m, x, nheads, m.qk_head_dim);
+    return 0;
+}
+
 /* The reference's tap_projection on one projection row (layer 0): `hist` is
  * that layer's [taps][dim] history (slot pos % taps takes the row), `w` its
  * staged [taps][dim] weights; `proj` is replaced by the convolved row. */

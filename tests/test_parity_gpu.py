@@ -629,3 +629,57 @@ def test_tensor_core_prefill_large_queries_stay_finite(dt):
             worst = max(worst, rel_err(got[t].reshape(H, D), want))
     assert worst <= TOL
     a.close()
+
+
+@pytest.mark.parametrize("H,HKV,QK,VD,theta", [(12, 2, 48, 64, 1e5), (8, 8, 64, 64, 1e4)])
+def test_rope_append_matches_reference(H, HKV, QK, VD, theta):
+    """K1 alone (nd_attn_rope_append) against the reference's own C: int8 K/V
+    bytes and scales bit-exact with kv_store_int8 (via the reference's token
+    step), q rotated in place bit-exact with zcrms_heads (norms set), over two
+    calls per layer; the second call's 130 tokens wrap one sequence's ring
+    past its sinks (stored in position order, the last one stays)."""
+    import torch
+    if not O.ref_available():
+        pytest.skip("reference build absent")
+    rng = np.random.default_rng(51)
+    L, W, S = 2, 96, 3
+    a = ndattn.Attn(n_layers=L, n_heads=H, n_kv_heads=HKV, qk_head_dim=QK, v_head_dim=VD, window=W, max_seqs=S,
+                    rope_theta=theta, kv_dtype="i8", act_dtype="f32", max_pos=512)
+    refs = [O.RefSeq(L, H, HKV, QK, VD, W, O.I8, theta=theta, max_pos=512) for _ in range(S)]
+    norms = []
+    for layer in range(L):
+        qs = (rng.standard_normal(QK) * 0.1).astype(np.float32)
+        ks = (rng.standard_normal(QK) * 0.1).astype(np.float32)
+        a.set_head_norm(layer, qs, ks)
+        for r in refs:
+            r.norms[layer] = (qs, ks)
+        norms.append(qs)
+    for call, lens in enumerate(([5, 17, 20], [40, 3, 130])):
+        if call == 1:                       # sequence 2 pins its first 20 positions as sinks
+            a.snapshot(2)
+            refs[2].snapshot()
+        T = sum(lens)
+        cu = np.concatenate([[0], np.cumsum(lens)])
+        for layer in range(L):
+            q = (rng.standard_normal((T, H * QK)) * 0.5).astype(np.float32)
+            k = (rng.standard_normal((T, HKV * QK)) * 0.5).astype(np.float32)
+            v = (rng.standard_normal((T, HKV * VD)) * 0.5).astype(np.float32)
+            qt = torch.from_numpy(q).cuda()
+            a.rope_append(layer, lens, qt, torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda())
+            a.sync()
+            got_q = qt.cpu().numpy()
+            for s in range(S):
+                for t in range(lens[s]):
+                    row = cu[s] + t
+                    want_q = O.ref_norm_rope(q[row], H, QK, theta, refs[s].pos + t, norm=norms[layer])
+                    assert np.array_equal(got_q[row].view(np.uint32), want_q.view(np.uint32)), (call, layer, s, t)
+                    refs[s].step(layer, q[row], k[row], v[row], off=t)   # the reference's own store
+        a.advance(S, lens=lens)
+        for s in range(S):
+            refs[s].advance(lens[s])
+    for s in range(S):
+        for layer in range(L):
+            kc, vc, ksc, vsc = a.read_cache(layer, s, 0, W)
+            assert np.array_equal(kc, refs[s].k[layer]) and np.array_equal(vc, refs[s].v[layer]), (s, layer)
+            assert np.array_equal(ksc, refs[s].ks[layer]) and np.array_equal(vsc, refs[s].vs[layer]), (s, layer)
+    a.close()
