@@ -562,7 +562,7 @@ int run_taps(nd_attn *h, uint32_t layer, uint32_t n_spans, const nda::SeqSpan *s
 // scales come in as TMA boxes too) with query groups of at most two rows,
 // with equal head dims of 64 or 128 (GQA
 // width <= 4 at 128), calls in which no position wraps the ring, and pages
-// (if any) holding whole 64-row boxes.
+// (if any) holding whole tiles (64 rows; 128 for int8, lean_rows).
 bool lean_ok(const nd_attn *h, bool no_wrap) {
     const nd_attn_config &cf = h->cfg;
     const int nq = nda::nq_for_rep(h->rep);
@@ -570,15 +570,18 @@ bool lean_ok(const nd_attn *h, bool no_wrap) {
                        (cf.kv_dtype == ND_DT_I8 && cf.n_kv_heads % 4 == 0 && nq <= 2);
     return no_wrap && dt_ok && cf.qk_head_dim == cf.v_head_dim &&
            (cf.qk_head_dim == 64 || (cf.qk_head_dim == 128 && nq <= 4)) &&
-           (cf.block_size == 0 || cf.block_size % (uint32_t)nda::kTmaRows == 0) && h->rows_per_layer < 0x7fffffffu;
+           (cf.block_size == 0 || cf.block_size % (uint32_t)nda::lean_rows(cf.kv_dtype == ND_DT_I8) == 0) &&
+           h->rows_per_layer < 0x7fffffffu;
 }
 
-// Balanced-launch tuning: share of the tiles in static units (percent; 16-bit
-// and int8 caches), least tiles per dynamic unit, dynamic units a producer
-// holds ahead. Config-2 decode swept over 50-90 %: 16-bit caches run fastest
-// at 60-65 % (245k tok/s against 240k at 75 %), int8 caches at 75 %.
-constexpr uint64_t kLeanStaticPct16 = 65, kLeanStaticPctI8 = 75, kLeanUnitMin = 2;
-constexpr uint32_t kLeanAhead = 2;
+// Balanced-launch tuning: share of the tiles in static units (percent), least
+// tiles per dynamic unit and dynamic units a producer holds ahead, for 16-bit
+// caches (64-row tiles) and int8 caches (128-row tiles). Config-2 decode swept
+// over 50-90 % static, 1-3 tiles per unit, 1-2 units ahead: 16-bit caches run
+// fastest at 60-65 %, 2 tiles, 2 ahead (245k tok/s against 240k at 75 %); int8
+// at 85-90 %, 1 tile, 1 ahead (31.9 us per launch against 33.9 at 75 %, 1, 2).
+constexpr uint64_t kLeanStaticPct16 = 65, kLeanStaticPctI8 = 85, kLeanUnitMin16 = 2, kLeanUnitMinI8 = 1;
+constexpr uint32_t kLeanAhead16 = 2, kLeanAheadI8 = 1;
 
 // Builds the balanced-launch plan of a call into h->lean_up: per token
 // {first tile, tiles per item, sequence, position} and a sentinel, then per
@@ -596,7 +599,8 @@ void lean_geometry(nd_attn *h, uint64_t nt, int occ) {
     const uint64_t pct = h->cfg.kv_dtype == ND_DT_I8 ? kLeanStaticPctI8 : kLeanStaticPct16;
     const uint64_t S = std::max<uint64_t>(1, nt * pct / (100 * G));
     const uint64_t dyn = nt - G * S;
-    uint64_t CH = std::max<uint64_t>(kLeanUnitMin, (dyn + 4 * G - 1) / (4 * G));
+    const uint64_t umin = h->cfg.kv_dtype == ND_DT_I8 ? kLeanUnitMinI8 : kLeanUnitMin16;
+    uint64_t CH = std::max<uint64_t>(umin, (dyn + 4 * G - 1) / (4 * G));
     while (G + (dyn + CH - 1) / CH > budget) CH *= 2;
     h->lean_nt = nt, h->lean_g = G, h->lean_s = S, h->lean_ch = CH, h->lean_nu = G + (dyn + CH - 1) / CH;
 }
@@ -604,12 +608,13 @@ void lean_geometry(nd_attn *h, uint64_t nt, int occ) {
 int build_lean_plan(nd_attn *h, uint32_t ntok, const std::vector<uint32_t> &vis, const std::vector<uint32_t> &tok_seq,
                     const std::vector<uint32_t> &tok_pos, int fuse_append, int occ) {
     const uint32_t n_kv = h->cfg.n_kv_heads;
+    const uint32_t tr = (uint32_t)nda::lean_rows(h->cfg.kv_dtype == ND_DT_I8);
     std::vector<uint32_t> &up = h->lean_up;
     up.assign((size_t)(ntok + 1) * 4, 0u);
     uint64_t nt = 0;
     for (uint32_t t = 0; t < ntok; t++) {
         const uint32_t rows = vis[t] - (fuse_append ? 1u : 0u);
-        const uint32_t T = std::max<uint32_t>(1u, (rows + nda::kTmaRows - 1) / nda::kTmaRows);
+        const uint32_t T = std::max<uint32_t>(1u, (rows + tr - 1) / tr);
         up[4 * t + 0] = (uint32_t)nt;
         up[4 * t + 1] = T;
         up[4 * t + 2] = tok_seq[t];
@@ -662,6 +667,7 @@ int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, co
                       : nda::attend_lean_launch_f16((int)hd, nq, km, vm, ksm, vsm, ktm, vtm, tk, P, occ, h->stream);
     };
     int &occ = h->lean_occ[(bf16 ? 4 : 0) + (nq == 1 ? 0 : nq == 2 ? 1 : nq == 4 ? 2 : 3)];
+    const uint32_t tr = (uint32_t)nda::lean_rows(cf.kv_dtype == ND_DT_I8);
     AttnParams P = base_params(h, layer);
     if (occ <= 0) {
         int b = 0;
@@ -677,7 +683,7 @@ int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, co
         uint64_t nt = 0;
         for (uint32_t t = 0; t < ntok; t++) {
             const uint32_t rows = vis[t] - (fuse_append ? 1u : 0u);
-            const uint32_t T = std::max<uint32_t>(1u, (rows + nda::kTmaRows - 1) / nda::kTmaRows);
+            const uint32_t T = std::max<uint32_t>(1u, (rows + tr - 1) / tr);
             tk.tok[t] = make_uint4((uint32_t)nt, T, tok_seq[t], tok_pos[t]);
             nt += (uint64_t)cf.n_kv_heads * T;
             if (nt > 0x7fffffffu) return fail(ND_ATTN_ERR_RANGE, "launch too large");
@@ -708,7 +714,7 @@ int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, co
     }
     const uint64_t nt = h->lean_nt, G = h->lean_g, S = h->lean_s, CH = h->lean_ch, NU = h->lean_nu;
     const size_t cnt_half = h->counter_cap / 2, slot_half = h->part_slots / 2;
-    P.lean_ahead = kLeanAhead;
+    P.lean_ahead = cf.kv_dtype == ND_DT_I8 ? kLeanAheadI8 : kLeanAhead16;
     P.lean_s = (uint32_t)S;
     P.lean_ch = (uint32_t)CH;
     P.n_units = (uint32_t)NU;
@@ -739,21 +745,21 @@ int run_lean(nd_attn *h, uint32_t layer, uint32_t ntok, const TokMeta *d_tok, co
         h->lean_map_ok.assign(cf.n_layers, 0);
     }
     if (!h->lean_map_ok[layer]) {   // the layer's cache never moves: encode its maps once
-        // Rows of [n_kv][hd] elements, box {hd, 64} (item tails: {hd, 16}) at x = g * hd; int8 scales
-        // [n_kv] f32 per row, box {4, 64} at x = g rounded down to 4 (16 bytes).
+        // Rows of [n_kv][hd] elements, box {hd, TR} (item tails: {hd, 16}) at x = g * hd; int8 scales
+        // [n_kv] f32 per row, box {4, TR} at x = g rounded down to 4 (16 bytes). TR = lean_rows().
         const size_t es = h->kes;
         int rc = make_map_dt(&h->lean_kmap[layer], cf.kv_dtype, P.c.k, h->k_dim, h->rows_per_layer,
-                             (uint64_t)h->k_dim * es, nda::kTmaRows, hd, false);
+                             (uint64_t)h->k_dim * es, tr, hd, false);
         if (!rc) rc = make_map_dt(&h->lean_vmap[layer], cf.kv_dtype, P.c.v, h->v_dim, h->rows_per_layer,
-                                  (uint64_t)h->v_dim * es, nda::kTmaRows, hd, false);
+                                  (uint64_t)h->v_dim * es, tr, hd, false);
         if (!rc) rc = make_map_dt(&h->lean_ktmap[layer], cf.kv_dtype, P.c.k, h->k_dim, h->rows_per_layer,
                                   (uint64_t)h->k_dim * es, 16, hd, false);
         if (!rc) rc = make_map_dt(&h->lean_vtmap[layer], cf.kv_dtype, P.c.v, h->v_dim, h->rows_per_layer,
                                   (uint64_t)h->v_dim * es, 16, hd, false);
         if (!rc && i8) rc = make_map_dt(&h->lean_ksmap[layer], ND_DT_F32, P.c.ks, cf.n_kv_heads, h->rows_per_layer,
-                                        (uint64_t)cf.n_kv_heads * 4, nda::kTmaRows, 4, false);
+                                        (uint64_t)cf.n_kv_heads * 4, tr, 4, false);
         if (!rc && i8) rc = make_map_dt(&h->lean_vsmap[layer], ND_DT_F32, P.c.vs, cf.n_kv_heads, h->rows_per_layer,
-                                        (uint64_t)cf.n_kv_heads * 4, nda::kTmaRows, 4, false);
+                                        (uint64_t)cf.n_kv_heads * 4, tr, 4, false);
         if (rc) return rc;
         if (!i8) h->lean_ksmap[layer] = h->lean_kmap[layer], h->lean_vsmap[layer] = h->lean_vmap[layer];  // unused
         h->lean_map_ok[layer] = 1;
@@ -2246,3 +2252,17 @@ const nd_attn_ops *nd_attn_cuda_ops(void) {
     };
     return &ops;
 }
+
+// Error reporting for the library's other translation units (nd_cq.cu): the
+// same per-thread message nd_attn_last_error() returns.
+namespace nda {
+int report_error(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+}  // namespace nda

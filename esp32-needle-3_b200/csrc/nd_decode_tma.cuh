@@ -1,12 +1,13 @@
 // nd_decode_tma.cuh - persistent, dynamically balanced split-KV attention with
 // the K/V rows staged by TMA.
 //
-// Same results as attend_kernel (nd_device.cuh) for 16-bit caches whose head
-// dims are equal (64 or 128) and calls in which no position wraps the ring
-// (visit index == slot == position).
+// Same results as attend_kernel (nd_device.cuh) for 16-bit and int8 caches
+// whose head dims are equal (64 or 128) and calls in which no position wraps
+// the ring (visit index == slot == position).
 //
-// Work. Item (t, g) = query token t, KV head g; it holds T_t tiles of 64 cache
-// rows. Items are concatenated token-major into NT tiles, cut into units:
+// Work. Item (t, g) = query token t, KV head g; it holds T_t tiles of TR cache
+// rows (64; 128 for int8 caches). Items are concatenated token-major into NT
+// tiles, cut into units:
 // G static units of S tiles (CTA c starts with unit c), then dynamic units of
 // CH tiles that CTAs take from a global counter as they run dry, so an SM that
 // the memory system serves faster takes more work and all CTAs end together.
@@ -21,15 +22,15 @@
 // attend_kernel, rows read from shared memory); 4 = producer: takes units,
 // publishes a descriptor per segment (maximal run of one item inside a unit)
 // into a SQ-deep slot ring and issues the TMA boxes (2D maps over
-// [rows][n_kv * hd], box hd x 64, each CTA loading its own) into a STAGES-deep ring;
+// [rows][n_kv * hd], box hd x TR, each CTA loading its own) into a STAGES-deep ring;
 // 5 = prep: query rows of each segment (norm + RoPE) and the fused append of
 // the newest row; 6 = finisher: merges the consumers' per-warp results of a
 // segment and writes the output, or the item's partial and a note of it in
 // shared memory, so the merge does not sit on the consumers' path. Every mbarrier wait is bounded (nd_async.cuh); on a timeout
 // each role stops (no named barriers, so none can be left waiting).
 //
-// Paged caches work when a page holds a whole number of 64-row boxes: tiles
-// start on multiples of 64 rows of an item, so every box lies in one page.
+// Paged caches work when a page holds a whole number of tiles: tiles start on
+// multiples of TR rows of an item, so every box lies in one page.
 //
 // Launch overlap (programmatic dependent launch): the kernel may start while
 // the previous kernel on the stream still runs. The prep and finisher warps
@@ -46,11 +47,6 @@
 
 namespace nda {
 
-#ifndef ND_TMA_ROWS_DEFINED
-#define ND_TMA_ROWS_DEFINED
-constexpr int kTmaRows = 64;   // rows per TMA box / tile
-#endif
-
 #ifndef ND_LEAN_STAGES64
 #define ND_LEAN_STAGES64 4
 #endif
@@ -61,24 +57,109 @@ constexpr int kLeanAheadMax = 4;
 template <int HD, typename KVT, int NQ> struct LeanCfg {
     static constexpr bool I8 = KvT<KVT>::dt == DT_I8;
     static constexpr int NW = 4;                                     // consumer warps
-    // Tile ring depth: int8 tiles are half the bytes, so more of them.
-    static constexpr int STAGES = I8 ? (HD == 64 ? 6 : 4) : HD == 64 ? ND_LEAN_STAGES64 : (NQ >= 4 ? 2 : 3);
+    static constexpr int TR = lean_rows(I8);                         // rows per tile
+    // Tile ring depth (int8: 128-row tiles).
+    static constexpr int STAGES = I8 ? (HD == 64 ? 3 : 2) : HD == 64 ? ND_LEAN_STAGES64 : (NQ >= 4 ? 2 : 3);
     static constexpr int SQ = NQ * HD >= 256 ? 2 : 4;                // segment slot ring depth
-    static constexpr uint32_t TILE = kTmaRows * HD * sizeof(KVT);
+    // CTAs per SM the register budget is sized for: one query row at hd 64 fits
+    // three (the shared-memory limit too) in 96 registers without spills.
+    static constexpr int MINB = NQ == 1 && HD == 64 ? 3 : 1;
+    static constexpr uint32_t TILE = TR * HD * sizeof(KVT);
     // An item's last tile loads only the 16-row sub-boxes that hold its rows.
     static constexpr int SUBR = 16;
     static constexpr uint32_t SUB = SUBR * HD * sizeof(KVT);
     // int8: per stage the K and V scales of the tile's rows for four KV heads
-    // (a {4, 64} f32 box: TMA moves at least 16 bytes per row).
-    static constexpr uint32_t SC = I8 ? kTmaRows * 16 : 0;
+    // (a {4, TR} f32 box: TMA moves at least 16 bytes per row).
+    static constexpr uint32_t SC = I8 ? TR * 16 : 0;
     static constexpr uint32_t OFF_V = STAGES * TILE;
-    static constexpr uint32_t OFF_KS = 2 * STAGES * TILE;                       // [STAGES][64][4] f32
+    static constexpr uint32_t OFF_KS = 2 * STAGES * TILE;                       // [STAGES][TR][4] f32
     static constexpr uint32_t OFF_VS = OFF_KS + STAGES * SC;
     static constexpr uint32_t OFF_Q = OFF_KS + 2 * STAGES * SC;                 // [SQ][NQ][HD] f32
     static constexpr uint32_t OFF_MO = OFF_Q + SQ * NQ * HD * 4;                // [SQ][NW][NQ][HD] f32
     static constexpr uint32_t OFF_ML = OFF_MO + SQ * NW * NQ * HD * 4;          // [SQ][NW][NQ][2] f32
     static constexpr uint32_t SMEM = OFF_ML + SQ * NW * NQ * 2 * 4;
 };
+
+// int8 rows: q.k on the integer dot-product path. A segment's query row q
+// (already scaled by scale * log2 e) is held as q = c * (l2 * 2^16 + l1 * 2^8 + l0),
+// a 23-bit fixed-point integer in three byte limbs (l2 signed, l1 and l0
+// unsigned) with c = 2^-sh a power of two picked from the row's largest |q|
+// (|q / c| < 2^22), so q.k over four cache bytes is one dp4a per limb, exact in
+// int32, and the three sums meet in f32. Quantising q costs at most 2^-23 of
+// the row's largest element: the size of the rounding the reference's own
+// float dot product makes (qk_dot8 in attn_heads, nd_model.c:2188-2214). A
+// non-finite query element makes c NaN, so the row's scores are NaN as with
+// float arithmetic.
+template <int NQ, int EK, int LPR>
+__device__ __forceinline__ void q_limbs(const float (&qr)[NQ][EK], uint32_t (&ql)[NQ][3][EK / 4],
+                                        float (&cq)[NQ][3]) {
+#pragma unroll
+    for (int qi = 0; qi < NQ; qi++) {
+        float mx = 0.0f, z = 0.0f;
+#pragma unroll
+        for (int e = 0; e < EK; e++) {
+            mx = fmaxf(mx, fabsf(qr[qi][e]));
+            z += qr[qi][e] * 0.0f;   // NaN when any element is Inf or NaN
+        }
+#pragma unroll
+        for (int o = 1; o < LPR; o <<= 1) {
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            z += __shfl_xor_sync(0xffffffffu, z, o);
+        }
+        // mx < 2^ex; scale by 2^sh, sh = 22 - ex, kept inside the normal range.
+        const int ex = (int)((__float_as_uint(mx) >> 23) & 0xffu) - 126;
+        const int sh = min(126, max(-126, 22 - ex));
+        const float up = __uint_as_float((uint32_t)(127 + sh) << 23);
+        const float c = __uint_as_float((uint32_t)(127 - sh) << 23) + z;
+        cq[qi][0] = c;
+        cq[qi][1] = c * 256.0f;
+        cq[qi][2] = c * 65536.0f;
+#pragma unroll
+        for (int w = 0; w < EK / 4; w++) {
+            uint32_t b0 = 0, b1 = 0, b2 = 0;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int x = z == 0.0f ? __float2int_rn(qr[qi][4 * w + j] * up) : 0;
+                b0 |= ((uint32_t)x & 0xffu) << (8 * j);
+                b1 |= ((uint32_t)(x >> 8) & 0xffu) << (8 * j);
+                b2 |= ((uint32_t)(x >> 16) & 0xffu) << (8 * j);
+            }
+            ql[qi][0][w] = b0;
+            ql[qi][1][w] = b1;
+            ql[qi][2][w] = b2;
+        }
+    }
+}
+
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// This lane's partial q.k of each row group from its K words (EK int8 values).
+template <int NQ, int EK, int UU>
+__device__ __forceinline__ void qk_i8dp(const uint32_t (&ql)[NQ][3][EK / 4], const float (&cq)[NQ][3],
+                                        const uint32_t (&kw)[UU][EK / 4], float (&s)[UU][NQ]) {
+#pragma unroll
+    for (int u = 0; u < UU; u++)
+#pragma unroll
+        for (int qi = 0; qi < NQ; qi++) {
+            int a2 = 0, a1 = 0, a0 = 0;
+#pragma unroll
+            for (int w = 0; w < EK / 4; w++) {
+                a2 = dp4a_ss(ql[qi][2][w], kw[u][w], a2);
+                a1 = dp4a_us(ql[qi][1][w], kw[u][w], a1);
+                a0 = dp4a_us(ql[qi][0][w], kw[u][w], a0);
+            }
+            s[u][qi] = fmaf((float)a2, cq[qi][2], fmaf((float)a1, cq[qi][1], (float)a0 * cq[qi][0]));
+        }
+}
 
 template <int HD, typename KVT, int NQ>
 constexpr uint32_t attend_lean_smem_bytes() {
@@ -219,7 +300,7 @@ struct LeanInfo {   // the same segment, completed by the prep warp
 };
 
 template <int HD, typename KVT, int NQ>
-__global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant__ CUtensorMap kmap,
+__global__ void __launch_bounds__(224, (LeanCfg<HD, KVT, NQ>::MINB)) attend_lean_kernel(const __grid_constant__ CUtensorMap kmap,
                                                           const __grid_constant__ CUtensorMap vmap,
                                                           const __grid_constant__ CUtensorMap ksmap,
                                                           const __grid_constant__ CUtensorMap vsmap,
@@ -229,7 +310,7 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                                                           const AttnParams P) {
     using C = LeanCfg<HD, KVT, NQ>;
     using S = AttendShape<HD, HD, KVT, NQ>;
-    constexpr int NW = C::NW, TR = kTmaRows, STAGES = C::STAGES, SQ = C::SQ;
+    constexpr int NW = C::NW, TR = C::TR, STAGES = C::STAGES, SQ = C::SQ;
     constexpr int PRODUCER = NW, PREP = NW + 1, FINISH = NW + 2;
     constexpr int LPR = S::LPR, RPW = S::RPW, EK = S::EK, EV = S::EV, WK = S::WK, WV = S::WV, ES = S::ES;
     constexpr int RW = TR / NW;              // rows per warp per tile
@@ -577,6 +658,9 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
 #pragma unroll
             for (int e = 0; e < EK; e++) qr[qi][e] = sq[i][qi][sub * EK + e];
         const LeanInfo si = info[i];
+        uint32_t ql[NQ][3][C::I8 ? EK / 4 : 1];
+        float cq[NQ][3];
+        if constexpr (C::I8) q_limbs<NQ, EK, LPR>(qr, ql, cq);
 
         float m[NQ], l[NQ], acc[NQ][EV];
 #pragma unroll
@@ -619,7 +703,9 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
                         ksc[u] = valid[u] ? ks[r * 4 + (d.g & 3u)] : 0.0f;
                         vsc[u] = valid[u] ? vs[r * 4 + (d.g & 3u)] : 0.0f;
                     }
-                    consume<HD, HD, KVT, NQ, UB, true>(qr, kw, vw, ksc, vsc, valid, m, l, acc);
+                    float sc[UB][NQ];
+                    qk_i8dp<NQ, EK, UB>(ql, cq, kw, sc);
+                    consume_scores<HD, HD, KVT, NQ, UB, true>(sc, vw, ksc, vsc, valid, m, l, acc);
                 } else {
                     consume<HD, HD, KVT, NQ, UB>(qr, kw, vw, zero_sc, zero_sc, valid, m, l, acc);
                 }
@@ -643,7 +729,13 @@ __global__ void __launch_bounds__(224) attend_lean_kernel(const __grid_constant_
             const bool valid[1] = {rl == 0};
             load_words<WK, false>(kb + row * (size_t)P.c.k_dim * ES, kw[0]);
             load_words<WV, false>(vb + row * (size_t)P.c.v_dim * ES, vw[0]);
-            consume<HD, HD, KVT, NQ, 1, true>(qr, kw, vw, ksc1, vsc1, valid, m, l, acc);
+            if constexpr (C::I8) {
+                float sc1[1][NQ];
+                qk_i8dp<NQ, EK, 1>(ql, cq, kw, sc1);
+                consume_scores<HD, HD, KVT, NQ, 1, true>(sc1, vw, ksc1, vsc1, valid, m, l, acc);
+            } else {
+                consume<HD, HD, KVT, NQ, 1, true>(qr, kw, vw, ksc1, vsc1, valid, m, l, acc);
+            }
         }
         // Reduce across the row lanes; hand (m, l, acc) of this warp over.
 #pragma unroll

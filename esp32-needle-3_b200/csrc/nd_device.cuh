@@ -34,6 +34,16 @@ namespace nda {
 
 enum : int { DT_I8 = 0, DT_F32 = 1, DT_F16 = 2, DT_BF16 = 3 };
 
+// Rows per TMA box of the TMA-staged decode kernels (16-bit caches); a tile of
+// the balanced kernel is one box, its splits are multiples.
+constexpr int kTmaRows = 64;
+// int8 tiles of the balanced kernel take 128 rows. One lane issues every TMA
+// box, and a box costs its issue about the same whatever its bytes, so int8's
+// half-size rows (and its two scale boxes per tile) would leave that lane the
+// limit at 64 rows.
+constexpr int kLeanRowsI8 = 128;
+constexpr int lean_rows(bool i8) { return i8 ? kLeanRowsI8 : kTmaRows; }
+
 // Per-sequence session state (nd_model.h:130-131: pos, n_sink).
 struct SeqState {
     uint32_t pos, n_sink;
@@ -623,30 +633,19 @@ struct AttendShape {
     static_assert(QK % LPR == 0 && (EK * ES) % 4 == 0, "K chunk");
 };
 
-// Online-softmax update of one warp with UU row groups of loaded K/V words
-// (I8_PERM: the int8 unpack above).
+// Online-softmax update of one warp with UU row groups: s[u][qi] holds this
+// lane's partial q.k of row group u (its EK elements), vw the loaded V words
+// (I8_PERM: the int8 unpack above). Sums the partials over the row's lanes,
+// applies the int8 K scale, masks rows past the item's end, then rescales and
+// accumulates p V.
 template <int QK, int VD, typename KVT, int NQ, int UU, bool I8_PERM = false>
-__device__ __forceinline__ void consume(const float (&qr)[NQ][AttendShape<QK, VD, KVT, NQ>::EK],
-                                        const uint32_t (&kw)[UU][AttendShape<QK, VD, KVT, NQ>::WK],
-                                        const uint32_t (&vw)[UU][AttendShape<QK, VD, KVT, NQ>::WV],
-                                        const float (&ksc)[UU], const float (&vsc)[UU],
-                                        const bool (&valid)[UU], float (&m)[NQ], float (&l)[NQ],
-                                        float (&acc)[NQ][AttendShape<QK, VD, KVT, NQ>::EV]) {
+__device__ __forceinline__ void consume_scores(float (&s)[UU][NQ],
+                                               const uint32_t (&vw)[UU][AttendShape<QK, VD, KVT, NQ>::WV],
+                                               const float (&ksc)[UU], const float (&vsc)[UU],
+                                               const bool (&valid)[UU], float (&m)[NQ], float (&l)[NQ],
+                                               float (&acc)[NQ][AttendShape<QK, VD, KVT, NQ>::EV]) {
     using S = AttendShape<QK, VD, KVT, NQ>;
     constexpr bool SCALED = KvT<KVT>::dt == DT_I8;
-    float s[UU][NQ];
-#pragma unroll
-    for (int u = 0; u < UU; u++) {
-        float kf[S::EK];
-        unpack<KVT, S::WK, I8_PERM>(kw[u], kf);
-#pragma unroll
-        for (int qi = 0; qi < NQ; qi++) {
-            float a = 0.0f;
-#pragma unroll
-            for (int e = 0; e < S::EK; e++) a = fmaf(qr[qi][e], kf[e], a);
-            s[u][qi] = a;
-        }
-    }
 #pragma unroll
     for (int u = 0; u < UU; u++)
 #pragma unroll
@@ -693,6 +692,32 @@ __device__ __forceinline__ void consume(const float (&qr)[NQ][AttendShape<QK, VD
             for (int e = 0; e < S::EV; e++) acc[qi][e] = fmaf(pv, vf[e], acc[qi][e]);
         }
     }
+}
+
+// The same update with the partial q.k of each row group formed in f32 from
+// the loaded K words.
+template <int QK, int VD, typename KVT, int NQ, int UU, bool I8_PERM = false>
+__device__ __forceinline__ void consume(const float (&qr)[NQ][AttendShape<QK, VD, KVT, NQ>::EK],
+                                        const uint32_t (&kw)[UU][AttendShape<QK, VD, KVT, NQ>::WK],
+                                        const uint32_t (&vw)[UU][AttendShape<QK, VD, KVT, NQ>::WV],
+                                        const float (&ksc)[UU], const float (&vsc)[UU],
+                                        const bool (&valid)[UU], float (&m)[NQ], float (&l)[NQ],
+                                        float (&acc)[NQ][AttendShape<QK, VD, KVT, NQ>::EV]) {
+    using S = AttendShape<QK, VD, KVT, NQ>;
+    float s[UU][NQ];
+#pragma unroll
+    for (int u = 0; u < UU; u++) {
+        float kf[S::EK];
+        unpack<KVT, S::WK, I8_PERM>(kw[u], kf);
+#pragma unroll
+        for (int qi = 0; qi < NQ; qi++) {
+            float a = 0.0f;
+#pragma unroll
+            for (int e = 0; e < S::EK; e++) a = fmaf(qr[qi][e], kf[e], a);
+            s[u][qi] = a;
+        }
+    }
+    consume_scores<QK, VD, KVT, NQ, UU, I8_PERM>(s, vw, ksc, vsc, valid, m, l, acc);
 }
 
 // Merge of one CTA's warps and of the splits of a (token, KV head): warps

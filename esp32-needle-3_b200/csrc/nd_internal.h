@@ -14,11 +14,9 @@ inline bool head_dims_supported(unsigned qk, unsigned vd) {
 }
 inline int nq_for_rep(unsigned rep) { return rep <= 1 ? 1 : rep <= 2 ? 2 : rep <= 4 ? 4 : 8; }
 
-// Rows per TMA box of the TMA-staged decode kernel; its splits are multiples.
-#ifndef ND_TMA_ROWS_DEFINED
-#define ND_TMA_ROWS_DEFINED
-constexpr int kTmaRows = 64;
-#endif
+// Sets the calling thread's nd_attn_last_error() message (printf-style) and
+// returns `code`.
+int report_error(int code, const char *fmt, ...);
 
 // Rows one attend CTA consumes per loop iteration (a split is a multiple).
 int attend_rows_per_iter(int kv_dt, int vd, int nq);

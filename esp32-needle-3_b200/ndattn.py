@@ -26,6 +26,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libndattn.so")
 HEADER_PATH = os.path.join(os.path.dirname(HERE), "include", "nd_attn.h")
+HEADER_PATHS = [HEADER_PATH, os.path.join(os.path.dirname(HERE), "include", "nd_cq.h")]
 
 DT_I8, DT_F32, DT_F16, DT_BF16 = 0, 1, 2, 3
 DT_NAMES = {"i8": DT_I8, "int8": DT_I8, "f32": DT_F32, "float32": DT_F32, "f16": DT_F16,
@@ -50,13 +51,27 @@ class Config(ctypes.Structure):
                 ("qkv_conv_taps", c_uint32)]
 
 
+class CqTensor(ctypes.Structure):
+    """nd_cq_tensor (include/nd_cq.h): one decoded .cact directory record."""
+    _fields_ = [("dtype", ctypes.c_uint8), ("ndim", ctypes.c_uint8), ("shape", c_uint32 * 4),
+                ("offset", c_uint64), ("nbytes", c_uint64), ("group", c_uint32), ("bits", c_uint32)]
+
+
+# Per-layer slots of a .cact archive (bind_layer, engine/src/nd_model.c:646-654).
+CQ_SLOTS = ["norm_in", "q_proj", "k_proj", "v_proj", "q_taps", "k_taps", "v_taps", "q_norm", "k_norm",
+            "gate_proj", "out_proj", "post_norm", "attn_gate", "pre_hada", "d1", "d2", "b2", "d3", "d4",
+            "w1a", "w1b", "w2a", "w2b", "w3a", "w3b", "cond_v", "cond_u"]
+
 _lib = None
 
 
-def header_functions(path: str = HEADER_PATH) -> list[str]:
-    """Names of every entry point include/nd_attn.h declares."""
-    src = open(path).read()
-    return sorted(set(re.findall(r"^ND_ATTN_API\s+[^(;]*?\b(nd_attn_\w+)\s*\(", src, re.M)))
+def header_functions(paths=None) -> list[str]:
+    """Names of every entry point include/nd_attn.h and include/nd_cq.h declare."""
+    names = set()
+    for path in paths or HEADER_PATHS:
+        src = open(path).read()
+        names |= set(re.findall(r"^ND_ATTN_API\s+[^(;]*?\b(nd_(?:attn|cq)_\w+)\s*\(", src, re.M))
+    return sorted(names)
 
 
 def load(path: str = LIB_PATH) -> ctypes.CDLL:
@@ -101,6 +116,13 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "nd_attn_sync": (c_int, [vp]),
         "nd_attn_selftest_wait": (c_int, [vp, u32]),
         "nd_attn_stream": (vp, [vp]),
+        "nd_cq_open": (c_int, [vp, c_size_t, c_int, POINTER(vp)]),
+        "nd_cq_close": (None, [vp]),
+        "nd_cq_header": (c_int, [vp, vp]),
+        "nd_cq_tensor_info": (c_int, [vp, u32, POINTER(CqTensor)]),
+        "nd_cq_layer_tensor": (c_int, [vp, u32, u32, u32p]),
+        "nd_cq_read_f32": (c_int, [vp, u32, vp, c_size_t]),
+        "nd_cq_project": (c_int, [vp, u32, vp, u32, vp, vp, vp]),
         "nd_attn_set_stream": (c_int, [vp, vp]),
         "nd_attn_launch_count": (c_uint64, [vp]),
         "nd_attn_last_error": (c_char_p, []),
@@ -360,3 +382,56 @@ class Attn:
     @property
     def launches(self) -> int:
         return load().nd_attn_launch_count(self.h)
+
+
+class CQ:
+    """A `.cact` archive through nd_cq_open (include/nd_cq.h): its header and
+    directory, FP16 tensors as floats, and the CQ2 projections on the device
+    (device < 0 opens it for reading only)."""
+
+    def __init__(self, blob: bytes, device: int = 0):
+        self._buf = ctypes.create_string_buffer(bytes(blob), len(blob))
+        h = c_void_p()
+        _check(load().nd_cq_open(self._buf, len(blob), device, ctypes.byref(h)))
+        self.h = h
+
+    def close(self) -> None:
+        if self.h:
+            load().nd_cq_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def header(self) -> np.ndarray:
+        w = np.zeros(49, np.uint32)
+        _check(load().nd_cq_header(self.h, w.ctypes.data))
+        return w
+
+    def tensor(self, index: int) -> CqTensor:
+        t = CqTensor()
+        _check(load().nd_cq_tensor_info(self.h, index, ctypes.byref(t)))
+        return t
+
+    def layer_tensor(self, layer: int, slot) -> int:
+        i = c_uint32()
+        sl = CQ_SLOTS.index(slot) if isinstance(slot, str) else slot
+        _check(load().nd_cq_layer_tensor(self.h, layer, sl, ctypes.byref(i)))
+        return i.value
+
+    def read_f32(self, index: int) -> np.ndarray:
+        t = self.tensor(index)
+        n = t.nbytes // (2 if t.dtype == 1 else 4)
+        out = np.zeros(max(n, 1), np.float32)
+        _check(load().nd_cq_read_f32(self.h, index, out.ctypes.data, out.size))
+        return out[:n]
+
+    def project(self, tensors, n_tok: int, x, ys, stream=None) -> None:
+        """ys[i] = W_i x for CQ2 tensors reducing over one input (device
+        tensors: x [n_tok][in] f32, ys[i] [n_tok][out_i] f32)."""
+        ids = np.ascontiguousarray(np.asarray(tensors, dtype=np.uint32))
+        outs = (c_void_p * len(ys))(*[_ptr(y) for y in ys])
+        _check(load().nd_cq_project(self.h, len(ids), ids.ctypes.data, n_tok, _ptr(x), outs, stream))

@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import struct
 from ctypes import POINTER, c_double, c_float, c_int, c_int32, c_long, c_size_t, c_uint16, c_uint32, c_void_p
 
 import numpy as np
@@ -105,6 +106,10 @@ def ref() -> ctypes.CDLL:
                                            POINTER(c_uint32)]
         lib.ndref_norm_rope.restype = c_int
         lib.ndref_norm_rope.argtypes = [POINTER(RefGeom), c_void_p, c_uint32, c_void_p, c_void_p, c_void_p]
+        lib.ndref_cq_project.restype = c_int
+        lib.ndref_cq_project.argtypes = [c_void_p, c_size_t, c_uint32, c_void_p, c_void_p]
+        lib.ndref_attention_layer.restype = c_int
+        lib.ndref_attention_layer.argtypes = [c_void_p, c_size_t, c_uint32, c_uint32, c_uint32] + [c_void_p] * 11
         lib.ndref_tap.restype = c_int
         lib.ndref_tap.argtypes = [c_uint32, c_uint32, c_uint32, c_void_p, c_void_p, c_void_p]
         lib.ndref_prefill_bench.restype = c_double
@@ -353,6 +358,54 @@ def ref_norm_rope(x, n_heads, qk, theta, pos, norm=None):
     nm = None if norm is None else np.ascontiguousarray(norm, dtype=np.float32)
     assert ref().ndref_norm_rope(ctypes.byref(g), y.ctypes.data, n_heads, _p(nm), cs.ctypes.data, sn.ctypes.data) == 0
     return y
+
+
+def ref_cq_project(blob: bytes, index: int, x):
+    """W x for CQ2 tensor `index` of a .cact archive through the reference's
+    own nd_cq_prepare + nd_cq_lut_build + nd_cq_gemv_lut2 (nd_quant.c)."""
+    buf = ctypes.create_string_buffer(blob, len(blob))
+    out_rows = struct.unpack_from("<I", blob, _cact_record(blob, index) + 4)[0]
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.zeros(out_rows, np.float32)
+    assert ref().ndref_cq_project(buf, len(blob), index, x.ctypes.data, y.ctypes.data) == 0
+    return y
+
+
+def _cact_record(blob: bytes, index: int) -> int:
+    """Byte offset of directory record `index` (nd_cact.c: header 196 B, then the codebook)."""
+    cb_len = struct.unpack_from("<I", blob, 8)[0]
+    return 196 + 4 * cb_len + 44 * index
+
+
+class RefAttentionLayer:
+    """The reference's whole attention() on layer 0 of a .cact archive, one
+    token per call (ndref_attention_layer): owns the int8 caches, scales and
+    QKV tap histories of one sequence."""
+
+    def __init__(self, blob: bytes, window: int, n_sink: int = 0):
+        h = struct.unpack_from("<48If", blob, 0)
+        self.blob = ctypes.create_string_buffer(blob, len(blob))
+        self.size = len(blob)
+        (self.d_model, self.n_heads, self.n_kv, self.qk, self.vd) = h[7], h[8], h[9], h[11], h[12]
+        self.taps, self.theta = h[19], h[48]
+        self.window, self.n_sink = window, n_sink
+        self.k_cache = np.zeros((window, self.n_kv * self.qk), np.int8)
+        self.v_cache = np.zeros((window, self.n_kv * self.vd), np.int8)
+        self.k_scale = np.zeros((window, self.n_kv), np.float32)
+        self.v_scale = np.zeros((window, self.n_kv), np.float32)
+        self.q_hist = np.zeros((self.taps, self.n_heads * self.qk), np.float32)
+        self.k_hist = np.zeros((self.taps, self.n_kv * self.qk), np.float32)
+        self.v_hist = np.zeros((self.taps, self.n_kv * self.vd), np.float32)
+
+    def step(self, pos: int, x):
+        cs, sn = ref_rope(self.theta, self.qk, pos)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.zeros(self.d_model, np.float32)
+        arrs = [self.k_cache, self.v_cache, self.k_scale, self.v_scale, cs, sn, self.q_hist, self.k_hist,
+                self.v_hist, x, out]
+        assert ref().ndref_attention_layer(self.blob, self.size, self.window, pos, self.n_sink,
+                                           *[a.ctypes.data for a in arrs]) == 0
+        return out
 
 
 def ref_rope(theta, qk, pos):

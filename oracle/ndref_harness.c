@@ -409,3 +409,98 @@ double ndref_prefill_bench(const ndref_geom *g, uint32_t n_seqs, uint32_t tokens
     }
     return worst;
 }
+
+/* ---- CQ2 projections and the whole attention() over a .cact archive ------
+ *
+ * The archive is parsed by the reference's own nd_cact_open (nd_cact.c), its
+ * layer-0 tensors bound by bind_layer (nd_model.c:642-658) and its fp16 slots
+ * converted by nd_f16, as nd_model_open does (nd_model.c:771-830). */
+
+/* y[0..shape[0]) = W x for CQ2 tensor `index` through the reference's own
+ * nd_cq_prepare + nd_cq_lut_build + nd_cq_gemv_lut2 (the path attention()
+ * takes for q/k/v/gate/out, nd_model.c:2402-2411, 2495-2501). */
+int ndref_cq_project(const void *blob, size_t size, uint32_t index, const float *x, float *y)
+{
+    nd_cact   c;
+    nd_tensor t;
+    float    *xh, *lut;
+    uint32_t  in_pad;
+    if (nd_cact_open(&c, blob, size) != 0 || nd_cact_tensor(&c, index, &t) != 0) return -1;
+    if (t.dtype != ND_DT_CQ || t.bits != 2) return -2;
+    in_pad = nd_cq_in_pad(&t);
+    xh  = (float *)malloc(sizeof(float) * in_pad);
+    lut = (float *)malloc(sizeof(float) * nd_cq_lut_floats(in_pad));
+    if (!xh || !lut) { free(xh); free(lut); return -12; }
+    nd_cq_prepare(&t, x, xh);
+    nd_cq_lut_build(&c, xh, in_pad, lut);
+    nd_cq_gemv_lut2(&t, nd_cact_data(&c, &t), lut, y);
+    free(xh); free(lut);
+    return 0;
+}
+
+/* One token of the reference's attention() (nd_model.c:2382-2502) on layer 0
+ * of the archive: CQ2 q/k/v/gate projections, the three QKV taps, head norm +
+ * RoPE, the int8 KV store, attn_heads, the output gate and the CQ2 out
+ * projection, all by the reference's own functions. The caller owns the
+ * layer-0 caches ([window][k_dim] int8, [window][n_kv] scales), the tap
+ * histories ([taps][dim] each) and the position's RoPE row (hd/2 cos, sin). */
+int ndref_attention_layer(const void *blob, size_t size, uint32_t window, uint32_t pos, uint32_t n_sink,
+                          int8_t *k_cache, int8_t *v_cache, float *k_scale, float *v_scale,
+                          const float *rope_cos, const float *rope_sin,
+                          float *q_hist, float *k_hist, float *v_hist, const float *xin, float *out)
+{
+    static const int F16[] = { 4, 5, 6, 7, 8 };   /* q/k/v taps, q_norm, k_norm */
+    nd_model  m;
+    nd_layer  L;
+    uint32_t  i, k, in_pad = 0;
+    int       rc = 0;
+    memset(&m, 0, sizeof(m));
+    if (nd_cact_open(&m.c, blob, size) != 0) return -1;
+    if (m.c.h.num_layers < 1 || m.c.h.qkv_conv_taps == 0) return -2;
+    m.d_model     = m.c.h.d_model;
+    m.n_layers    = 1;
+    m.n_heads     = m.c.h.num_heads;
+    m.n_kv_heads  = m.c.h.num_kv_heads;
+    m.qk_head_dim = m.c.h.qk_head_dim;
+    m.v_head_dim  = m.c.h.v_head_dim;
+    m.attn_dim    = m.n_heads * m.v_head_dim;
+    m.k_dim       = m.n_kv_heads * m.qk_head_dim;
+    m.v_dim       = m.n_kv_heads * m.v_head_dim;
+    m.window      = window;
+    if (m.qk_head_dim > ND_KV_HD_CAP || m.v_head_dim > ND_KV_HD_CAP) return -10;
+    m.layer = &L;
+    bind_layer(&m, 0);
+    {
+        const nd_tensor *proj[5] = { &L.q_proj, &L.k_proj, &L.v_proj, &L.gate_proj, &L.out_proj };
+        for (i = 0; i < 5; i++)
+            if (nd_cq_in_pad(proj[i]) > in_pad) in_pad = nd_cq_in_pad(proj[i]);
+    }
+    for (k = 0; k < 5; k++) {
+        nd_tensor       t;
+        const uint16_t *h;
+        nd_cact_tensor(&m.c, 1 + (m.c.h.qkv_conv_taps ? 27 : 24) * 0 + F16[k], &t);
+        h = (const uint16_t *)nd_cact_data(&m.c, &t);
+        m.fp16_slot[0][F16[k]] = (float *)malloc(sizeof(float) * (t.nbytes / 2 + 1));
+        if (!h || !m.fp16_slot[0][F16[k]]) { rc = -12; goto out; }
+        for (i = 0; i < t.nbytes / 2; i++) m.fp16_slot[0][F16[k]][i] = nd_f16(h[i]);
+    }
+    m.xh   = (float *)malloc(sizeof(float) * in_pad);
+    m.lut  = (float *)malloc(sizeof(float) * nd_cq_lut_floats(in_pad));
+    m.q    = (float *)malloc(sizeof(float) * m.n_heads * m.qk_head_dim);
+    m.kbuf = (float *)malloc(sizeof(float) * m.k_dim);
+    m.vbuf = (float *)malloc(sizeof(float) * m.v_dim);
+    m.gate = (float *)malloc(sizeof(float) * m.attn_dim);
+    m.attn = (float *)malloc(sizeof(float) * m.attn_dim);
+    if (!m.xh || !m.lut || !m.q || !m.kbuf || !m.vbuf || !m.gate || !m.attn) { rc = -12; goto out; }
+    m.pos = pos;
+    m.n_sink = n_sink;
+    m.k_cache = k_cache; m.v_cache = v_cache;
+    m.k_scale = k_scale; m.v_scale = v_scale;
+    m.rope_cos = (float *)rope_cos; m.rope_sin = (float *)rope_sin;
+    m.q_hist = q_hist; m.k_hist = k_hist; m.v_hist = v_hist;
+    attention(&m, 0, xin, out);
+out:
+    for (k = 0; k < 5; k++) free(m.fp16_slot[0][F16[k]]);
+    free(m.xh); free(m.lut); free(m.q); free(m.kbuf); free(m.vbuf); free(m.gate); free(m.attn);
+    return rc;
+}

@@ -184,11 +184,12 @@ def test_config4_geometry_long_context_paged():
     a.close()
 
 
-@pytest.mark.parametrize("hd,rep,block_size", [(64, 1, 0), (64, 2, 0), (64, 1, 256), (128, 1, 64), (128, 2, 0)])
+@pytest.mark.parametrize("hd,rep,block_size", [(64, 1, 0), (64, 2, 0), (64, 1, 256), (128, 1, 128), (128, 2, 0), (64, 1, 64)])
 def test_int8_balanced_decode(hd, rep, block_size):
     """int8 caches (the reference's own format, f32 activations) through the
     balanced kernel: KV-head counts whose scale rows are 16-byte multiples,
-    so the scales arrive as TMA boxes beside the int8 rows. Every slot is
+    so the scales arrive as TMA boxes beside the int8 rows (128-row tiles;
+    64-row pages hold no whole tile and take the exact-grid kernel). Every slot is
     first poisoned with arbitrary int8 bytes and NaN scales; ragged contexts
     are then filled by prefill (K1 append + the balanced attend, outputs
     checked too) and decoded for two steps. Outputs within TOL of the oracle,
