@@ -26,6 +26,7 @@ the same workloads.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -520,6 +521,135 @@ def run_decode_int8(args, world, rank, local, dist):
             "gpu_launches": int(launches)}
 
 
+# ------------------------------------------- GPU: real-model attention block
+def run_layer_block(args, world, rank, local, dist):
+    """One layer of the reference model's attention block on a synthetic .cact
+    archive (tests/golden/make_cact.py: 12 q / 2 kv heads, qk 48, v 64, d_model
+    768, CQ2 group 128, 3 QKV taps, theta 1e5, window 384): per step, 64
+    sequences at positions U[128, 320] (seed 5000 + rank) go through the CQ2
+    q/k/v/gate projections (nd_cq_project), the int8-KV decode with taps, head
+    norms, RoPE and gate (nd_attn_decode), and the CQ2 out projection, all on
+    the handle's stream. Reports tok/s of the whole block and the share of its
+    time in the projections; the CPU line is the reference's own attention()
+    (oracle/_ref ndref_attention_layer) on one host thread."""
+    import numpy as np
+    import torch
+
+    import ndattn
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import make_cact as MC
+
+    K, Wm, B, Wn = args.steps, args.warmup, BATCH, 384
+    blob, _ = MC.synthetic_cact(seed=7)
+    cq = ndattn.CQ(blob, device=local)
+    hd = cq.header()
+    dm, Hh, Hk, qk, vd, taps = (int(hd[i]) for i in (7, 8, 9, 11, 12, 19))
+    theta = float(np.frombuffer(np.uint32(hd[48]).tobytes(), np.float32)[0])
+    a = ndattn.Attn(n_layers=1, n_heads=Hh, n_kv_heads=Hk, qk_head_dim=qk, v_head_dim=vd, window=Wn,
+                    max_seqs=B, rope_theta=theta, kv_dtype="i8", act_dtype="f32", out_dtype="f32",
+                    qkv_conv_taps=taps, device=local)
+    ids = {s_: cq.layer_tensor(0, s_) for s_ in MC.SLOTS}
+    a.set_head_norm(0, cq.read_f32(ids["q_norm"]), cq.read_f32(ids["k_norm"]))
+    a.set_conv_taps(0, *(cq.read_f32(ids[s_]).reshape(taps, -1) for s_ in ("q_taps", "k_taps", "v_taps")))
+    rng = np.random.default_rng(5000 + rank)
+    ctx = rng.integers(128, 321, size=B)
+    for s_ in range(B):
+        n = int(ctx[s_])
+        kk = torch.from_numpy(rng.integers(-127, 128, size=(n, Hk * qk), dtype=np.int8)).cuda()
+        vv = torch.from_numpy(rng.integers(-127, 128, size=(n, Hk * vd), dtype=np.int8)).cuda()
+        ks = torch.from_numpy(rng.uniform(0.005, 0.02, size=(n, Hk)).astype(np.float32)).cuda()
+        vs = torch.from_numpy(rng.uniform(0.005, 0.02, size=(n, Hk)).astype(np.float32)).cuda()
+        a.write_cache(0, s_, 0, n, kk, vv, ks, vs)
+        torch.cuda.synchronize()
+        a.set_state(s_, n, 0)
+    nsteps = K + Wm
+    x = torch.randn((nsteps, B, dm), device="cuda")
+    q = torch.empty((B, Hh * qk), device="cuda")
+    k = torch.empty((B, Hk * qk), device="cuda")
+    v = torch.empty((B, Hk * vd), device="cuda")
+    g = torch.empty((B, Hh * vd), device="cuda")
+    at = torch.empty((B, Hh * vd), device="cuda")
+    y = torch.empty((nsteps, B, dm), device="cuda")
+    lib = ndattn.load()
+    st = a.stream
+    ids_in = np.array([ids["q_proj"], ids["k_proj"], ids["v_proj"], ids["gate_proj"]], np.uint32)
+    ids_out = np.array([ids["out_proj"]], np.uint32)
+    outs_in = (ctypes.c_void_p * 4)(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr())
+    outs_y = [(ctypes.c_void_p * 1)(addr(y, i)) for i in range(nsteps)]
+    dc = Direct(a)
+
+    def project_in(i):
+        rc = lib.nd_cq_project(cq.h, 4, ids_in.ctypes.data, B, addr(x, i), outs_in, st)
+        if rc:
+            raise RuntimeError(f"projection failed ({rc}): {lib.nd_attn_last_error()}")
+
+    def step(i, attend=True):
+        project_in(i)
+        if attend:
+            dc.decode(0, B, q.data_ptr(), k.data_ptr(), v.data_ptr(), at.data_ptr())
+        rc = lib.nd_cq_project(cq.h, 1, ids_out.ctypes.data, B, at.data_ptr(), outs_y[i], st)
+        if rc:
+            raise RuntimeError(f"projection failed ({rc}): {lib.nd_attn_last_error()}")
+        if attend:
+            dc.advance(B)
+
+    stream = torch.cuda.ExternalStream(st)
+
+    def timed(attend):
+        for i in range(Wm):
+            step(i, attend)
+        a.sync()
+        torch.cuda.synchronize()
+        l0 = a.launches
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(K):
+            step(Wm + i, attend)
+        e1.record(stream)
+        a.sync()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / K, a.launches - l0
+
+    ms, launches = timed(True)
+    for s_ in range(B):
+        a.set_state(s_, int(ctx[s_]), 0)
+    ms_proj, _ = timed(False)
+    a.close()
+    cq.close()
+    t = torch.tensor([ms, ms_proj], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ms_proj = float(t[0]), float(t[1])
+    out = {"value": B * world / (ms / 1e3), "unit": "tok/s (one layer's attention block per token)",
+           "ms_per_step": ms, "steps": K, "projection_ms_per_step": ms_proj,
+           "projection_share": ms_proj / ms,
+           "config": "synthetic .cact archive, reference model attention geometry (12/2 heads, qk 48, v 64, "
+                     "d_model 768, CQ2 group 128, 3 QKV taps), int8 KV, 64 sequences at positions U[128, 320]",
+           "gpu_launches": int(launches) + 7 * K,   # per step: 1 + 4 and 1 + 1 projection kernels
+           "kernels": "cq_prepare_kernel + cq_rows_kernel (x2 calls), attend kernel of nd_attn_decode, taps kernel"}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        O = _oracle()
+        ref = O.RefAttentionLayer(blob, Wn)
+        ref.k_cache[:] = rng.integers(-127, 128, size=ref.k_cache.shape, dtype=np.int8)
+        ref.v_cache[:] = rng.integers(-127, 128, size=ref.v_cache.shape, dtype=np.int8)
+        ref.k_scale[:] = 0.01
+        ref.v_scale[:] = 0.01
+        xs = rng.standard_normal((64, dm)).astype(np.float32)
+        pos = [int(p_) for p_ in rng.integers(128, 321, size=64)]
+        ref.step(pos[0], xs[0])
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < 5.0 and n < 4096:
+            ref.step(pos[n % 64], xs[n % 64])
+            n += 1
+        secs = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": n / secs, "unit": out["unit"], "cores": 1, "kind": "reference",
+                               "sample": f"{n} tokens of the reference's attention() (nd_model.c:2382-2502: CQ2 "
+                                         "projections, taps, norm + RoPE, int8 KV store, attn_heads, gate, out "
+                                         "projection) at positions U[128, 320], one thread"}
+    return out
+
+
 # ------------------------------------------------------- GPU: head-sharded decode
 def run_decode_taps(args, world, rank, local, dist, plain_value):
     """Config 2 with the reference model's 3-tap QKV short causal convolution
@@ -986,6 +1116,7 @@ def run_ours(args):
         pre = run_prefill(args, world, rank, local, dist) if args.prefill_steps > 0 else None
         lng = run_long(args, world, rank, local, dist) if args.long_steps > 0 else None
         srv = run_serve(args, world, rank, local, dist) if args.serve else None
+        blk = run_layer_block(args, world, rank, local, dist)
         cpu = None
         if rank == 0 and world == 1 and not args.no_cpu:
             v_cpu, cores, sample = cpu_decode(10.0, 0)
@@ -1009,9 +1140,9 @@ def run_ours(args):
                     "roofline": dec["roofline"], "cpu_baseline": cpu, "e2e": dec["e2e"],
                     "gpu_launches": dec["gpu_launches"] + (pre["gpu_launches"] if pre else 0)
                     + (lng["gpu_launches"] if lng else 0) + (srv["gpu_launches"] if srv else 0)
-                    + taps["gpu_launches"] + i8["gpu_launches"],
+                    + taps["gpu_launches"] + i8["gpu_launches"] + blk["gpu_launches"],
                     "clocks": dec["clocks"], "prefill": pre, "long_decode": lng, "serving": srv,
-                    "head_sharded": heads, "conv_taps": taps, "decode_int8": i8}
+                    "head_sharded": heads, "conv_taps": taps, "decode_int8": i8, "layer_block": blk}
             print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -12,24 +12,19 @@
 //   y_r = sum over groups of f16(norm) * ((s0 + s1) + (s2 + s3)), s_k the
 //         running sums of the table entries that the k-th nibble of each 16-bit
 //         half-word of the row's index words selects   nd_lut2_rows_c 722-763
-// Both kernels below evaluate exactly these statements in this order, with
+// The kernel below evaluates exactly these statements in this order, with
 // explicitly rounded float operations (no contraction into FMAs: the
 // reference's engine build has none on its target and the checker is built
 // with -ffp-contract=off), so the outputs are the reference's bit for bit.
 //
-// Kernels:
-//   cq_prepare_kernel  one CTA per token: stage x in shared memory, run the
-//                      per-group butterflies stage by stage (every butterfly
-//                      of a stage in parallel: each element's sequence of
-//                      adds is the reference's whatever the order), scale,
-//                      then write the token's pair table to global memory.
-//   cq_rows_kernel     one thread per (output row, token); the token's table
-//                      is staged in shared memory once per CTA and every
-//                      thread walks its own row's index words and norms.
-// The projections of the attention block are small (the reference model's
-// q/k/v/gate/out are 768 x 768 at most, 2 bits per weight): these kernels
-// are latency-bound by design and sized for correctness over a batch of
-// tokens, not for the tensor cores.
+// One launch per call (cq_project_kernel): a CTA takes 128 output rows of one
+// of the call's tensors for TT tokens, rebuilds those tokens' transforms and
+// pair tables in shared memory (cheap next to the row walks, and no table
+// round trip through global memory), then every thread walks its row's index
+// words once for all TT tokens. The projections of the attention block are
+// small (the reference model's q/k/v/gate/out are 768 x 768 at most, 2 bits
+// per weight): work per call is a few microseconds of table lookups, not
+// tensor-core shaped.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -49,7 +44,8 @@ constexpr uint32_t kHeaderWords = ND_CQ_HEADER_WORDS;
 constexpr uint32_t kHeaderBytes = kHeaderWords * 4;
 constexpr uint32_t kRecordBytes = 44;
 constexpr uint32_t kTag = 0x05E12A84u;
-constexpr uint32_t kMaxInPad = 4096;   // pair table of a token: in_pad * 8 floats in shared memory
+constexpr uint32_t kMaxInPad = 4096;   // one token's table and transform: in_pad * 36 bytes of shared memory
+constexpr size_t kSmemBudget = 112 * 1024;   // two CTAs per SM where TT allows
 constexpr int kRowsPerCta = 128;
 
 uint32_t rd_u32(const uint8_t *p) {
@@ -64,80 +60,125 @@ float half_bits_to_float(uint16_t h) {
     return __half2float(__half(r));
 }
 
-__global__ void __launch_bounds__(256) cq_prepare_kernel(const float *__restrict__ x, uint32_t in, uint32_t in_pad,
-                                                         uint32_t g, float scale, const float *__restrict__ cb2,
-                                                         float *__restrict__ lut) {
-    extern __shared__ float xh[];
-    const uint32_t tok = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
-    const float *xr = x + (size_t)tok * in;
-    for (uint32_t i = tid; i < in_pad; i += nt) xh[i] = i < in ? xr[i] : 0.0f;
+// The tensors of one nd_cq_project call, each a run of 128-row blocks of the
+// grid's x dimension.
+constexpr int kMaxJobs = 8;
+struct CqJob {
+    const uint8_t *packed;     // [out][rowbytes] indices
+    const uint16_t *norms;     // [out][ngroup] f16
+    float *y;                  // [n_tok][out]
+    uint32_t out, rb0;         // rows, first row block
+};
+struct CqJobs {
+    CqJob job[kMaxJobs];
+    uint32_t n;
+};
+
+// One CTA of 128 x TT threads: 128 output rows of one tensor for TT tokens.
+// Phase 1 stages the tokens' activations, runs the per-group butterflies
+// (every butterfly of a stage in parallel: each element's sequence of adds is
+// the reference's whatever the order), scales, and builds the tokens' pair
+// tables in shared memory. Phase 2: thread (row, token) walks the row's index
+// words and norms and accumulates in the reference's order (per group the
+// four running sums, then acc += f16(norm) * ((s0 + s1) + (s2 + s3))).
+template <int TT>
+__global__ void __launch_bounds__(kRowsPerCta * 4) cq_project_kernel(const float *__restrict__ x, uint32_t n_tok,
+                                                                 uint32_t in, uint32_t in_pad, uint32_t g, float scale,
+                                                                 float4 cb, const __grid_constant__ CqJobs jobs) {
+    extern __shared__ float4 smem4[];
+    float *lut = reinterpret_cast<float *>(smem4);          // [TT][in_pad / 2][16]
+    float *xh = lut + (size_t)TT * in_pad * 8;               // [TT][in_pad]
+    const uint32_t tid = threadIdx.x, nt = blockDim.x, t0 = blockIdx.y * TT;
+    const uint32_t ntt = min((uint32_t)TT, n_tok - t0);
+#pragma unroll
+    for (int tt = 0; tt < TT; tt++)
+        for (uint32_t c = tid; c < in_pad; c += nt)
+            xh[(size_t)tt * in_pad + c] = (uint32_t)tt < ntt && c < in ? x[(size_t)(t0 + tt) * in + c] : 0.0f;
     __syncthreads();
-    // nd_fwht (nd_quant.c:20-58): stages len = 1, 2, .., g/2; each butterfly
+    // nd_fwht (nd_quant.c:20-58): stages len = 1, 2, .., g/2; butterfly
     // (j, j + len) of a block of 2 len within a group becomes (a + b, a - b).
-    const uint32_t half_g = g / 2, npairs = in_pad / 2;
-    for (uint32_t len = 1; len < g; len <<= 1) {
-        for (uint32_t b = tid; b < npairs; b += nt) {
-            const uint32_t gi = b / half_g, k = b % half_g;
-            const uint32_t j = gi * g + (k / len) * 2 * len + (k % len);
-            const float a = xh[j], c = xh[j + len];
-            xh[j] = __fadd_rn(a, c);
-            xh[j + len] = __fsub_rn(a, c);
+    // g is a power of two: butterfly b of a token sits in group b >> lg_h at
+    // (k >> ls) << (ls + 1) | (k & (len - 1)), k = b & (g/2 - 1).
+    const uint32_t half_g = g / 2, npairs = in_pad / 2, lg_h = __ffs(half_g) - 1;
+    for (uint32_t ls = 0, len = 1; len < g; ls++, len <<= 1) {
+#pragma unroll
+        for (int tt = 0; tt < TT; tt++) {
+            float *xt = xh + (size_t)tt * in_pad;
+            for (uint32_t b = tid; b < npairs; b += nt) {
+                const uint32_t k = b & (half_g - 1);
+                float *blk = xt + ((b >> lg_h) << (lg_h + 1)) + ((k >> ls) << (ls + 1)) + (k & (len - 1));
+                const float a = blk[0], c = blk[len];
+                blk[0] = __fadd_rn(a, c);
+                blk[len] = __fsub_rn(a, c);
+            }
         }
         __syncthreads();
     }
-    // fw_scale (nd_quant.c:99-110), then the pair table (lutb_rows).
-    const float c0 = cb2[0], c1 = cb2[1], c2 = cb2[2], c3 = cb2[3];
-    float4 *T4 = reinterpret_cast<float4 *>(lut + (size_t)tok * npairs * 16);
+    // fw_scale (nd_quant.c:99-110), then the pair table (lutb_rows, 75-97):
+    // T[i0 + 4 i1] = cb[i0] x0 + cb[i1] x1.
+#pragma unroll
+    for (int tt = 0; tt < TT; tt++)
     for (uint32_t p = tid; p < npairs; p += nt) {
-        const float x0 = __fmul_rn(xh[2 * p], scale), x1 = __fmul_rn(xh[2 * p + 1], scale);
-        const float a0 = __fmul_rn(c0, x0), a1 = __fmul_rn(c1, x0), a2 = __fmul_rn(c2, x0), a3 = __fmul_rn(c3, x0);
-        const float b0 = __fmul_rn(c0, x1), b1 = __fmul_rn(c1, x1), b2 = __fmul_rn(c2, x1), b3 = __fmul_rn(c3, x1);
-        T4[4 * p + 0] = make_float4(__fadd_rn(a0, b0), __fadd_rn(a1, b0), __fadd_rn(a2, b0), __fadd_rn(a3, b0));
-        T4[4 * p + 1] = make_float4(__fadd_rn(a0, b1), __fadd_rn(a1, b1), __fadd_rn(a2, b1), __fadd_rn(a3, b1));
-        T4[4 * p + 2] = make_float4(__fadd_rn(a0, b2), __fadd_rn(a1, b2), __fadd_rn(a2, b2), __fadd_rn(a3, b2));
-        T4[4 * p + 3] = make_float4(__fadd_rn(a0, b3), __fadd_rn(a1, b3), __fadd_rn(a2, b3), __fadd_rn(a3, b3));
+        const float x0 = __fmul_rn(xh[(size_t)tt * in_pad + 2 * p], scale);
+        const float x1 = __fmul_rn(xh[(size_t)tt * in_pad + 2 * p + 1], scale);
+        const float a0 = __fmul_rn(cb.x, x0), a1 = __fmul_rn(cb.y, x0), a2 = __fmul_rn(cb.z, x0),
+                    a3 = __fmul_rn(cb.w, x0);
+        const float b0 = __fmul_rn(cb.x, x1), b1 = __fmul_rn(cb.y, x1), b2 = __fmul_rn(cb.z, x1),
+                    b3 = __fmul_rn(cb.w, x1);
+        float4 *T4 = reinterpret_cast<float4 *>(lut + ((size_t)tt * npairs + p) * 16);
+        T4[0] = make_float4(__fadd_rn(a0, b0), __fadd_rn(a1, b0), __fadd_rn(a2, b0), __fadd_rn(a3, b0));
+        T4[1] = make_float4(__fadd_rn(a0, b1), __fadd_rn(a1, b1), __fadd_rn(a2, b1), __fadd_rn(a3, b1));
+        T4[2] = make_float4(__fadd_rn(a0, b2), __fadd_rn(a1, b2), __fadd_rn(a2, b2), __fadd_rn(a3, b2));
+        T4[3] = make_float4(__fadd_rn(a0, b3), __fadd_rn(a1, b3), __fadd_rn(a2, b3), __fadd_rn(a3, b3));
     }
-}
-
-__global__ void __launch_bounds__(kRowsPerCta) cq_rows_kernel(const uint8_t *__restrict__ packed,
-                                                              const uint16_t *__restrict__ norms, uint32_t out,
-                                                              uint32_t rowbytes, uint32_t ngroup, uint32_t g,
-                                                              uint32_t in_pad, const float *__restrict__ lut,
-                                                              float *__restrict__ y) {
-    extern __shared__ float T_s[];
-    const uint32_t tok = blockIdx.y, tid = threadIdx.x;
-    const uint32_t n4 = in_pad * 2;   // float4s of the token's table
-    const float4 *src = reinterpret_cast<const float4 *>(lut + (size_t)tok * in_pad * 8);
-    for (uint32_t i = tid; i < n4; i += blockDim.x) reinterpret_cast<float4 *>(T_s)[i] = src[i];
     __syncthreads();
-    const uint32_t r = blockIdx.x * kRowsPerCta + tid;
-    if (r >= out) return;
-    const uint8_t *row = packed + (size_t)r * rowbytes;
-    const uint16_t *nrm = norms + (size_t)r * ngroup;
+    // Thread (row, token): which tensor's block this is, then the row's index
+    // words and norms, the next group's fetched while this one is summed.
+    uint32_t j = 0;
+    while (j + 1 < jobs.n && blockIdx.x >= jobs.job[j + 1].rb0) j++;
+    const CqJob &J = jobs.job[j];
+    const uint32_t r = (blockIdx.x - J.rb0) * kRowsPerCta + tid % kRowsPerCta, tt = tid / kRowsPerCta;
+    if (r >= J.out || tt >= ntt) return;
+    const uint32_t ngroup = in_pad / g, wpg = g / 16;   // index words per group
+    const uint32_t *row = reinterpret_cast<const uint32_t *>(J.packed + (size_t)r * (in_pad / 4));
+    const uint16_t *nrm = J.norms + (size_t)r * ngroup;
+    const float *Tt = lut + (size_t)tt * npairs * 16;
+    uint32_t wv[16], wn[16];   // g <= 256
+    uint16_t hn = nrm[0];
+#pragma unroll
+    for (uint32_t q = 0; q < 16; q++) wv[q] = q < wpg ? row[q] : 0u;
     float acc = 0.0f;
     for (uint32_t gi = 0; gi < ngroup; gi++) {
+        const bool more = gi + 1 < ngroup;
+        const uint16_t hnext = more ? nrm[gi + 1] : (uint16_t)0;
+#pragma unroll
+        for (uint32_t q = 0; q < 16; q++) wn[q] = more && q < wpg ? row[(gi + 1) * wpg + q] : 0u;
         __half_raw hr;
-        hr.x = nrm[gi];
+        hr.x = hn;
         const float nf = __half2float(__half(hr));
+        const float *T = Tt + (size_t)gi * half_g * 16;
         float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
-        const uint32_t *qq = reinterpret_cast<const uint32_t *>(row + (size_t)gi * (g / 4));
-        const float *T = T_s + (size_t)gi * (g / 2) * 16;
-        for (uint32_t j = 0; j < g; j += 16) {
-            const uint32_t w = *qq++;
-            s0 = __fadd_rn(s0, T[w & 15u]);
-            s1 = __fadd_rn(s1, T[16 + ((w >> 4) & 15u)]);
-            s2 = __fadd_rn(s2, T[32 + ((w >> 8) & 15u)]);
-            s3 = __fadd_rn(s3, T[48 + ((w >> 12) & 15u)]);
-            T += 64;
-            s0 = __fadd_rn(s0, T[(w >> 16) & 15u]);
-            s1 = __fadd_rn(s1, T[16 + ((w >> 20) & 15u)]);
-            s2 = __fadd_rn(s2, T[32 + ((w >> 24) & 15u)]);
-            s3 = __fadd_rn(s3, T[48 + (w >> 28)]);
-            T += 64;
+#pragma unroll
+        for (uint32_t q = 0; q < 16; q++) {
+            if (q < wpg) {
+                const uint32_t w = wv[q];
+                s0 = __fadd_rn(s0, T[w & 15u]);
+                s1 = __fadd_rn(s1, T[16 + ((w >> 4) & 15u)]);
+                s2 = __fadd_rn(s2, T[32 + ((w >> 8) & 15u)]);
+                s3 = __fadd_rn(s3, T[48 + ((w >> 12) & 15u)]);
+                s0 = __fadd_rn(s0, T[64 + ((w >> 16) & 15u)]);
+                s1 = __fadd_rn(s1, T[80 + ((w >> 20) & 15u)]);
+                s2 = __fadd_rn(s2, T[96 + ((w >> 24) & 15u)]);
+                s3 = __fadd_rn(s3, T[112 + (w >> 28)]);
+                T += 128;
+            }
         }
         acc = __fadd_rn(acc, __fmul_rn(nf, __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3))));
+        hn = hnext;
+#pragma unroll
+        for (uint32_t q = 0; q < 16; q++) wv[q] = wn[q];
     }
-    y[(size_t)tok * out + r] = acc;
+    J.y[(size_t)(t0 + tt) * J.out + r] = acc;
 }
 
 }  // namespace
@@ -149,8 +190,6 @@ struct nd_cq {
     uint32_t n = 0;
     int device = -1;
     uint8_t *d_blob = nullptr;      // device copy (CQ tensors and codebook read in place)
-    float *d_lut = nullptr;         // pair tables, [tokens][in_pad / 2][16]
-    size_t lut_cap = 0;             // floats
 };
 
 namespace {
@@ -176,7 +215,7 @@ int cq2_geometry(const nd_cq *c, uint32_t index, nd_cq_tensor *t, uint32_t *in_p
     decode_record(c, index, t);
     if (t->dtype != ND_CQ_DT_CQ || t->bits != 2 || t->ndim != 2)
         return nda::report_error(ND_ATTN_ERR_ARG, "tensor %u is not a 2-bit CQ matrix", index);
-    if (t->group == 0 || t->group % 16 != 0 || t->shape[0] == 0 || t->shape[1] == 0)
+    if (t->group < 16 || t->group > 256 || (t->group & (t->group - 1)) || t->shape[0] == 0 || t->shape[1] == 0)
         return nda::report_error(ND_ATTN_ERR_ARG, "tensor %u: group %u", index, t->group);
     *in_pad = (t->shape[1] + t->group - 1) / t->group * t->group;
     *rowbytes = *in_pad / 4;
@@ -241,7 +280,6 @@ void nd_cq_close(nd_cq *c) {
         cudaGetDevice(&prev);
         cudaSetDevice(c->device);
         cudaFree(c->d_blob);
-        cudaFree(c->d_lut);
         cudaSetDevice(prev);
     }
     delete c;
@@ -299,7 +337,8 @@ int nd_cq_project(nd_cq *c, uint32_t n_tensors, const uint32_t *tensors, uint32_
     if (c->device < 0 || !c->d_blob) return nda::report_error(ND_ATTN_ERR_ARG, "handle opened without a device");
     if (n_tensors == 0 || n_tok == 0) return ND_ATTN_OK;
     std::vector<nd_cq_tensor> ts(n_tensors);
-    uint32_t in_pad = 0, rowbytes = 0, in = 0, g = 0;
+    if (n_tensors > (uint32_t)kMaxJobs) return nda::report_error(ND_ATTN_ERR_RANGE, "%u tensors per call", n_tensors);
+    uint32_t in_pad = 0, in = 0, g = 0;
     for (uint32_t i = 0; i < n_tensors; i++) {
         uint32_t ip = 0, rb = 0;
         int rc = cq2_geometry(c, tensors[i], &ts[i], &ip, &rb);
@@ -309,43 +348,40 @@ int nd_cq_project(nd_cq *c, uint32_t n_tensors, const uint32_t *tensors, uint32_
         else if (ts[i].shape[1] != in || ts[i].group != g)
             return nda::report_error(ND_ATTN_ERR_ARG, "tensors reduce over different inputs");
     }
+    CqJobs jobs;
+    memset(&jobs, 0, sizeof(jobs));
+    uint32_t blocks = 0;
+    for (uint32_t i = 0; i < n_tensors; i++) {
+        const uint32_t out = ts[i].shape[0];
+        const uint8_t *packed = c->d_blob + ts[i].offset;
+        jobs.job[i] = CqJob{packed, reinterpret_cast<const uint16_t *>(packed + (size_t)out * (in_pad / 4)), y[i], out,
+                            blocks};
+        blocks += (out + kRowsPerCta - 1) / kRowsPerCta;
+    }
+    jobs.n = n_tensors;
+    const size_t per_tok = (size_t)in_pad * 36;   // table (8 floats per input) + transform (1)
+    const int tt = per_tok * 4 <= kSmemBudget ? 4 : per_tok * 2 <= kSmemBudget ? 2 : 1;
+    const size_t smem = per_tok * tt;
+    // The 2-bit slice of the codebook is its first 4 floats (nd_cact_codebook).
+    float4 cb;
+    memcpy(&cb, c->blob.data() + kHeaderBytes, sizeof(cb));
+    const float scale = 1.0f / sqrtf((float)g);   // nd_cq_prepare's scale
+    const dim3 grid(blocks, (n_tok + tt - 1) / tt);
     int prev = 0;
     cudaGetDevice(&prev);
     if (prev != c->device) cudaSetDevice(c->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    int rc = ND_ATTN_OK;
-    const size_t need = (size_t)n_tok * in_pad * 8;
-    if (need > c->lut_cap) {
-        cudaFree(c->d_lut);
-        c->d_lut = nullptr;
-        c->lut_cap = 0;
-        if (cudaMalloc(&c->d_lut, need * sizeof(float)) != cudaSuccess) {
-            rc = nda::report_error(ND_ATTN_ERR_NOMEM, "pair tables for %u tokens", n_tok);
-        } else {
-            c->lut_cap = need;
-        }
-    }
-    if (!rc) {
-        // The codebook's 2-bit slice is its first 4 floats (nd_cact_codebook).
-        const float *cb2 = reinterpret_cast<const float *>(c->d_blob + kHeaderBytes);
-        const float scale = 1.0f / sqrtf((float)g);   // nd_cq_prepare's scale
-        cq_prepare_kernel<<<n_tok, 256, in_pad * sizeof(float), s>>>(x, in, in_pad, g, scale, cb2, c->d_lut);
-        const size_t smem = (size_t)in_pad * 8 * sizeof(float);
-        cudaError_t e = cudaFuncSetAttribute(cq_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        for (uint32_t i = 0; i < n_tensors && e == cudaSuccess; i++) {
-            const nd_cq_tensor &t = ts[i];
-            const uint32_t out = t.shape[0];
-            rowbytes = in_pad / 4;
-            const uint8_t *packed = c->d_blob + t.offset;
-            const uint16_t *norms = reinterpret_cast<const uint16_t *>(packed + (size_t)out * rowbytes);
-            const dim3 grid((out + kRowsPerCta - 1) / kRowsPerCta, n_tok);
-            cq_rows_kernel<<<grid, kRowsPerCta, smem, s>>>(packed, norms, out, rowbytes, in_pad / g, g, in_pad,
-                                                            c->d_lut, y[i]);
+    auto go = [&](auto kern) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e == cudaSuccess) {
+            kern<<<grid, kRowsPerCta * tt, smem, s>>>(x, n_tok, in, in_pad, g, scale, cb, jobs);
             e = cudaGetLastError();
         }
-        if (e == cudaSuccess) e = cudaGetLastError();
-        if (e != cudaSuccess) rc = nda::report_error(ND_ATTN_ERR_CUDA, "projection launch: %s", cudaGetErrorString(e));
-    }
+        return e;
+    };
+    const cudaError_t e = tt == 4 ? go(cq_project_kernel<4>) : tt == 2 ? go(cq_project_kernel<2>) : go(cq_project_kernel<1>);
+    const int rc = e == cudaSuccess ? ND_ATTN_OK
+                                    : nda::report_error(ND_ATTN_ERR_CUDA, "projection launch: %s", cudaGetErrorString(e));
     if (prev != c->device) cudaSetDevice(prev);
     return rc;
 }

@@ -85,7 +85,8 @@ ND_ATTN_API int nd_cq_read_f32(const nd_cq *c, uint32_t index, float *host, size
  * one pair table per token serve them all. x: device [n_tok][shape[1]] f32;
  * y[i]: device [n_tok][shape[0] of tensor i] f32. Enqueued on `stream` (a
  * cudaStream_t of the handle's device; NULL = the legacy default stream).
- * Limits: 2-bit tensors, group a multiple of 16, padded input <= 4096. */
+ * Limits: at most 8 tensors per call, 2-bit tensors, group a power of two from
+ * 16 to 256, padded input <= 4096. */
 ND_ATTN_API int nd_cq_project(nd_cq *c, uint32_t n_tensors, const uint32_t *tensors, uint32_t n_tok,
                               const float *x, float *const *y, void *stream);
 
