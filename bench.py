@@ -867,7 +867,7 @@ def run_serve(args, world, rank, local, dist):
     dout = torch.empty((R, H * VD), dtype=torch.float16, device="cuda")
     lens = [int(x) for x in suf]
 
-    def serve_round(ev=None):
+    def serve_round(ev=None, shared=True):
         for l in range(LAYERS):
             a.prefill(l, lens, sq[l], sk[l], sv[l], sout)
         a.advance(R, lens=lens)
@@ -875,40 +875,53 @@ def run_serve(args, world, rank, local, dist):
             ev.record(stream)
         for i in range(S_STEPS):
             for l in range(LAYERS):
-                a.decode(l, R, dq[i, l], dk[i, l], dv[i, l], dout)
+                if shared:   # the prefix rows read once per CTA (nd_attn_decode_shared)
+                    a.decode_shared(l, R, tpl, S_PREFIX, dq[i, l], dk[i, l], dv[i, l], dout)
+                else:        # every request reads the prefix rows itself (nd_attn_decode)
+                    a.decode(l, R, dq[i, l], dk[i, l], dv[i, l], dout)
             a.advance(R)
 
-    serve_round()                                     # warm-up round, then back to the prefix
-    for r in range(R):
-        a.rewind(r)
-    a.sync()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    launches0 = a.launches
-    t0, tm, t1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-    with Clocks(local) as clk:
-        t0.record(stream)
-        serve_round(tm)
-        t1.record(stream)
+    def timed_round(shared):
+        serve_round(shared=shared)                    # warm-up round, then back to the prefix
+        for r in range(R):
+            a.rewind(r)
         a.sync()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-    launches = a.launches - launches0
-    ms, pre_ms = t0.elapsed_time(t1), t0.elapsed_time(tm)
+        launches0 = a.launches
+        t0, tm, t1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        with Clocks(local) as clk:
+            t0.record(stream)
+            serve_round(tm, shared=shared)
+            t1.record(stream)
+            a.sync()
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+        launches = a.launches - launches0
+        for r in range(R):
+            a.rewind(r)
+        times = torch.tensor([t0.elapsed_time(t1), t0.elapsed_time(tm)], device="cuda", dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(times, op=dist.ReduceOp.MAX)
+        return float(times[0]), float(times[1]), launches, clk
+
+    ms_u, pre_u, _, _ = timed_round(False)
+    ms, pre_ms, launches, clk = timed_round(True)
     a.close()
-    times = torch.tensor([ms, pre_ms], device="cuda", dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    ms, pre_ms = float(times[0]), float(times[1])
     dec_ms = (ms - pre_ms) / S_STEPS
+    dec_ms_u = (ms_u - pre_u) / S_STEPS
     row = HKV * (QK + VD) * 2                         # bytes of one K+V row, all heads
     uniq = (S_PREFIX + float(np.sum(suf)) + R * (S_STEPS / 2 + 1)) * row * LAYERS
     logical = float(np.sum(S_PREFIX + suf + S_STEPS / 2 + 1)) * row * LAYERS
     pk_, peak_kind = peaks()
     return {"metric": S_METRIC, "value": (T + R * S_STEPS) * world / (ms / 1e3), "unit": "tok/s",
             "ms_per_round": ms, "prefill_ms": pre_ms, "decode_ms_per_step": dec_ms,
+            "decode": "nd_attn_decode_shared (the 213 prefix rows staged once per CTA and shared by its requests)",
+            "unshared": {"value": (T + R * S_STEPS) * world / (ms_u / 1e3), "ms_per_round": ms_u,
+                         "decode_ms_per_step": dec_ms_u,
+                         "decode": "nd_attn_decode (each request reads the prefix rows itself, from L2)"},
             "prefill_tok_s": T * world / (pre_ms / 1e3), "decode_tok_s": R * world / (dec_ms / 1e3),
             "scaling": "strong", "requests_per_gpu": R, "suffix_tokens_per_gpu": T, "gpu_launches": int(launches),
             "roofline": {"bound": "hbm (prefix rows from L2)", "unit": "GB/s", "peak": pk_["hbm_gbs"],

@@ -253,6 +253,7 @@ struct nd_attn {
     cudaStream_t stream = nullptr;   // where work is enqueued
     cudaStream_t own = nullptr;      // the handle's own stream
     int sm_count = 148;
+    int shared_variant = 2;          // highest nd_attn_decode_shared variant to use (ND_ATTN_SHARED_VARIANT)
     uint32_t rep = 1, k_dim = 0, v_dim = 0, blocks_per_seq = 1, block_shift = 0;
     size_t rows_per_layer = 0, kes = 1;
     void *kc = nullptr, *vc = nullptr;
@@ -1056,6 +1057,9 @@ int nd_attn_open(const nd_attn_config *cfg_in, nd_attn **out) {
     nd_attn *h = new nd_attn();
     h->cfg = cfg;
     h->sm_count = prop.multiProcessorCount;
+    // ND_ATTN_SHARED_VARIANT=1 keeps nd_attn_decode_shared on its lane-map
+    // kernel (variant 1) where variant 2 would run (tests cover both).
+    if (const char *sv = getenv("ND_ATTN_SHARED_VARIANT")) h->shared_variant = atoi(sv) == 1 ? 1 : 2;
     h->rep = cfg.n_heads / cfg.n_kv_heads;
     h->k_dim = cfg.n_kv_heads * cfg.qk_head_dim;
     h->v_dim = cfg.n_kv_heads * cfg.v_head_dim;
@@ -1376,6 +1380,95 @@ int nd_attn_decode(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_i
     }
     return run_attend(h, layer, n, d_tok, nullptr, 0, vis, 1, q, k, v, gate, out, no_wrap ? &tseq : nullptr,
                       no_wrap ? &tpos : nullptr);
+}
+
+int nd_attn_decode_shared(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids, uint32_t prefix_seq,
+                          uint32_t prefix_rows, const void *q, const void *k, const void *v, const void *gate,
+                          void *out) {
+    int rc = check_call(h, layer, n, seq_ids, nullptr);
+    if (rc) return rc;
+    if (!q || !k || !v || !out) return fail(ND_ATTN_ERR_ARG, "null tensor");
+    const nd_attn_config &c = h->cfg;
+    if (prefix_seq >= c.max_seqs)
+        return fail(ND_ATTN_ERR_RANGE, "prefix sequence %u >= max_seqs %u", prefix_seq, c.max_seqs);
+    if (prefix_rows == 0 || prefix_rows > h->seqs[prefix_seq].pos)
+        return fail(ND_ATTN_ERR_RANGE, "prefix rows %u: sequence %u holds %u written positions", prefix_rows,
+                    prefix_seq, h->seqs[prefix_seq].pos);
+    for (uint32_t i = 0; i < n; i++) {
+        const uint32_t s = seq_ids ? seq_ids[i] : i;
+        const uint32_t pos = h->seqs[s].pos;
+        if (pos >= c.window)
+            return fail(ND_ATTN_ERR_RANGE, "sequence %u at position %u wraps the %u-slot ring", s, pos, c.window);
+        if (pos < prefix_rows)
+            return fail(ND_ATTN_ERR_RANGE, "sequence %u at position %u is inside the %u prefix rows", s, pos,
+                        prefix_rows);
+    }
+    const int qk = (int)c.qk_head_dim, vd = (int)c.v_head_dim, nq = nda::nq_for_rep(h->rep);
+    auto launch = [&](const AttnParams &P, uint32_t tpc, dim3 grid, int variant, size_t *smem) {
+        switch (c.kv_dtype) {
+        case ND_DT_I8:
+            return nda::attend_shared_launch_i8(qk, vd, nq, P, prefix_seq, prefix_rows, tpc, grid, variant, smem,
+                                                h->stream);
+        case ND_DT_F32:
+            return nda::attend_shared_launch_f32(qk, vd, nq, P, prefix_seq, prefix_rows, tpc, grid, variant, smem,
+                                                 h->stream);
+        case ND_DT_F16:
+            return nda::attend_shared_launch_f16(qk, vd, nq, P, prefix_seq, prefix_rows, tpc, grid, variant, smem,
+                                                 h->stream);
+        default:
+            return nda::attend_shared_launch_bf16(qk, vd, nq, P, prefix_seq, prefix_rows, tpc, grid, variant, smem,
+                                                  h->stream);
+        }
+    };
+    DeviceGuard dg(c.device);
+    int smem_max = 0;
+    ND_CUDA(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, c.device));
+    // Variant 2 (one lane per query row over the prefix) where it is built
+    // (head dims up to 64) and its f32 staging fits; else variant 1; else the
+    // regular path, which gives the same results.
+    int variant = 0;
+    size_t smem = 0;
+    if (h->shared_variant >= 2 && launch(AttnParams{}, 0, dim3(1), 2, &smem) == cudaSuccess &&
+        smem <= (size_t)smem_max && (reinterpret_cast<uintptr_t>(q) & 15u) == 0)
+        variant = 2;
+    else if (launch(AttnParams{}, 0, dim3(1), 1, &smem) == cudaSuccess && smem <= (size_t)smem_max)
+        variant = 1;
+    if (!variant) return nd_attn_decode(h, layer, n, seq_ids, q, k, v, gate, out);
+    if (c.qkv_conv_taps) {
+        std::vector<nda::SeqSpan> sp;
+        if (seq_ids) {
+            sp.resize(n);
+            for (uint32_t i = 0; i < n; i++) sp[i] = nda::SeqSpan{seq_ids[i], i, 1u};
+        }
+        rc = run_taps(h, layer, n, seq_ids ? sp.data() : nullptr, n, &q, &k, &v);
+        if (rc) return rc;
+    }
+    const TokMeta *d_tok = nullptr;
+    if (seq_ids) {
+        std::vector<TokMeta> tok(n);
+        for (uint32_t i = 0; i < n; i++) tok[i] = TokMeta{seq_ids[i], 0u, i};
+        rc = upload_tok(h, tok);
+        if (rc) return rc;
+        d_tok = h->d_tok;
+    }
+    AttnParams P = base_params(h, layer);
+    P.q = q; P.k = k; P.v = v; P.gate = gate; P.out = out;
+    P.tok = d_tok;
+    P.n_tok = n;
+    P.fuse_append = 1;
+    // Tokens per CTA: the call's (token, KV head) pairs over the CTAs the GPU
+    // holds at once (variant 2: one per SM; variant 1: two), a whole number of
+    // the CTA's 8 warps x tokens per warp step.
+    const uint32_t per_sm = variant == 2 ? 1u : 2u;
+    const uint32_t tw = variant == 2 ? 32u / (uint32_t)nq : (nq >= 4 ? 1u : 4u / (uint32_t)nq), step = 8u * tw;
+    const uint64_t ctas = (uint64_t)per_sm * (uint64_t)h->sm_count;
+    const uint64_t want = ((uint64_t)n * c.n_kv_heads + ctas - 1) / ctas;
+    const uint32_t tpc = (uint32_t)std::max<uint64_t>(step, (want + step - 1) / step * step);
+    const dim3 grid(c.n_kv_heads, (n + tpc - 1) / tpc, 1);
+    note_writer(h, (int)layer);
+    ND_CUDA(launch(P, tpc, grid, variant, nullptr));
+    h->launches++;
+    return ND_ATTN_OK;
 }
 
 }  // extern "C"

@@ -28,7 +28,10 @@ int attend_rows_per_iter(int kv_dt, int vd, int nq);
     cudaError_t attend_lean_launch_##SUF(int hd, int nq, const void *kmap, const void *vmap,            \
                                          const void *ksmap, const void *vsmap, const void *ktmap,        \
                                          const void *vtmap, const LeanTok *tk, const AttnParams &P,      \
-                                         int *blocks_per_sm, cudaStream_t s);
+                                         int *blocks_per_sm, cudaStream_t s);                            \
+    cudaError_t attend_shared_launch_##SUF(int qk, int vd, int nq, const AttnParams &P, uint32_t pseq,  \
+                                           uint32_t prows, uint32_t tpc, dim3 grid, int variant,        \
+                                           size_t *smem_bytes, cudaStream_t s);
 ND_DECLARE_KV(i8)
 ND_DECLARE_KV(f32)
 ND_DECLARE_KV(f16)

@@ -4,6 +4,7 @@
 #pragma once
 #include "nd_decode_tma.cuh"
 #include "nd_internal.h"
+#include "nd_shared.cuh"
 
 namespace nda {
 
@@ -110,6 +111,42 @@ cudaError_t attend_lean_launch_t(int hd, int nq, const void *kmap, const void *v
     return cudaErrorInvalidValue;
 }
 
+// Shared-prefix decode (nd_shared.cuh): variant 2 (one lane per query row in
+// the prefix pass, head dims up to 64) or variant 1 (lane map throughout).
+// With smem_bytes set, only reports the dynamic shared memory a launch of
+// `prows` staged rows needs (no launch); cudaErrorInvalidValue when the
+// variant is not built for the shape.
+template <typename KVT>
+cudaError_t attend_shared_launch_t(int qk, int vd, int nq, const AttnParams &P, uint32_t pseq, uint32_t prows,
+                                   uint32_t tpc, dim3 grid, int variant, size_t *smem_bytes, cudaStream_t s) {
+#define ND_CASE(K, Q, V, N, SMEM)                                                                     \
+    if (qk == Q && vd == V && nq == N) {                                                              \
+        const size_t smem = SMEM<Q, V, KVT, N>(prows);                                                \
+        if (smem_bytes) {                                                                             \
+            *smem_bytes = smem;                                                                       \
+            return cudaSuccess;                                                                       \
+        }                                                                                             \
+        cudaError_t e = cudaFuncSetAttribute(K<Q, V, KVT, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                             (int)smem);                                              \
+        if (e != cudaSuccess) return e;                                                               \
+        K<Q, V, KVT, N><<<grid, 256, smem, s>>>(P, pseq, prows, tpc);                                 \
+        return cudaGetLastError();                                                                    \
+    }
+#define ND_CASES(K, Q, V, SMEM) ND_CASE(K, Q, V, 1, SMEM) ND_CASE(K, Q, V, 2, SMEM) ND_CASE(K, Q, V, 4, SMEM) \
+    ND_CASE(K, Q, V, 8, SMEM)
+    if (variant == 2) {
+        ND_CASES(attend_shared2_kernel, 48, 64, shared2_smem_bytes)
+        ND_CASES(attend_shared2_kernel, 64, 64, shared2_smem_bytes)
+    } else {
+        ND_CASES(attend_shared_kernel, 48, 64, shared_smem_bytes)
+        ND_CASES(attend_shared_kernel, 64, 64, shared_smem_bytes)
+        ND_CASES(attend_shared_kernel, 128, 128, shared_smem_bytes)
+    }
+#undef ND_CASES
+#undef ND_CASE
+    return cudaErrorInvalidValue;
+}
+
 }  // namespace nda
 
 #define ND_DEFINE_KV(SUF, KVT)                                                                  \
@@ -126,5 +163,10 @@ cudaError_t attend_lean_launch_t(int hd, int nq, const void *kmap, const void *v
                                          const void *vtmap, const LeanTok *tk, const AttnParams &P, \
                                          int *blocks_per_sm, cudaStream_t s) {                  \
         return attend_lean_launch_t<KVT>(hd, nq, kmap, vmap, ksmap, vsmap, ktmap, vtmap, tk, P, blocks_per_sm, s); \
+    }                                                                                           \
+    cudaError_t attend_shared_launch_##SUF(int qk, int vd, int nq, const AttnParams &P, uint32_t pseq,  \
+                                           uint32_t prows, uint32_t tpc, dim3 grid, int variant,        \
+                                           size_t *smem_bytes, cudaStream_t s) {                \
+        return attend_shared_launch_t<KVT>(qk, vd, nq, P, pseq, prows, tpc, grid, variant, smem_bytes, s); \
     }                                                                                           \
     }

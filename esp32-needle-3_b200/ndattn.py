@@ -101,6 +101,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "nd_attn_rope_append": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp]),
         "nd_attn_decode_host": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp, vp]),
         "nd_attn_decode_noalloc": (c_int, [vp, u32, u32, vp, vp, vp, vp, vp]),
+        "nd_attn_decode_shared": (c_int, [vp, u32, u32, vp, u32, u32, vp, vp, vp, vp, vp]),
         "nd_attn_gather_check": (c_int, [vp, u32, u32]),
         "nd_attn_gather_init": (c_int, [vp, u32, u32, vp]),
         "nd_attn_gather_attach": (c_int, [vp, vp]),
@@ -285,6 +286,14 @@ class Attn:
         ids = _u32(seq_ids)
         _check(load().nd_attn_decode(self.h, layer, n, _hptr(ids), _ptr(q), _ptr(k), _ptr(v), _ptr(gate),
                                      _ptr(out)))
+
+    def decode_shared(self, layer, n, prefix_seq, prefix_rows, q, k, v, out, gate=None, seq_ids=None) -> None:
+        """nd_attn_decode for sequences whose cache rows [0, prefix_rows) equal
+        those of prefix_seq (nd_attn_decode_shared): the prefix is read once per
+        CTA and shared across the requests."""
+        ids = _u32(seq_ids)
+        _check(load().nd_attn_decode_shared(self.h, layer, n, _hptr(ids), prefix_seq, prefix_rows, _ptr(q), _ptr(k),
+                                            _ptr(v), _ptr(gate), _ptr(out)))
 
     def prefill(self, layer, lens, q, k, v, out, gate=None, seq_ids=None) -> None:
         ln, ids = _u32(lens), _u32(seq_ids)

@@ -169,6 +169,24 @@ ND_ATTN_API int  nd_attn_set_state(nd_attn *h, uint32_t seq, uint32_t pos, uint3
 ND_ATTN_API int  nd_attn_decode(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids,
                     const void *q, const void *k, const void *v, const void *gate,
                     void *out);
+/* Decode of `n` sequences that all begin with the same cache rows: the
+ * requests of shared-prefix serving, each restored from one saved schema
+ * prefix (nd_model_prefix_restore, nd_model.c:1543-1553, per request as in
+ * esp32/main/main.c:281-315). Same arguments, work and results as
+ * nd_attn_decode, given that cache rows [0, prefix_rows) of every listed
+ * sequence hold the same K/V as those of sequence `prefix_seq` (block tables
+ * that map the same pages, or prefix_restore of the same image). The library
+ * reads those rows once per CTA from prefix_seq (staged in shared memory and
+ * scored against many requests' queries) instead of once per request; each
+ * request's own rows [prefix_rows, pos] come from its cache.
+ * Requires: no position of the call wraps the ring (pos < window), every
+ * listed sequence at pos >= prefix_rows, prefix_seq at pos >= prefix_rows
+ * (rows written); else ND_ATTN_ERR_RANGE and nothing is launched. A prefix too
+ * large to stage in shared memory runs as nd_attn_decode. DEVICE pointers.
+ * Does not advance. */
+ND_ATTN_API int  nd_attn_decode_shared(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids,
+                                       uint32_t prefix_seq, uint32_t prefix_rows, const void *q,
+                                       const void *k, const void *v, const void *gate, void *out);
 /* Causal prefill of len[i] tokens for each of `n` sequences, starting at their
  * current positions: exactly len[i] successive decode steps of the reference
  * (esp32/main/main.c:233-234, host/nd_dump.c:265-271), i.e. token t appends
