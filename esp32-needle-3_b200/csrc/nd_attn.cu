@@ -265,6 +265,8 @@ struct nd_attn {
     std::vector<HostSeq> seqs;
     int32_t *d_btab = nullptr;
     float *part_o = nullptr, *part_ml = nullptr;
+    float *shared_part = nullptr;    // nd_attn_decode_shared: (m, l, o) over the prefix per (token, query head)
+    size_t shared_part_cap = 0;
     int *counters = nullptr;
     size_t part_slots = 0;     // (item, split) slots the scratch holds
     size_t counter_cap = 0;    // items with a ticket counter
@@ -1189,7 +1191,7 @@ void nd_attn_close(nd_attn *h) {
     if (h->stream) cudaStreamSynchronize(h->stream);
     cudaFree(h->kc); cudaFree(h->vc); cudaFree(h->ks); cudaFree(h->vs);
     cudaFree(h->rope); cudaFree(h->norms); cudaFree(h->d_state); cudaFree(h->d_btab);
-    cudaFree(h->part_o); cudaFree(h->part_ml); cudaFree(h->counters);
+    cudaFree(h->part_o); cudaFree(h->part_ml); cudaFree(h->counters); cudaFree(h->shared_part);
     cudaFree(h->d_tok); cudaFree(h->d_u32); cudaFree(h->d_lean); cudaFree(h->d_vbig); cudaFree(h->dio); cudaFree(h->d_work); cudaFree(h->d_spans);
     cudaFree(h->d_tapw); cudaFree(h->d_hist); cudaFree(h->d_snaphist); cudaFree(h->d_tapio); cudaFree(h->d_tspans);
     if (h->hstage) cudaFreeHost(h->hstage);
@@ -1404,19 +1406,19 @@ int nd_attn_decode_shared(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t
                         prefix_rows);
     }
     const int qk = (int)c.qk_head_dim, vd = (int)c.v_head_dim, nq = nda::nq_for_rep(h->rep);
-    auto launch = [&](const AttnParams &P, uint32_t tpc, dim3 grid, int variant, size_t *smem) {
+    auto launch = [&](const AttnParams &P, uint32_t tpc, dim3 grid, int variant, float *part, size_t *smem) {
         switch (c.kv_dtype) {
         case ND_DT_I8:
-            return nda::attend_shared_launch_i8(qk, vd, nq, P, prefix_seq, prefix_rows, tpc, grid, variant, smem,
+            return nda::attend_shared_launch_i8(qk, vd, nq, P, prefix_seq, prefix_rows, tpc, grid, variant, part, smem,
                                                 h->stream);
         case ND_DT_F32:
-            return nda::attend_shared_launch_f32(qk, vd, nq, P, prefix_seq, prefix_rows, tpc, grid, variant, smem,
+            return nda::attend_shared_launch_f32(qk, vd, nq, P, prefix_seq, prefix_rows, tpc, grid, variant, part, smem,
                                                  h->stream);
         case ND_DT_F16:
-            return nda::attend_shared_launch_f16(qk, vd, nq, P, prefix_seq, prefix_rows, tpc, grid, variant, smem,
+            return nda::attend_shared_launch_f16(qk, vd, nq, P, prefix_seq, prefix_rows, tpc, grid, variant, part, smem,
                                                  h->stream);
         default:
-            return nda::attend_shared_launch_bf16(qk, vd, nq, P, prefix_seq, prefix_rows, tpc, grid, variant, smem,
+            return nda::attend_shared_launch_bf16(qk, vd, nq, P, prefix_seq, prefix_rows, tpc, grid, variant, part, smem,
                                                   h->stream);
         }
     };
@@ -1428,10 +1430,10 @@ int nd_attn_decode_shared(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t
     // regular path, which gives the same results.
     int variant = 0;
     size_t smem = 0;
-    if (h->shared_variant >= 2 && launch(AttnParams{}, 0, dim3(1), 2, &smem) == cudaSuccess &&
+    if (h->shared_variant >= 2 && launch(AttnParams{}, 0, dim3(1), 2, nullptr, &smem) == cudaSuccess &&
         smem <= (size_t)smem_max && (reinterpret_cast<uintptr_t>(q) & 15u) == 0)
         variant = 2;
-    else if (launch(AttnParams{}, 0, dim3(1), 1, &smem) == cudaSuccess && smem <= (size_t)smem_max)
+    else if (launch(AttnParams{}, 0, dim3(1), 1, nullptr, &smem) == cudaSuccess && smem <= (size_t)smem_max)
         variant = 1;
     if (!variant) return nd_attn_decode(h, layer, n, seq_ids, q, k, v, gate, out);
     if (c.qkv_conv_taps) {
@@ -1451,22 +1453,28 @@ int nd_attn_decode_shared(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t
         if (rc) return rc;
         d_tok = h->d_tok;
     }
+    if (variant == 2) {
+        rc = grow(&h->shared_part, &h->shared_part_cap, (size_t)n * c.n_heads * (c.v_head_dim + 2));
+        if (rc) return rc;
+    }
     AttnParams P = base_params(h, layer);
     P.q = q; P.k = k; P.v = v; P.gate = gate; P.out = out;
     P.tok = d_tok;
     P.n_tok = n;
     P.fuse_append = 1;
-    // Tokens per CTA: the call's (token, KV head) pairs over the CTAs the GPU
-    // holds at once (variant 2: one per SM; variant 1: two), a whole number of
-    // the CTA's 8 warps x tokens per warp step.
-    const uint32_t per_sm = variant == 2 ? 1u : 2u;
-    const uint32_t tw = variant == 2 ? 32u / (uint32_t)nq : (nq >= 4 ? 1u : 4u / (uint32_t)nq), step = 8u * tw;
+    // Tokens per CTA of the staging launch: the call's (token, KV head) pairs
+    // over two CTAs per SM, a whole number of the CTA's warps (variant 2:
+    // nda::kSharedPrefixWarps; variant 1: 8) x tokens per warp step.
+    const uint32_t per_sm = 2u;
+    const uint32_t tw = variant == 2 ? 32u / (uint32_t)nq : (nq >= 4 ? 1u : 4u / (uint32_t)nq);
+    const uint32_t step = (variant == 2 ? (uint32_t)nda::kSharedPrefixWarps : 8u) * tw;
     const uint64_t ctas = (uint64_t)per_sm * (uint64_t)h->sm_count;
     const uint64_t want = ((uint64_t)n * c.n_kv_heads + ctas - 1) / ctas;
     const uint32_t tpc = (uint32_t)std::max<uint64_t>(step, (want + step - 1) / step * step);
     const dim3 grid(c.n_kv_heads, (n + tpc - 1) / tpc, 1);
     note_writer(h, (int)layer);
-    ND_CUDA(launch(P, tpc, grid, variant, nullptr));
+    ND_CUDA(launch(P, tpc, grid, variant, h->shared_part, nullptr));
+    if (variant == 2) h->launches++;
     h->launches++;
     return ND_ATTN_OK;
 }

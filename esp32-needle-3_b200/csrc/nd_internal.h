@@ -14,6 +14,10 @@ inline bool head_dims_supported(unsigned qk, unsigned vd) {
 }
 inline int nq_for_rep(unsigned rep) { return rep <= 1 ? 1 : rep <= 2 ? 2 : rep <= 4 ? 4 : 8; }
 
+// Warps per CTA of the shared-prefix staging kernel (nd_shared.cuh): two CTAs
+// per SM, every lane with all 255 registers for its query row and output.
+constexpr int kSharedPrefixWarps = 4;
+
 // Sets the calling thread's nd_attn_last_error() message (printf-style) and
 // returns `code`.
 int report_error(int code, const char *fmt, ...);
@@ -31,7 +35,7 @@ int attend_rows_per_iter(int kv_dt, int vd, int nq);
                                          int *blocks_per_sm, cudaStream_t s);                            \
     cudaError_t attend_shared_launch_##SUF(int qk, int vd, int nq, const AttnParams &P, uint32_t pseq,  \
                                            uint32_t prows, uint32_t tpc, dim3 grid, int variant,        \
-                                           size_t *smem_bytes, cudaStream_t s);
+                                           float *part, size_t *smem_bytes, cudaStream_t s);
 ND_DECLARE_KV(i8)
 ND_DECLARE_KV(f32)
 ND_DECLARE_KV(f16)

@@ -111,39 +111,56 @@ cudaError_t attend_lean_launch_t(int hd, int nq, const void *kmap, const void *v
     return cudaErrorInvalidValue;
 }
 
-// Shared-prefix decode (nd_shared.cuh): variant 2 (one lane per query row in
-// the prefix pass, head dims up to 64) or variant 1 (lane map throughout).
-// With smem_bytes set, only reports the dynamic shared memory a launch of
-// `prows` staged rows needs (no launch); cudaErrorInvalidValue when the
-// variant is not built for the shape.
+// Shared-prefix decode (nd_shared.cuh): variant 2 (the prefix pass and the
+// own-rows pass as two launches, head dims up to 64; `part` holds the (m, l,
+// o) of every (token, query head), [n_tok][n_heads][vd + 2] f32) or variant 1
+// (lane map throughout, one launch). With smem_bytes set, only reports the
+// dynamic shared memory of the staging launch for `prows` rows (no launch);
+// cudaErrorInvalidValue when the variant is not built for the shape.
 template <typename KVT>
 cudaError_t attend_shared_launch_t(int qk, int vd, int nq, const AttnParams &P, uint32_t pseq, uint32_t prows,
-                                   uint32_t tpc, dim3 grid, int variant, size_t *smem_bytes, cudaStream_t s) {
-#define ND_CASE(K, Q, V, N, SMEM)                                                                     \
+                                   uint32_t tpc, dim3 grid, int variant, float *part, size_t *smem_bytes,
+                                   cudaStream_t s) {
+#define ND_CASE1(Q, V, N)                                                                             \
     if (qk == Q && vd == V && nq == N) {                                                              \
-        const size_t smem = SMEM<Q, V, KVT, N>(prows);                                                \
+        const size_t smem = shared_smem_bytes<Q, V, KVT, N>(prows);                                   \
         if (smem_bytes) {                                                                             \
             *smem_bytes = smem;                                                                       \
             return cudaSuccess;                                                                       \
         }                                                                                             \
-        cudaError_t e = cudaFuncSetAttribute(K<Q, V, KVT, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                             (int)smem);                                              \
+        cudaError_t e = cudaFuncSetAttribute(attend_shared_kernel<Q, V, KVT, N>,                      \
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
         if (e != cudaSuccess) return e;                                                               \
-        K<Q, V, KVT, N><<<grid, 256, smem, s>>>(P, pseq, prows, tpc);                                 \
+        attend_shared_kernel<Q, V, KVT, N><<<grid, 256, smem, s>>>(P, pseq, prows, tpc);              \
         return cudaGetLastError();                                                                    \
     }
-#define ND_CASES(K, Q, V, SMEM) ND_CASE(K, Q, V, 1, SMEM) ND_CASE(K, Q, V, 2, SMEM) ND_CASE(K, Q, V, 4, SMEM) \
-    ND_CASE(K, Q, V, 8, SMEM)
-    if (variant == 2) {
-        ND_CASES(attend_shared2_kernel, 48, 64, shared2_smem_bytes)
-        ND_CASES(attend_shared2_kernel, 64, 64, shared2_smem_bytes)
-    } else {
-        ND_CASES(attend_shared_kernel, 48, 64, shared_smem_bytes)
-        ND_CASES(attend_shared_kernel, 64, 64, shared_smem_bytes)
-        ND_CASES(attend_shared_kernel, 128, 128, shared_smem_bytes)
+#define ND_CASE2(Q, V, N)                                                                             \
+    if (qk == Q && vd == V && nq == N) {                                                              \
+        const size_t smem = shared2_smem_bytes<Q, V, KVT, N>(prows);                                  \
+        if (smem_bytes) {                                                                             \
+            *smem_bytes = smem;                                                                       \
+            return cudaSuccess;                                                                       \
+        }                                                                                             \
+        cudaError_t e = cudaFuncSetAttribute(shared_prefix_kernel<Q, V, KVT, N>,                      \
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+        if (e != cudaSuccess) return e;                                                               \
+        shared_prefix_kernel<Q, V, KVT, N><<<grid, 32 * kSharedPrefixWarps, smem, s>>>(P, pseq, prows, tpc, part); \
+        e = cudaGetLastError();                                                                       \
+        if (e != cudaSuccess) return e;                                                               \
+        const size_t items = (size_t)P.n_tok * P.c.n_kv;                                              \
+        shared_own_kernel<Q, V, KVT, N><<<(unsigned)((items + 3) / 4), 128, 0, s>>>(P, prows, part);  \
+        return cudaGetLastError();                                                                    \
     }
-#undef ND_CASES
-#undef ND_CASE
+    if (variant == 2) {
+        ND_CASE2(48, 64, 1) ND_CASE2(48, 64, 2) ND_CASE2(48, 64, 4) ND_CASE2(48, 64, 8)
+        ND_CASE2(64, 64, 1) ND_CASE2(64, 64, 2) ND_CASE2(64, 64, 4) ND_CASE2(64, 64, 8)
+    } else {
+        ND_CASE1(48, 64, 1) ND_CASE1(48, 64, 2) ND_CASE1(48, 64, 4) ND_CASE1(48, 64, 8)
+        ND_CASE1(64, 64, 1) ND_CASE1(64, 64, 2) ND_CASE1(64, 64, 4) ND_CASE1(64, 64, 8)
+        ND_CASE1(128, 128, 1) ND_CASE1(128, 128, 2) ND_CASE1(128, 128, 4) ND_CASE1(128, 128, 8)
+    }
+#undef ND_CASE1
+#undef ND_CASE2
     return cudaErrorInvalidValue;
 }
 
@@ -166,7 +183,7 @@ cudaError_t attend_shared_launch_t(int qk, int vd, int nq, const AttnParams &P, 
     }                                                                                           \
     cudaError_t attend_shared_launch_##SUF(int qk, int vd, int nq, const AttnParams &P, uint32_t pseq,  \
                                            uint32_t prows, uint32_t tpc, dim3 grid, int variant,        \
-                                           size_t *smem_bytes, cudaStream_t s) {                \
-        return attend_shared_launch_t<KVT>(qk, vd, nq, P, pseq, prows, tpc, grid, variant, smem_bytes, s); \
+                                           float *part, size_t *smem_bytes, cudaStream_t s) {   \
+        return attend_shared_launch_t<KVT>(qk, vd, nq, P, pseq, prows, tpc, grid, variant, part, smem_bytes, s); \
     }                                                                                           \
     }

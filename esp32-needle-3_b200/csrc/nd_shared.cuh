@@ -16,18 +16,19 @@
 // Two kernels:
 //   attend_shared_kernel  (variant 1) the lane map throughout; a warp scores
 //                         TB tokens' query rows against each staged row.
-//   attend_shared2_kernel (variant 2, head dims up to 64) the prefix pass
-//                         gives every lane one (token, query head) pair, its
-//                         query row and output accumulator in registers, the
-//                         staged rows as f32 broadcast reads; the pair's
-//                         (m, l, o) then seeds the lane-map pass over the
+//   variant 2 (head dims up to 64): shared_prefix_kernel gives every lane
+//                         one (token, query head) pair, its query row and
+//                         output accumulator in registers, the staged rows
+//                         as f32 broadcast reads, and writes the pair's
+//                         (m, l, o); shared_own_kernel (one warp per token
+//                         and KV head) continues that softmax over the
 //                         token's own rows.
 //
 // The caller guarantees that rows [0, prows) of every sequence of the call
 // hold the prefix sequence's values (shared pages, or prefix_restore from the
 // same image); the host checks positions (no wrap, p >= prows, prows written).
 #pragma once
-#include "nd_device.cuh"
+#include "nd_internal.h"
 
 namespace nda {
 
@@ -307,23 +308,26 @@ __global__ void __launch_bounds__(256, SharedShape<NQ>::MINB)
     }
 }
 
-// ---- head dims up to 64: one lane per (request, query head) for the prefix
+// ---- head dims up to 64: the prefix pass as its own kernel
 //
 // The lane map spends most of its instructions on the lanes' shuffles and the
 // per-row softmax upkeep, which a prefix scored by many requests does not
-// need. Here the prefix pass gives every lane one (token, query head) pair of
-// the warp: its rotated query row and its output accumulator live in the
-// lane's registers, each staged row (f32, int8 already scaled) is a broadcast
-// shared-memory read, and the lane runs its own online softmax over chunks of
-// 8 rows (one rescale per chunk). The pair's (m, l, o) then seeds the
-// lane-map pass over the token's own rows, as the prefix part of the same
-// softmax.
-constexpr int kShared2Warps = 8;
+// need. Variant 2 splits the call in two launches:
+//   shared_prefix_kernel  every lane takes one (token, query head) pair: its
+//                         rotated query row and output accumulator live in
+//                         the lane's registers, each staged prefix row (f32,
+//                         int8 already scaled) is a broadcast shared-memory
+//                         read, and the lane runs its own online softmax over
+//                         chunks of 8 rows (one rescale per chunk). It writes
+//                         the pair's (m, l, o) over the prefix to `part`.
+//   shared_own_kernel     one warp per (token, KV head), many CTAs per SM:
+//                         the newest row's append, then attend_kernel's lane
+//                         map over the token's own rows [prows, pos], the
+//                         softmax seeded with the pair's (m, l, o); output.
 
 template <int QK, int VD, typename KVT, int NQ>
 __host__ __device__ constexpr size_t shared2_smem_bytes(uint32_t prows) {
-    return (size_t)prows * (QK + VD) * 4 + (size_t)kShared2Warps * 32 * (VD + 2) * 4 +
-           (size_t)kShared2Warps * NQ * QK * 4;
+    return (size_t)prows * (QK + VD) * 4;
 }
 
 // QK activation values of one head row into f32 registers (16-byte loads).
@@ -358,22 +362,29 @@ __device__ __forceinline__ void lane_load_row(float (&x)[QK], const void *src, i
     }
 }
 
+// Position of token `tok` of the call when it may be served (no wrap, past
+// the prefix), else false (and the status word is set).
+__device__ __forceinline__ bool shared_token(const AttnParams &P, uint32_t tok, uint32_t prows, TokMeta &tm,
+                                             uint32_t &pos) {
+    tm = token_meta(P, tok);
+    const SeqState st = P.state[tm.seq];
+    pos = st.pos + tm.off;
+    return !(pos >= P.max_pos || pos >= P.c.window || pos < prows || st.n_sink >= P.c.window);
+}
+
+// grid = (n_kv, ceil(n_tok / tpc)); part: [n_tok][n_heads][VD + 2] f32 =
+// (m, l, o) of every (token, query head) over the prefix rows.
 template <int QK, int VD, typename KVT, int NQ>
-__global__ void __launch_bounds__(256, 1)
-    attend_shared2_kernel(const AttnParams P, uint32_t pseq, uint32_t prows, uint32_t tpc) {
-    using S = AttendShape<QK, VD, KVT, NQ>;   // lane map of the own-rows pass
-    constexpr int LPR = S::LPR, RPW = S::RPW, EK = S::EK, EV = S::EV, WK = S::WK, WV = S::WV, ES = S::ES;
-    constexpr int NWS = kShared2Warps, TW = 32 / NQ, U = 4;
+__global__ void __launch_bounds__(128, 2)
+    shared_prefix_kernel(const AttnParams P, uint32_t pseq, uint32_t prows, uint32_t tpc, float *part) {
+    constexpr int NWS = kSharedPrefixWarps, TW = 32 / NQ;
     constexpr bool SCALED = KvT<KVT>::dt == DT_I8;
     static_assert(QK <= 64 && VD <= 64 && QK % 8 == 0 && VD % 4 == 0, "registers per lane");
     extern __shared__ __align__(16) unsigned char sh[];
     float *sK = reinterpret_cast<float *>(sh);             // [prows][QK]
     float *sV = sK + (size_t)prows * QK;                     // [prows][VD]
-    float *hand = sV + (size_t)prows * VD;                   // [NWS][32][VD + 2]: m, l, o
-    float *sq = hand + (size_t)NWS * 32 * (VD + 2);          // [NWS][NQ][QK]
-
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, sub = lane % LPR, rl = lane / LPR;
-    const uint32_t g = blockIdx.x, n_kv = P.c.n_kv, W = P.c.window, rep = P.rep;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t g = blockIdx.x, n_kv = P.c.n_kv, rep = P.rep;
 
     // Rows [0, prows) of KV head g of the prefix sequence as f32 (int8 rows
     // times their scales).
@@ -393,209 +404,209 @@ __global__ void __launch_bounds__(256, 1)
     }
     __syncthreads();
 
-    float *hw = hand + (size_t)warp * 32 * (VD + 2);
-    float *sqw = sq + (size_t)warp * NQ * QK;
-    const char *kbase = static_cast<const char *>(P.c.k) + ((size_t)g * QK + (size_t)sub * EK) * ES;
-    const char *vbase = static_cast<const char *>(P.c.v) + ((size_t)g * VD + (size_t)sub * EV) * ES;
-    const size_t krow_bytes = (size_t)P.c.k_dim * ES, vrow_bytes = (size_t)P.c.v_dim * ES;
     const uint32_t t0 = blockIdx.y * tpc;
-
     for (uint32_t c0 = (uint32_t)warp * TW; c0 < tpc; c0 += NWS * TW) {
-        // ---- prefix pass: lane = (token c0 + lane / NQ, query head lane % NQ)
-        {
-            const uint32_t tl = c0 + lane / NQ, qi = lane % NQ, tok = t0 + tl;
-            bool live = tl < tpc && tok < P.n_tok && qi < rep;
-            uint32_t pos = 0, orow = 0;
-            if (live) {
-                const TokMeta tm = token_meta(P, tok);
-                const SeqState st = P.state[tm.seq];
-                pos = st.pos + tm.off;
-                orow = tm.row;
-                live = !(pos >= P.max_pos || pos >= W || pos < prows || st.n_sink >= W);
+        // lane = (token c0 + lane / NQ, query head g * rep + lane % NQ)
+        const uint32_t tl = c0 + lane / NQ, qi = lane % NQ, tok = t0 + tl;
+        TokMeta tm{};
+        uint32_t pos = 0;
+        const bool live = tl < tpc && tok < P.n_tok && qi < rep && shared_token(P, tok, prows, tm, pos);
+        float q[QK];
+#pragma unroll
+        for (int i = 0; i < QK; i++) q[i] = 0.0f;
+        if (live) {
+            lane_load_row<QK>(q, P.q, P.act_dt, ((size_t)tm.row * P.n_heads + g * rep + qi) * QK);
+            if (P.qnorm) {
+                float ss = 0.0f;
+#pragma unroll
+                for (int i = 0; i < QK; i++) ss = fmaf(q[i], q[i], ss);
+                const float inv = rsqrtf(ss * (1.0f / QK) + 1e-6f);
+#pragma unroll
+                for (int i = 0; i < QK; i++) q[i] *= (1.0f + P.qnorm[i]) * inv;
             }
-            float q[QK];
+            const float4 *cs4 = reinterpret_cast<const float4 *>(P.rope + (size_t)pos * (QK / 2));
 #pragma unroll
-            for (int i = 0; i < QK; i++) q[i] = 0.0f;
-            if (live) {
-                lane_load_row<QK>(q, P.q, P.act_dt, ((size_t)orow * P.n_heads + g * rep + qi) * QK);
-                if (P.qnorm) {
-                    float ss = 0.0f;
-#pragma unroll
-                    for (int i = 0; i < QK; i++) ss = fmaf(q[i], q[i], ss);
-                    const float inv = rsqrtf(ss * (1.0f / QK) + 1e-6f);
-#pragma unroll
-                    for (int i = 0; i < QK; i++) q[i] *= (1.0f + P.qnorm[i]) * inv;
-                }
-                const float4 *cs4 = reinterpret_cast<const float4 *>(P.rope + (size_t)pos * (QK / 2));
-#pragma unroll
-                for (int i = 0; i < QK / 2; i += 2) {
-                    const float4 t = cs4[i / 2];   // pairs i and i + 1: (cos, sin, cos, sin)
-                    const float a0 = q[i], b0 = q[i + QK / 2], a1 = q[i + 1], b1 = q[i + 1 + QK / 2];
-                    q[i] = (a0 * t.x - b0 * t.y) * P.scale_log2;
-                    q[i + QK / 2] = (b0 * t.x + a0 * t.y) * P.scale_log2;
-                    q[i + 1] = (a1 * t.z - b1 * t.w) * P.scale_log2;
-                    q[i + 1 + QK / 2] = (b1 * t.z + a1 * t.w) * P.scale_log2;
-                }
+            for (int i = 0; i < QK / 2; i += 2) {
+                const float4 t = cs4[i / 2];   // pairs i and i + 1: (cos, sin, cos, sin)
+                const float a0 = q[i], b0 = q[i + QK / 2], a1 = q[i + 1], b1 = q[i + 1 + QK / 2];
+                q[i] = (a0 * t.x - b0 * t.y) * P.scale_log2;
+                q[i + QK / 2] = (b0 * t.x + a0 * t.y) * P.scale_log2;
+                q[i + 1] = (a1 * t.z - b1 * t.w) * P.scale_log2;
+                q[i + 1 + QK / 2] = (b1 * t.z + a1 * t.w) * P.scale_log2;
             }
-            float m = -INFINITY, l = 0.0f, o[VD];
+        }
+        float m = -INFINITY, l = 0.0f, o[VD];
 #pragma unroll
-            for (int i = 0; i < VD; i++) o[i] = 0.0f;
-            for (uint32_t k0 = 0; k0 < prows; k0 += 8) {
-                float s[8];
+        for (int i = 0; i < VD; i++) o[i] = 0.0f;
+        for (uint32_t k0 = 0; k0 < prows; k0 += 8) {
+            float s[8];
 #pragma unroll
-                for (int kk = 0; kk < 8; kk++) {
-                    const uint32_t key = k0 + kk < prows ? k0 + kk : prows - 1;
-                    const float4 *kr = reinterpret_cast<const float4 *>(sK + (size_t)key * QK);
-                    float a = 0.0f;
+            for (int kk = 0; kk < 8; kk++) {
+                const uint32_t key = k0 + kk < prows ? k0 + kk : prows - 1;
+                const float4 *kr = reinterpret_cast<const float4 *>(sK + (size_t)key * QK);
+                float a = 0.0f;
 #pragma unroll
-                    for (int i = 0; i < QK / 4; i++) {
-                        const float4 kv = kr[i];
-                        a = fmaf(q[4 * i], kv.x, a);
-                        a = fmaf(q[4 * i + 1], kv.y, a);
-                        a = fmaf(q[4 * i + 2], kv.z, a);
-                        a = fmaf(q[4 * i + 3], kv.w, a);
-                    }
-                    s[kk] = k0 + kk < prows ? a : -INFINITY;
+                for (int i = 0; i < QK / 4; i++) {
+                    const float4 kv = kr[i];
+                    a = fmaf(q[4 * i], kv.x, a);
+                    a = fmaf(q[4 * i + 1], kv.y, a);
+                    a = fmaf(q[4 * i + 2], kv.z, a);
+                    a = fmaf(q[4 * i + 3], kv.w, a);
                 }
-                float mx = s[0];
+                s[kk] = k0 + kk < prows ? a : -INFINITY;
+            }
+            float mx = s[0];
 #pragma unroll
-                for (int kk = 1; kk < 8; kk++) mx = fmaxf(mx, s[kk]);
-                const float mn = fmaxf(m, mx);
-                const float alpha = ex2(m - mn);
-                m = mn;
-                l *= alpha;
+            for (int kk = 1; kk < 8; kk++) mx = fmaxf(mx, s[kk]);
+            const float mn = fmaxf(m, mx);
+            const float alpha = ex2(m - mn);
+            m = mn;
+            l *= alpha;
 #pragma unroll
-                for (int i = 0; i < VD; i++) o[i] *= alpha;
+            for (int i = 0; i < VD; i++) o[i] *= alpha;
 #pragma unroll
-                for (int kk = 0; kk < 8; kk++) {
-                    const uint32_t key = k0 + kk < prows ? k0 + kk : prows - 1;
-                    const float p = ex2(s[kk] - mn);
-                    l += p;
-                    const float4 *vr = reinterpret_cast<const float4 *>(sV + (size_t)key * VD);
+            for (int kk = 0; kk < 8; kk++) {
+                const uint32_t key = k0 + kk < prows ? k0 + kk : prows - 1;
+                const float p = ex2(s[kk] - mn);
+                l += p;
+                const float4 *vr = reinterpret_cast<const float4 *>(sV + (size_t)key * VD);
 #pragma unroll
-                    for (int i = 0; i < VD / 4; i++) {
-                        const float4 vv = vr[i];
-                        o[4 * i] = fmaf(p, vv.x, o[4 * i]);
-                        o[4 * i + 1] = fmaf(p, vv.y, o[4 * i + 1]);
-                        o[4 * i + 2] = fmaf(p, vv.z, o[4 * i + 2]);
-                        o[4 * i + 3] = fmaf(p, vv.w, o[4 * i + 3]);
-                    }
+                for (int i = 0; i < VD / 4; i++) {
+                    const float4 vv = vr[i];
+                    o[4 * i] = fmaf(p, vv.x, o[4 * i]);
+                    o[4 * i + 1] = fmaf(p, vv.y, o[4 * i + 1]);
+                    o[4 * i + 2] = fmaf(p, vv.z, o[4 * i + 2]);
+                    o[4 * i + 3] = fmaf(p, vv.w, o[4 * i + 3]);
                 }
             }
-            float *hp = hw + (size_t)lane * (VD + 2);
+        }
+        if (live) {
+            float *hp = part + ((size_t)tok * P.n_heads + g * rep + qi) * (VD + 2);
             hp[0] = m;
             hp[1] = l;
 #pragma unroll
             for (int i = 0; i < VD; i++) hp[2 + i] = o[i];
         }
-        __syncwarp();
+    }
+}
 
-        // ---- own rows: lane map, one token at a time, seeded with its
-        // prefix (m, l, o); the newest row appended first.
-        for (uint32_t tl = c0; tl < c0 + TW && tl < tpc; tl++) {
-            const uint32_t tok = t0 + tl;
-            if (tok >= P.n_tok) break;
-            const TokMeta tm = token_meta(P, tok);
-            const SeqState st = P.state[tm.seq];
-            const uint32_t pos = st.pos + tm.off;
-            if (pos >= P.max_pos || pos >= W || pos < prows || st.n_sink >= W) {
-                if (lane == 0) set_err(P.err, 2);
-                continue;
-            }
-            const float2 *cs = P.rope + (size_t)pos * (QK / 2);
+// One warp per (token, KV head) item; 4 warps per CTA.
+template <int QK, int VD, typename KVT, int NQ>
+__global__ void __launch_bounds__(128) shared_own_kernel(const AttnParams P, uint32_t prows, const float *part) {
+    using S = AttendShape<QK, VD, KVT, NQ>;
+    constexpr int LPR = S::LPR, RPW = S::RPW, EK = S::EK, EV = S::EV, WK = S::WK, WV = S::WV, ES = S::ES;
+    constexpr int U = 4;
+    constexpr bool SCALED = KvT<KVT>::dt == DT_I8;
+    __shared__ float sq[4][NQ][QK];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, sub = lane % LPR, rl = lane / LPR;
+    const uint32_t n_kv = P.c.n_kv, rep = P.rep;
+    const size_t item = (size_t)blockIdx.x * 4 + warp;
+    if (item >= (size_t)P.n_tok * n_kv) return;
+    const uint32_t tok = (uint32_t)(item / n_kv), g = (uint32_t)(item % n_kv);
+    TokMeta tm;
+    uint32_t pos;
+    if (!shared_token(P, tok, prows, tm, pos)) {
+        if (lane == 0) set_err(P.err, 2);
+        return;
+    }
+    const float2 *cs = P.rope + (size_t)pos * (QK / 2);
+    float *sqw = &sq[warp][0][0];
 #pragma unroll
-            for (int qi = 0; qi < NQ; qi++) {
-                if ((uint32_t)qi < rep) {
-                    RopePairs<QK> x;
-                    warp_load_pairs<QK>(x, P.q, P.act_dt, ((size_t)tm.row * P.n_heads + g * rep + qi) * QK, lane);
-                    warp_norm_rope<QK>(x, cs, P.qnorm, lane);
+    for (int qi = 0; qi < NQ; qi++) {
+        if ((uint32_t)qi < rep) {
+            RopePairs<QK> x;
+            warp_load_pairs<QK>(x, P.q, P.act_dt, ((size_t)tm.row * P.n_heads + g * rep + qi) * QK, lane);
+            warp_norm_rope<QK>(x, cs, P.qnorm, lane);
 #pragma unroll
-                    for (int c = 0; c < RopePairs<QK>::PPL; c++) {
-                        const int i = lane + 32 * c;
-                        if (i < QK / 2) {
-                            sqw[qi * QK + i] = x.a[c] * P.scale_log2;
-                            sqw[qi * QK + i + QK / 2] = x.b[c] * P.scale_log2;
-                        }
-                    }
-                } else {
-                    for (int i = lane; i < QK; i += 32) sqw[qi * QK + i] = 0.0f;
+            for (int c = 0; c < RopePairs<QK>::PPL; c++) {
+                const int i = lane + 32 * c;
+                if (i < QK / 2) {
+                    sqw[qi * QK + i] = x.a[c] * P.scale_log2;
+                    sqw[qi * QK + i + QK / 2] = x.b[c] * P.scale_log2;
                 }
             }
-            warp_append<QK, VD, KVT>(P.c, phys_row(P.c, tm.seq, pos), g, P.k, P.v, P.act_dt,
-                                     ((size_t)tm.row * n_kv + g) * QK, ((size_t)tm.row * n_kv + g) * VD, cs,
-                                     P.knorm, lane);
-            __syncwarp();
-            float qr[NQ][EK], m[NQ], l[NQ], acc[NQ][EV];
+        } else {
+            for (int i = lane; i < QK; i += 32) sqw[qi * QK + i] = 0.0f;
+        }
+    }
+    warp_append<QK, VD, KVT>(P.c, phys_row(P.c, tm.seq, pos), g, P.k, P.v, P.act_dt,
+                             ((size_t)tm.row * n_kv + g) * QK, ((size_t)tm.row * n_kv + g) * VD, cs, P.knorm, lane);
+    __syncwarp();
+    float qr[NQ][EK], m[NQ], l[NQ], acc[NQ][EV];
 #pragma unroll
-            for (int qi = 0; qi < NQ; qi++) {
-                const float *hp = hw + (size_t)((tl - c0) * NQ + qi) * (VD + 2);
-                m[qi] = hp[0];
-                l[qi] = rl == 0 ? hp[1] : 0.0f;
+    for (int qi = 0; qi < NQ; qi++) {
 #pragma unroll
-                for (int e = 0; e < EK; e++) qr[qi][e] = sqw[qi * QK + sub * EK + e];
+        for (int e = 0; e < EK; e++) qr[qi][e] = sqw[qi * QK + sub * EK + e];
+        if ((uint32_t)qi < rep) {
+            const float *hp = part + ((size_t)tok * P.n_heads + g * rep + qi) * (VD + 2);
+            m[qi] = hp[0];
+            l[qi] = rl == 0 ? hp[1] : 0.0f;
 #pragma unroll
-                for (int e = 0; e < EV; e++) acc[qi][e] = rl == 0 ? hp[2 + sub * EV + e] : 0.0f;
-            }
-            __syncwarp();   // sqw is rewritten for the next token
-            for (uint32_t base = prows; base <= pos; base += U * RPW) {
-                uint32_t kw[U][WK], vw[U][WV];
-                float ksc[U], vsc[U];
-                bool valid[U];
+            for (int e = 0; e < EV; e++) acc[qi][e] = rl == 0 ? hp[2 + sub * EV + e] : 0.0f;
+        } else {
+            m[qi] = -INFINITY;
+            l[qi] = 0.0f;
 #pragma unroll
-                for (int u = 0; u < U; u++) {
-                    const uint32_t j = base + u * RPW + rl;
-                    valid[u] = j <= pos;
-                    ksc[u] = vsc[u] = 0.0f;
-                    if (valid[u]) {
-                        const size_t row = phys_row(P.c, tm.seq, j);
-                        if (j < pos) {
-                            load_words<WK, true>(kbase + row * krow_bytes, kw[u]);
-                            load_words<WV, true>(vbase + row * vrow_bytes, vw[u]);
-                        } else {   // the newest row, written by this warp: the coherent path
-                            load_words<WK, false>(kbase + row * krow_bytes, kw[u]);
-                            load_words<WV, false>(vbase + row * vrow_bytes, vw[u]);
-                        }
-                        if constexpr (SCALED) {
-                            ksc[u] = P.c.ks[row * n_kv + g];
-                            vsc[u] = P.c.vs[row * n_kv + g];
-                        }
-                    } else {
+            for (int e = 0; e < EV; e++) acc[qi][e] = 0.0f;
+        }
+    }
+    const char *kbase = static_cast<const char *>(P.c.k) + ((size_t)g * QK + (size_t)sub * EK) * ES;
+    const char *vbase = static_cast<const char *>(P.c.v) + ((size_t)g * VD + (size_t)sub * EV) * ES;
+    const size_t krow_bytes = (size_t)P.c.k_dim * ES, vrow_bytes = (size_t)P.c.v_dim * ES;
+    for (uint32_t base = prows; base <= pos; base += U * RPW) {
+        uint32_t kw[U][WK], vw[U][WV];
+        float ksc[U], vsc[U];
+        bool valid[U];
 #pragma unroll
-                        for (int i = 0; i < WK; i++) kw[u][i] = 0u;
-#pragma unroll
-                        for (int i = 0; i < WV; i++) vw[u][i] = 0u;
-                    }
+        for (int u = 0; u < U; u++) {
+            const uint32_t j = base + u * RPW + rl;
+            valid[u] = j <= pos;
+            ksc[u] = vsc[u] = 0.0f;
+            if (valid[u]) {
+                const size_t row = phys_row(P.c, tm.seq, j);
+                if (j < pos) {
+                    load_words<WK, true>(kbase + row * krow_bytes, kw[u]);
+                    load_words<WV, true>(vbase + row * vrow_bytes, vw[u]);
+                } else {   // the newest row, written by this warp: the coherent path
+                    load_words<WK, false>(kbase + row * krow_bytes, kw[u]);
+                    load_words<WV, false>(vbase + row * vrow_bytes, vw[u]);
                 }
-                consume<QK, VD, KVT, NQ, U>(qr, kw, vw, ksc, vsc, valid, m, l, acc);
-            }
-#pragma unroll
-            for (int qi = 0; qi < NQ; qi++) {
-#pragma unroll
-                for (int o = LPR; o < 32; o <<= 1) {
-                    l[qi] += __shfl_xor_sync(0xffffffffu, l[qi], o);
-#pragma unroll
-                    for (int e = 0; e < EV; e++) acc[qi][e] += __shfl_xor_sync(0xffffffffu, acc[qi][e], o);
+                if constexpr (SCALED) {
+                    ksc[u] = P.c.ks[row * n_kv + g];
+                    vsc[u] = P.c.vs[row * n_kv + g];
                 }
-            }
-            if (rl == 0) {
+            } else {
 #pragma unroll
-                for (int qi = 0; qi < NQ; qi++) {
-                    if ((uint32_t)qi >= rep) continue;
-                    const uint32_t h = g * rep + qi;
-                    const size_t ob = ((size_t)tm.row * P.n_heads + h) * VD;
-                    const float inv = 1.0f / l[qi];
+                for (int i = 0; i < WK; i++) kw[u][i] = 0u;
 #pragma unroll
-                    for (int e = 0; e < EV; e++) {
-                        const uint32_t d = sub * EV + e;
-                        float val = acc[qi][e] * inv;
-                        if (P.gate)
-                            val *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, ob + d) * 1.4426950408889634f));
-                        out_store<VD>(P, tm.row, h * VD + d, val);
-                    }
-                }
+                for (int i = 0; i < WV; i++) vw[u][i] = 0u;
             }
         }
-        __syncwarp();   // the hand-off slots are rewritten by the next chunk
+        consume<QK, VD, KVT, NQ, U>(qr, kw, vw, ksc, vsc, valid, m, l, acc);
+    }
+#pragma unroll
+    for (int qi = 0; qi < NQ; qi++) {
+#pragma unroll
+        for (int o = LPR; o < 32; o <<= 1) {
+            l[qi] += __shfl_xor_sync(0xffffffffu, l[qi], o);
+#pragma unroll
+            for (int e = 0; e < EV; e++) acc[qi][e] += __shfl_xor_sync(0xffffffffu, acc[qi][e], o);
+        }
+    }
+    if (rl != 0) return;
+#pragma unroll
+    for (int qi = 0; qi < NQ; qi++) {
+        if ((uint32_t)qi >= rep) continue;
+        const uint32_t h = g * rep + qi;
+        const size_t ob = ((size_t)tm.row * P.n_heads + h) * VD;
+        const float inv = 1.0f / l[qi];
+#pragma unroll
+        for (int e = 0; e < EV; e++) {
+            const uint32_t d = sub * EV + e;
+            float val = acc[qi][e] * inv;
+            if (P.gate) val *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, ob + d) * 1.4426950408889634f));
+            out_store<VD>(P, tm.row, h * VD + d, val);
+        }
     }
 }
 
