@@ -387,20 +387,31 @@ __global__ void __launch_bounds__(128, 2)
     const uint32_t g = blockIdx.x, n_kv = P.c.n_kv, rep = P.rep;
 
     // Rows [0, prows) of KV head g of the prefix sequence as f32 (int8 rows
-    // times their scales).
-    for (uint32_t i = tid; i < prows * QK; i += blockDim.x) {
-        const uint32_t r = i / QK, d = i - r * QK;
-        const size_t row = phys_row(P.c, pseq, r);
-        float x = (float)static_cast<const KVT *>(P.c.k)[row * P.c.k_dim + (size_t)g * QK + d];
-        if constexpr (SCALED) x *= P.c.ks[row * n_kv + g];
-        sK[i] = x;
-    }
-    for (uint32_t i = tid; i < prows * VD; i += blockDim.x) {
-        const uint32_t r = i / VD, d = i - r * VD;
-        const size_t row = phys_row(P.c, pseq, r);
-        float x = (float)static_cast<const KVT *>(P.c.v)[row * P.c.v_dim + (size_t)g * VD + d];
-        if constexpr (SCALED) x *= P.c.vs[row * n_kv + g];
-        sV[i] = x;
+    // times their scales), 16-byte chunks of the cache rows.
+    {
+        constexpr int ES = (int)sizeof(KVT), EPC = 16 / ES;   // elements per chunk
+        constexpr uint32_t KC = QK * ES / 16, VC = VD * ES / 16;
+        static_assert((QK * ES) % 16 == 0 && (VD * ES) % 16 == 0 && EPC % 4 == 0, "16-byte row chunks");
+        const char *kc = static_cast<const char *>(P.c.k), *vc = static_cast<const char *>(P.c.v);
+#pragma unroll 4
+        for (uint32_t i = tid; i < prows * (KC + VC); i += blockDim.x) {
+            const bool isk = i < prows * KC;
+            const uint32_t ii = isk ? i : i - prows * KC, CPR = isk ? KC : VC;
+            const uint32_t r = ii / CPR, c = ii - r * CPR;
+            const size_t row = phys_row(P.c, pseq, r);
+            const char *src = isk ? kc + (row * P.c.k_dim + (size_t)g * QK) * ES + c * 16
+                                  : vc + (row * P.c.v_dim + (size_t)g * VD) * ES + c * 16;
+            uint32_t w[4];
+            load_words<4, true>(src, w);
+            float f[EPC];
+            unpack<KVT, 4>(w, f);
+            float sc = 1.0f;
+            if constexpr (SCALED) sc = isk ? P.c.ks[row * n_kv + g] : P.c.vs[row * n_kv + g];
+            float4 *dst = reinterpret_cast<float4 *>((isk ? sK + (size_t)r * QK : sV + (size_t)r * VD) + c * EPC);
+#pragma unroll
+            for (int e = 0; e < EPC / 4; e++)
+                dst[e] = make_float4(f[4 * e] * sc, f[4 * e + 1] * sc, f[4 * e + 2] * sc, f[4 * e + 3] * sc);
+        }
     }
     __syncthreads();
 
