@@ -450,22 +450,28 @@ __global__ void __launch_bounds__(128, 2)
 #pragma unroll
         for (int i = 0; i < VD; i++) o[i] = 0.0f;
         for (uint32_t k0 = 0; k0 < prows; k0 += 8) {
+            // Eight independent dot products, advanced together one 4-wide
+            // chunk of the head dim at a time (eight FMA chains in flight).
             float s[8];
+            const float4 *kr[8];
 #pragma unroll
             for (int kk = 0; kk < 8; kk++) {
-                const uint32_t key = k0 + kk < prows ? k0 + kk : prows - 1;
-                const float4 *kr = reinterpret_cast<const float4 *>(sK + (size_t)key * QK);
-                float a = 0.0f;
-#pragma unroll
-                for (int i = 0; i < QK / 4; i++) {
-                    const float4 kv = kr[i];
-                    a = fmaf(q[4 * i], kv.x, a);
-                    a = fmaf(q[4 * i + 1], kv.y, a);
-                    a = fmaf(q[4 * i + 2], kv.z, a);
-                    a = fmaf(q[4 * i + 3], kv.w, a);
-                }
-                s[kk] = k0 + kk < prows ? a : -INFINITY;
+                s[kk] = 0.0f;
+                kr[kk] = reinterpret_cast<const float4 *>(sK + (size_t)(k0 + kk < prows ? k0 + kk : prows - 1) * QK);
             }
+#pragma unroll
+            for (int i = 0; i < QK / 4; i++) {
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++) {
+                    const float4 kv = kr[kk][i];
+                    s[kk] = fmaf(q[4 * i], kv.x, s[kk]);
+                    s[kk] = fmaf(q[4 * i + 1], kv.y, s[kk]);
+                    s[kk] = fmaf(q[4 * i + 2], kv.z, s[kk]);
+                    s[kk] = fmaf(q[4 * i + 3], kv.w, s[kk]);
+                }
+            }
+#pragma unroll
+            for (int kk = 0; kk < 8; kk++) s[kk] = k0 + kk < prows ? s[kk] : -INFINITY;
             float mx = s[0];
 #pragma unroll
             for (int kk = 1; kk < 8; kk++) mx = fmaxf(mx, s[kk]);
