@@ -502,6 +502,17 @@ __global__ void __launch_bounds__(192, 2)
                         vb[e] *= 1.0f / (1.0f + ex2(-act_load(P.gate, P.act_dt, obase + 32 + e) * 1.4426950408889634f));
                     }
                 }
+                // The block still holds item k+1's RoPE rows, which every
+                // softmax warp reads in its set-up of item k+1; this row's
+                // output lands on another warp's rows (row r's 128 bytes are
+                // RoPE row r/2's, the f32 second box rows 64 + r/2). Write only
+                // once all four warps have finished that set-up (q_ready's
+                // phase for item k+1 completes with their four arrivals).
+                if (k + 1 < n_items &&
+                    !__all_sync(0xffffffffu, mbar_wait(&B.q_ready, (k + 1) & 1, abort_flag))) {
+                    ok = false;
+                    break;
+                }
                 if (P.out_dt == DT_F32) {
 #pragma unroll
                     for (int e = 0; e < 8; e++) {
