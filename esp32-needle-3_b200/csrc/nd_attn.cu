@@ -253,7 +253,7 @@ struct nd_attn {
     cudaStream_t stream = nullptr;   // where work is enqueued
     cudaStream_t own = nullptr;      // the handle's own stream
     int sm_count = 148;
-    int shared_variant = 2;          // highest nd_attn_decode_shared variant to use (ND_ATTN_SHARED_VARIANT)
+    int shared_variant = 0;          // nd_attn_decode_shared kernel: 0 by call size, 1 or 2 forced (ND_ATTN_SHARED_VARIANT)
     uint32_t rep = 1, k_dim = 0, v_dim = 0, blocks_per_seq = 1, block_shift = 0;
     size_t rows_per_layer = 0, kes = 1;
     void *kc = nullptr, *vc = nullptr;
@@ -1059,9 +1059,13 @@ int nd_attn_open(const nd_attn_config *cfg_in, nd_attn **out) {
     nd_attn *h = new nd_attn();
     h->cfg = cfg;
     h->sm_count = prop.multiProcessorCount;
-    // ND_ATTN_SHARED_VARIANT=1 keeps nd_attn_decode_shared on its lane-map
-    // kernel (variant 1) where variant 2 would run (tests cover both).
-    if (const char *sv = getenv("ND_ATTN_SHARED_VARIANT")) h->shared_variant = atoi(sv) == 1 ? 1 : 2;
+    // ND_ATTN_SHARED_VARIANT=1 or 2 makes nd_attn_decode_shared use that
+    // kernel whatever the call's size (variant 2 where it is built), so tests
+    // cover both on small calls.
+    if (const char *sv = getenv("ND_ATTN_SHARED_VARIANT")) {
+        const int x = atoi(sv);
+        h->shared_variant = x == 1 || x == 2 ? x : 0;
+    }
     h->rep = cfg.n_heads / cfg.n_kv_heads;
     h->k_dim = cfg.n_kv_heads * cfg.qk_head_dim;
     h->v_dim = cfg.n_kv_heads * cfg.v_head_dim;
@@ -1427,10 +1431,17 @@ int nd_attn_decode_shared(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t
     ND_CUDA(cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, c.device));
     // Variant 2 (one lane per query row over the prefix) where it is built
     // (head dims up to 64) and its f32 staging fits; else variant 1; else the
-    // regular path, which gives the same results.
+    // regular path, which gives the same results. By default a call of fewer
+    // than kSharedMinItems (token, KV head) pairs takes the regular path: a
+    // warp of the staging kernel serves 32 query rows over the whole prefix,
+    // so a small call leaves most SMs idle (config 5 at 1024 requests: 0.72
+    // against 0.74 ms per step; at 4096: 1.49 against 2.50).
+    constexpr uint64_t kSharedMinItems = 8192;
+    if (h->shared_variant == 0 && (uint64_t)n * c.n_kv_heads < kSharedMinItems)
+        return nd_attn_decode(h, layer, n, seq_ids, q, k, v, gate, out);
     int variant = 0;
     size_t smem = 0;
-    if (h->shared_variant >= 2 && launch(AttnParams{}, 0, dim3(1), 2, nullptr, &smem) == cudaSuccess &&
+    if (h->shared_variant != 1 && launch(AttnParams{}, 0, dim3(1), 2, nullptr, &smem) == cudaSuccess &&
         smem <= (size_t)smem_max && (reinterpret_cast<uintptr_t>(q) & 15u) == 0)
         variant = 2;
     else if (launch(AttnParams{}, 0, dim3(1), 1, nullptr, &smem) == cudaSuccess && smem <= (size_t)smem_max)

@@ -30,6 +30,13 @@ from harness import TOL, cache_bits, dev, oracle_cache, rel_err
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def _force_kernel(monkeypatch):
+    """The library takes its regular decode for calls this small; the tests
+    force the shared-prefix kernels (variant 2 where built, else variant 1)."""
+    monkeypatch.setenv("ND_ATTN_SHARED_VARIANT", "2")
+
+
 def _run_oracle(seqs, layer, rows, gate):
     """One oracle step per listed sequence (C calls release the GIL)."""
     def run(i):
