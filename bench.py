@@ -1121,6 +1121,11 @@ def run_ours(args):
         if rank == 0:
             print(json.dumps(dict(pre, n_gpus=world, higher_is_better=True, scaling="weak", vs_baseline=None,
                                   data="synthetic")), flush=True)
+    elif args.workload == "serve":
+        srv = run_serve(args, world, rank, local, dist)
+        if rank == 0:
+            print(json.dumps(dict(srv, n_gpus=world, higher_is_better=True, vs_baseline=None, data="synthetic")),
+                  flush=True)
     else:
         dec = run_decode(args, world, rank, local, dist)
         taps = run_decode_taps(args, world, rank, local, dist, dec["value"])
@@ -1168,17 +1173,21 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
-                    help="decode: config 2 line with the config 3 prefill inside; prefill: config 3 alone")
+    ap.add_argument("--workload", choices=["decode", "prefill", "serve"], default="decode",
+                    help="decode: config 2 line with the other legs inside; prefill: config 3 alone; "
+                         "serve: config 5 alone")
     ap.add_argument("--prefill-steps", type=int, default=5, help="timed config-3 steps (0 skips the prefill leg)")
     ap.add_argument("--long-steps", type=int, default=L_STEPS,
                     help="timed config-4 decode steps (0 skips the long-context leg)")
     ap.add_argument("--serve", type=int, default=1, help="1 runs the config-5 shared-prefix serving leg, 0 skips it")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling only: fewer layers than the config")
     ap.add_argument("--seqs", type=int, default=0, help="profiling only: fewer config-3 sequences")
+    ap.add_argument("--serve-requests", type=int, default=0, help="profiling only: fewer config-5 requests")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     globals()["LAYERS"] = args.layers
+    if args.serve_requests:
+        globals()["S_REQ"] = args.serve_requests
     if args.impl == "reference":
         run_reference(args)
     else:
