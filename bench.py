@@ -50,8 +50,8 @@ P_METRIC = "prefill tok/s (config 3: 512 seq x 1024 tok x 8 layers, GQA 16/4, hd
 # the decode launch on the one-layer case (per-launch work equals a launch
 # here), the prefill launch on 64 sequences scaled by 8 to 512 (traffic grows
 # with the sequences processed).
-DECODE_TRAFFIC = (153.7e6 + 1.8e6)
-PREFILL_TRAFFIC = (309.5e6 + 100.4e6) * 8
+DECODE_TRAFFIC = (151.4e6 + 4.8e6)
+PREFILL_TRAFFIC = (315.7e6 + 101.4e6) * 8
 # config 4 (long-context paged decode)
 L_SEQS, L_CTX, L_H, L_HD, L_BLOCK, L_STEPS = 256, 32768, 8, 128, 64, 64
 L_METRIC = ("decode tok/s (config 4: B=256/GPU x 32768 cached, 8x128 MHA, fp16 KV, 64-slot pages in a "
