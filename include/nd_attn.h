@@ -183,8 +183,11 @@ ND_ATTN_API int  nd_attn_decode(nd_attn *h, uint32_t layer, uint32_t n, const ui
  * listed sequence at pos >= prefix_rows, prefix_seq at pos >= prefix_rows
  * (rows written); else ND_ATTN_ERR_RANGE and nothing is launched. A prefix too
  * large to stage in shared memory, and a call of fewer than 8192 (sequence, KV
- * head) pairs (too few to fill the GPU that way), run as nd_attn_decode.
- * DEVICE pointers. Does not advance. */
+ * head) pairs (too few to fill the GPU that way), run as nd_attn_decode; with
+ * ND_ATTN_SHARED_VARIANT=2 (or 1) in the environment when the handle is
+ * opened, every call that fits uses the shared-prefix kernels (2: the
+ * one-lane-per-query-row kernel where built, head dims up to 64; 1: the lane-
+ * map kernel). DEVICE pointers. Does not advance. */
 ND_ATTN_API int  nd_attn_decode_shared(nd_attn *h, uint32_t layer, uint32_t n, const uint32_t *seq_ids,
                                        uint32_t prefix_seq, uint32_t prefix_rows, const void *q,
                                        const void *k, const void *v, const void *gate, void *out);
